@@ -1,0 +1,139 @@
+"""Model and chunk-schedule configuration for the Matrix-Game-2-shaped causal Wan DiT.
+
+The reference runtime reads every dimension off the official model object
+(``fastworld/models/mg2/static.py:27-72``) and hard-codes the chunk geometry
+(``FPB=3``, ``TOK=880``, ``TH, TW = 22, 40``; ``fastworld/models/mg2/model.py:18-19``,
+``static.py:17``).  The official Matrix-Game-2 package that owns the module widths is not
+vendored by the reference, so the synthetic model is pinned here explicitly.  Module
+semantics follow the public Wan2.1 architecture:
+
+* LayerNorm eps 1e-6; ``norm1``/``norm2`` without affine, ``norm3`` with affine.
+* q/k RMSNorm (eps 1e-6, with weight) over the full hidden width, not per head.
+* 3D RoPE over (t, h, w) with 44/42/42 real dims of head_dim 128, theta 10000, applied to
+  interleaved (even, odd) pairs.
+* FFN ``Linear -> GELU(tanh) -> Linear``; ``img_emb`` = ``LN -> Linear -> GELU(erf) -> Linear -> LN``.
+* Head: ``LN -> (1 + scale) * x + shift -> Linear(dim, 16 * 1 * 2 * 2)``.
+* Flow-matching scheduler with sigma(t) = t / 1000 (x0 = x_t - sigma * v;
+  x' = (1 - sigma') * x0 + sigma' * eps).
+
+The action module (keyboard + mouse conditioning, on ``action_blocks``) keeps the buffer
+shapes of the reference (``static.py:49-54,63-64``): 16 heads x 64, a 3-frame mouse/keyboard
+history per block, pixel/latent time ratio 4 and window 3.
+"""
+from __future__ import annotations
+
+import dataclasses
+from dataclasses import dataclass, field
+from typing import Tuple
+
+
+@dataclass(frozen=True)
+class DiTConfig:
+    name: str = "mg2"
+    dim: int = 1536
+    heads: int = 12
+    head_dim: int = 128
+    ffn: int = 8960
+    layers: int = 30
+    freq_dim: int = 256
+    # latent / patch geometry (static.py:58-61; model.py:18)
+    lat_ch: int = 16
+    cond_ch: int = 20
+    frames: int = 3             # latent frames per chunk (FPB)
+    lat_h: int = 44
+    lat_w: int = 80
+    patch: Tuple[int, int, int] = (1, 2, 2)
+    # image context (static.py:62): CLIP tokens
+    ctx_tokens: int = 257
+    ctx_dim: int = 1280
+    # action module (static.py:49-57,145-185)
+    action_blocks: Tuple[int, ...] = tuple(range(15))
+    act_heads: int = 16
+    act_head_dim: int = 64
+    mouse_hidden: int = 1024
+    keyboard_hidden: int = 256
+    mouse_dim: int = 2
+    keyboard_dim: int = 4
+    time_ratio: int = 4         # vae_time_compression_ratio
+    window: int = 3             # windows_size
+    # schedule; the context forward runs at t = 0
+    steps: Tuple[float, ...] = (1000.0, 750.0, 500.0, 250.0)
+    eps: float = 1e-6
+    rope_theta: float = 10000.0
+    max_frames: int = 1024      # RoPE table rows (Wan rope_params max_seq_len)
+
+    # ---- derived
+    @property
+    def th(self) -> int:
+        return self.lat_h // self.patch[1]
+
+    @property
+    def tw(self) -> int:
+        return self.lat_w // self.patch[2]
+
+    @property
+    def tok_per_frame(self) -> int:
+        return self.th * self.tw
+
+    @property
+    def tokens(self) -> int:
+        return self.frames * self.tok_per_frame
+
+    @property
+    def patch_k(self) -> int:
+        return (self.lat_ch + self.cond_ch) * self.patch[0] * self.patch[1] * self.patch[2]
+
+    @property
+    def out_dim(self) -> int:
+        return self.lat_ch * self.patch[0] * self.patch[1] * self.patch[2]
+
+    @property
+    def act_dim(self) -> int:
+        return self.act_heads * self.act_head_dim
+
+    @property
+    def pad_t(self) -> int:
+        return self.time_ratio * self.window
+
+    @property
+    def kc_len(self) -> int:
+        """Keyboard window length in pixel frames (static.py:64)."""
+        return self.frames * self.time_ratio + self.pad_t - 3
+
+    @property
+    def rope_split(self) -> Tuple[int, int, int]:
+        """Complex RoPE frequencies for (t, h, w) (static.py:114)."""
+        c = self.head_dim // 2
+        return (c - 2 * (c // 3), c // 3, c // 3)
+
+    @property
+    def n_fwd(self) -> int:
+        return len(self.steps) + 1
+
+    def replace(self, **kw) -> "DiTConfig":
+        return dataclasses.replace(self, **kw)
+
+    def validate(self) -> None:
+        assert self.dim == self.heads * self.head_dim
+        assert self.head_dim % 2 == 0 and self.act_head_dim % 2 == 0
+        assert self.dim % 8 == 0 and self.ffn % 8 == 0, "row strides must be 16-byte aligned"
+        assert all(0 <= b < self.layers for b in self.action_blocks)
+        assert self.lat_h % self.patch[1] == 0 and self.lat_w % self.patch[2] == 0
+        assert self.patch[0] == 1
+
+
+# one Wan-1.3B block (parity case, no action module).
+BLOCK = DiTConfig(name="block", layers=1, action_blocks=())
+# the Matrix-Game-2-shaped DiT, 30 blocks + action modules.
+MG2 = DiTConfig()
+# Wan-14B shape (40 x 128 heads, 5120 wide, 1560 tokens per frame).
+WAN14B = DiTConfig(name="wan14b", dim=5120, heads=40, head_dim=128, ffn=13824, layers=40,
+                   lat_h=60, lat_w=104, action_blocks=())
+# Small shapes for CPU tests: same code paths, tiny widths, the reference's chunk geometry.
+TINY = DiTConfig(name="tiny", dim=128, heads=2, head_dim=64, ffn=256, layers=2, ctx_dim=64,
+                 action_blocks=(0,), act_heads=2, mouse_hidden=128, keyboard_hidden=32)
+# TINY with GPU-friendly widths (multiples of the GEMM tile) for fast GPU parity tests.
+SMALL = DiTConfig(name="small", dim=256, heads=2, head_dim=128, ffn=512, layers=2, ctx_dim=256,
+                  action_blocks=(1,), act_heads=4, mouse_hidden=256, keyboard_hidden=64)
+
+PRESETS = {c.name: c for c in (BLOCK, MG2, WAN14B, TINY, SMALL)}
