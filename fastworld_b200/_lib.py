@@ -1,0 +1,117 @@
+"""ctypes binding of ``libfastworld_b200.so`` (declared in ``include/fastworld_b200.h``).
+
+The library is built in-tree by ``python -m fastworld_b200.build``; importing the binding
+never falls back to anything else: a missing library raises immediately.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libfastworld_b200.so")
+
+FW_MAX_ACTION_BLOCKS = 64
+FW_MAX_STEPS = 16
+KIND_WEIGHT, KIND_STATE, KIND_INPUT, KIND_OUTPUT, KIND_WORKSPACE, KIND_STATUS = range(6)
+DT_BF16, DT_F32, DT_I32, DT_U8 = range(4)
+EPI_BF16, EPI_GELU_BF16, EPI_RESID_F32, EPI_F32, EPI_GELU_ERF_BF16 = range(5)
+
+
+class FwConfig(ctypes.Structure):
+    _fields_ = [
+        ("dim", ctypes.c_int), ("heads", ctypes.c_int), ("head_dim", ctypes.c_int), ("ffn", ctypes.c_int),
+        ("layers", ctypes.c_int), ("freq_dim", ctypes.c_int),
+        ("lat_ch", ctypes.c_int), ("cond_ch", ctypes.c_int), ("frames", ctypes.c_int), ("lat_h", ctypes.c_int),
+        ("lat_w", ctypes.c_int),
+        ("ctx_tokens", ctypes.c_int), ("ctx_dim", ctypes.c_int),
+        ("n_action", ctypes.c_int), ("action_blocks", ctypes.c_int * FW_MAX_ACTION_BLOCKS),
+        ("act_heads", ctypes.c_int), ("act_head_dim", ctypes.c_int), ("mouse_hidden", ctypes.c_int),
+        ("keyboard_hidden", ctypes.c_int), ("mouse_dim", ctypes.c_int), ("keyboard_dim", ctypes.c_int),
+        ("time_ratio", ctypes.c_int), ("window", ctypes.c_int),
+        ("n_steps", ctypes.c_int), ("steps", ctypes.c_float * FW_MAX_STEPS),
+        ("eps", ctypes.c_float), ("eps_ln", ctypes.c_float), ("rope_theta", ctypes.c_float),
+    ]
+
+
+class FwTensorInfo(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char_p), ("kind", ctypes.c_int), ("dtype", ctypes.c_int), ("ndim", ctypes.c_int),
+                ("shape", ctypes.c_int64 * 5), ("bytes", ctypes.c_size_t)]
+
+
+_SIGS = {
+    "fw_abi_version": (ctypes.c_int, []),
+    "fw_strerror": (ctypes.c_char_p, [ctypes.c_int]),
+    "fw_create": (ctypes.c_int, [ctypes.POINTER(FwConfig), ctypes.POINTER(ctypes.c_void_p)]),
+    "fw_tensor_count": (ctypes.c_int, [ctypes.c_void_p]),
+    "fw_tensor_info_at": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(FwTensorInfo)]),
+    "fw_bind": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_char_p, ctypes.c_void_p, ctypes.c_size_t]),
+    "fw_finalize": (ctypes.c_int, [ctypes.c_void_p]),
+    "fw_chunk": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]),
+    "fw_prefill": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]),
+    "fw_forward": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]),
+    "fw_destroy": (None, [ctypes.c_void_p]),
+    "fw_copy": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+    "fw_gemm_bf16": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
+                                    ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]),
+    "fw_gemm_bf16_resid": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                          ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                          ctypes.c_void_p]),
+    "fw_attention": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
+                                    ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p,
+                                    ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),
+}
+
+_LIB = None
+
+
+def lib() -> ctypes.CDLL:
+    """Load the engine library (raises if it has not been built)."""
+    global _LIB
+    if _LIB is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"{LIB_PATH} is missing: build it with `python -m fastworld_b200.build`")
+        L = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in _SIGS.items():
+            f = getattr(L, name)
+            f.restype, f.argtypes = res, args
+        _LIB = L
+    return _LIB
+
+
+def strerror(rc: int) -> str:
+    return lib().fw_strerror(rc).decode()
+
+
+def check(rc: int, what: str = "call") -> None:
+    if rc != 0:
+        raise RuntimeError(f"fastworld_b200 {what} failed: {strerror(rc)} (code {rc})")
+
+
+def make_config(cfg) -> FwConfig:
+    """fw_config from a :class:`fastworld_b200.config.DiTConfig`."""
+    c = FwConfig()
+    for f in ("dim", "heads", "head_dim", "ffn", "layers", "freq_dim", "lat_ch", "cond_ch", "frames", "lat_h",
+              "lat_w", "ctx_tokens", "ctx_dim", "act_heads", "act_head_dim", "mouse_hidden", "keyboard_hidden",
+              "mouse_dim", "keyboard_dim", "time_ratio", "window"):
+        setattr(c, f, int(getattr(cfg, f)))
+    if len(cfg.action_blocks) > FW_MAX_ACTION_BLOCKS or len(cfg.steps) > FW_MAX_STEPS:
+        raise ValueError("too many action blocks or steps")
+    c.n_action = len(cfg.action_blocks)
+    for i, b in enumerate(cfg.action_blocks):
+        c.action_blocks[i] = int(b)
+    c.n_steps = len(cfg.steps)
+    for i, t in enumerate(cfg.steps):
+        c.steps[i] = float(t)
+    c.eps, c.eps_ln, c.rope_theta = float(cfg.eps), 1e-5, float(cfg.rope_theta)
+    return c
+
+
+def ptr(t) -> int:
+    return t.data_ptr() if t is not None else 0
+
+
+def stream_ptr(stream=None):
+    import torch
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return ctypes.c_void_p(s.cuda_stream)

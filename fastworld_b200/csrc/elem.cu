@@ -1,0 +1,536 @@
+// Fused memory-bound kernels of the chunk forward (sm_100a).  All are HBM/L2-bound row
+// kernels: one warp per row (or per (token, head)), 16-byte vector access, fp32 math.
+//
+// Reference ops replaced (fastworld/models/mg2/static.py):
+//   ln_kernel            norm1/norm2 + adaLN modulate (206, 224), norm3 (221), img_emb LNs (201),
+//                        mouse_mlp LayerNorm (150)
+//   rms_rope_kernel      norm_q / norm_k (208-209, 189-190) fused with the fp64 complex RoPE
+//                        (_rope, 130-133; computed here in fp32 from an fp64-built table)
+//   rope_table_kernel    the per-chunk RoPE table fi (113-118) and action RoPE acos/asin (120)
+//   smallm_linear_kernel time_embedding / time_projection (199-200), keyboard_embed and
+//                        keyboard_attn_kv (165-168), the mouse-window part of mouse_mlp (150)
+//   patchify_kernel      cat([x, cc]) + Conv3d(k = s = (1,2,2)) operand layout (197-198)
+//   scheduler_kernel     unpatchify + _convert_flow_pred_to_x0 + add_noise (227-240)
+//   mouse_attn_kernel    mouse branch of _action: RMSNorm + rotate-half RoPE + attention over
+//                        [mk | current] frames + history write (151-161)
+//   kb_kv_kernel         keyboard K/V norm + RoPE (171-175)
+//   kb_attn_kernel       keyboard attention over [kk | current] (173-184)
+#include <math.h>
+
+#include "../../include/fastworld_b200.h"
+#include "fw_elem.h"
+#include "fw_ptx.cuh"
+
+namespace fw {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__device__ __forceinline__ void load4(const float* p, float (&v)[4]) {
+  float4 u = *reinterpret_cast<const float4*>(p);
+  v[0] = u.x; v[1] = u.y; v[2] = u.z; v[3] = u.w;
+}
+__device__ __forceinline__ void load4(const __nv_bfloat16* p, float (&v)[4]) {
+  uint2 u = *reinterpret_cast<const uint2*>(p);
+  float2 a = unpack_bf16(u.x), b = unpack_bf16(u.y);
+  v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+}
+__device__ __forceinline__ void store4(__nv_bfloat16* p, const float (&v)[4]) {
+  *reinterpret_cast<uint2*>(p) = make_uint2(pack_bf16(v[0], v[1]), pack_bf16(v[2], v[3]));
+}
+
+// ------------------------------------------------------------------ LayerNorm
+// out = LN(x) [* w + b] [* (1 + scale) + shift], one warp per row, D = 128 * NG.
+template <typename Tin, int NG>
+__global__ void __launch_bounds__(256) ln_kernel(const Tin* __restrict__ x, int ldx, int M, float eps,
+                                                 const float* __restrict__ shift, const float* __restrict__ scale,
+                                                 const __nv_bfloat16* __restrict__ w,
+                                                 const __nv_bfloat16* __restrict__ b, __nv_bfloat16* __restrict__ out,
+                                                 int ldo) {
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (row >= M) return;
+  constexpr int D = 128 * NG;
+  float v[NG][4];
+  float s = 0.f;
+#pragma unroll
+  for (int g = 0; g < NG; ++g) {
+    load4(x + (size_t)row * ldx + g * 128 + lane * 4, v[g]);
+    s += v[g][0] + v[g][1] + v[g][2] + v[g][3];
+  }
+  const float mean = warp_sum(s) * (1.f / D);
+  float q = 0.f;
+#pragma unroll
+  for (int g = 0; g < NG; ++g)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float d = v[g][i] - mean;
+      q += d * d;
+    }
+  const float rstd = rsqrtf(warp_sum(q) * (1.f / D) + eps);
+#pragma unroll
+  for (int g = 0; g < NG; ++g) {
+    const int c = g * 128 + lane * 4;
+    float y[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) y[i] = (v[g][i] - mean) * rstd;
+    if (w) {
+      float wv[4], bv[4];
+      load4(w + c, wv);
+      load4(b + c, bv);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) y[i] = y[i] * wv[i] + bv[i];
+    }
+    if (scale) {
+      float sc[4], sh[4];
+      load4(scale + c, sc);
+      load4(shift + c, sh);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) y[i] = y[i] * (1.f + sc[i]) + sh[i];
+    }
+    store4(out + (size_t)row * ldo + c, y);
+  }
+}
+
+template <typename Tin>
+static int ln_dispatch(const Tin* x, int ldx, int M, int D, float eps, const float* shift, const float* scale,
+                       const __nv_bfloat16* w, const __nv_bfloat16* b, __nv_bfloat16* out, int ldo, cudaStream_t s) {
+  if (D % 128 || ldx % 4 || ldo % 4) return FW_ESHAPE;
+  const dim3 grid((M + 7) / 8), block(256);
+  switch (D / 128) {
+#define FW_LN_CASE(n) \
+  case n: ln_kernel<Tin, n><<<grid, block, 0, s>>>(x, ldx, M, eps, shift, scale, w, b, out, ldo); break;
+    FW_LN_CASE(1) FW_LN_CASE(2) FW_LN_CASE(3) FW_LN_CASE(4) FW_LN_CASE(5) FW_LN_CASE(6) FW_LN_CASE(7)
+    FW_LN_CASE(8) FW_LN_CASE(9) FW_LN_CASE(10) FW_LN_CASE(11) FW_LN_CASE(12) FW_LN_CASE(16)
+#undef FW_LN_CASE
+    default: return FW_ESHAPE;
+  }
+  return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
+}
+
+int ln_f32(const float* x, int ldx, int M, int D, float eps, const float* shift, const float* scale,
+           const __nv_bfloat16* w, const __nv_bfloat16* b, __nv_bfloat16* out, int ldo, cudaStream_t s) {
+  return ln_dispatch<float>(x, ldx, M, D, eps, shift, scale, w, b, out, ldo, s);
+}
+int ln_bf16(const __nv_bfloat16* x, int ldx, int M, int D, float eps, const float* shift, const float* scale,
+            const __nv_bfloat16* w, const __nv_bfloat16* b, __nv_bfloat16* out, int ldo, cudaStream_t s) {
+  return ln_dispatch<__nv_bfloat16>(x, ldx, M, D, eps, shift, scale, w, b, out, ldo, s);
+}
+
+// ------------------------------------------------------------------ RMSNorm (+ RoPE)
+// out = RMSNorm(x) * w over D = 128 * NG, then (optionally) each (even, odd) pair of every
+// head is rotated by rope[row, pair % (hd / 2)] = (cos, sin).
+template <int NG>
+__global__ void __launch_bounds__(256) rms_rope_kernel(const __nv_bfloat16* __restrict__ x, int ldx, int M,
+                                                       float eps, const __nv_bfloat16* __restrict__ w,
+                                                       const float2* __restrict__ rope, int hd,
+                                                       __nv_bfloat16* __restrict__ out, int ldo) {
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (row >= M) return;
+  constexpr int D = 128 * NG;
+  float v[NG][4];
+  float q = 0.f;
+#pragma unroll
+  for (int g = 0; g < NG; ++g) {
+    load4(x + (size_t)row * ldx + g * 128 + lane * 4, v[g]);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) q += v[g][i] * v[g][i];
+  }
+  const float r = rsqrtf(warp_sum(q) * (1.f / D) + eps);
+  const int half = hd >> 1;
+#pragma unroll
+  for (int g = 0; g < NG; ++g) {
+    const int c = g * 128 + lane * 4;
+    float wv[4], y[4];
+    load4(w + c, wv);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) y[i] = v[g][i] * r * wv[i];
+    if (rope) {
+#pragma unroll
+      for (int p = 0; p < 2; ++p) {
+        const int pair = ((c % hd) >> 1) + p;
+        const float2 cs = __ldg(rope + (size_t)row * half + pair);
+        const float a = y[2 * p], bb = y[2 * p + 1];
+        y[2 * p] = a * cs.x - bb * cs.y;
+        y[2 * p + 1] = a * cs.y + bb * cs.x;
+      }
+    }
+    store4(out + (size_t)row * ldo + c, y);
+  }
+}
+
+int rms_rope(const __nv_bfloat16* x, int ldx, int M, int D, float eps, const __nv_bfloat16* w, const float2* rope,
+             int hd, __nv_bfloat16* out, int ldo, cudaStream_t s) {
+  if (D % 128 || ldx % 4 || ldo % 4 || (rope && (hd % 4 || D % hd))) return FW_ESHAPE;
+  const dim3 grid((M + 7) / 8), block(256);
+  switch (D / 128) {
+#define FW_RMS_CASE(n) \
+  case n: rms_rope_kernel<n><<<grid, block, 0, s>>>(x, ldx, M, eps, w, rope, hd, out, ldo); break;
+    FW_RMS_CASE(1) FW_RMS_CASE(2) FW_RMS_CASE(3) FW_RMS_CASE(4) FW_RMS_CASE(6) FW_RMS_CASE(8)
+    FW_RMS_CASE(10) FW_RMS_CASE(12) FW_RMS_CASE(16)
+#undef FW_RMS_CASE
+    default: return FW_ESHAPE;
+  }
+  return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
+}
+
+// ------------------------------------------------------------------ RoPE tables
+// table[token, i] = (cos, sin)(pos * theta^(-2 j / dim_part)) with (pos, j, dim_part) the
+// t / h / w position, the index within its part and the part's real width; angles in fp64
+// as in Wan's rope_params.  act_cos/act_sin[f, d] for the action module (pair d / 2).
+__global__ void rope_table_kernel(const int* __restrict__ chunk, int F, int th, int tw, int hd, double theta,
+                                  float2* __restrict__ table, int act_hd, float* __restrict__ act_cos,
+                                  float* __restrict__ act_sin) {
+  const int half = hd / 2;
+  const int nt = half - 2 * (half / 3), nh = half / 3;
+  const int s0 = __ldg(chunk + 1);   // first absolute latent frame of the chunk
+  const int L = F * th * tw;
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx < L * half) {
+    const int tok = idx / half, i = idx % half;
+    const int f = tok / (th * tw), h = (tok / tw) % th, w = tok % tw;
+    int pos, j, part;
+    if (i < nt) { pos = s0 + f; j = i; part = 2 * nt; }
+    else if (i < nt + nh) { pos = h; j = i - nt; part = 2 * nh; }
+    else { pos = w; j = i - nt - nh; part = 2 * nh; }
+    const double ang = (double)pos * (1.0 / pow(theta, (double)(2 * j) / (double)part));
+    double sn, cs;
+    sincos(ang, &sn, &cs);
+    table[idx] = make_float2((float)cs, (float)sn);
+  }
+  if (act_cos && idx < F * act_hd) {
+    const int f = idx / act_hd, d = idx % act_hd, j = d >> 1;
+    const double ang = (double)(s0 + f) * (1.0 / pow(theta, (double)(2 * j) / (double)act_hd));
+    double sn, cs;
+    sincos(ang, &sn, &cs);
+    act_cos[idx] = (float)cs;
+    act_sin[idx] = (float)sn;
+  }
+}
+
+int rope_tables(const int* chunk, int F, int th, int tw, int hd, double theta, float2* table, int act_hd,
+                float* act_cos, float* act_sin, cudaStream_t s) {
+  const int n = F * th * tw * (hd / 2);
+  const int m = n > F * act_hd ? n : F * act_hd;
+  rope_table_kernel<<<(m + 255) / 256, 256, 0, s>>>(chunk, F, th, tw, hd, theta, table, act_hd, act_cos, act_sin);
+  return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
+}
+
+// ------------------------------------------------------------------ small-M linear
+// out[m, n] = act_out(sum_k act_in(x[m, k]) W[n, k] + b[n]), one warp per output column n.
+template <typename Tx>
+__global__ void __launch_bounds__(256) smallm_linear_kernel(const Tx* __restrict__ x, int ldx, int M,
+                                                            const __nv_bfloat16* __restrict__ W, int ldw,
+                                                            const __nv_bfloat16* __restrict__ bias, int N, int K,
+                                                            int act_in, int act_out, float* __restrict__ outf,
+                                                            __nv_bfloat16* __restrict__ outb, int ldo) {
+  const int n = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (n >= N) return;
+  const __nv_bfloat16* wr = W + (size_t)n * ldw;
+  const float bn = bias ? __bfloat162float(bias[n]) : 0.f;
+  for (int m = 0; m < M; ++m) {
+    const Tx* xr = x + (size_t)m * ldx;
+    float acc = 0.f;
+    for (int k = lane; k < K; k += 32) {
+      float xv = (float)xr[k];
+      if (act_in == ACT_SILU) xv = xv / (1.f + __expf(-xv));
+      acc += xv * __bfloat162float(wr[k]);
+    }
+    acc = warp_sum(acc) + bn;
+    if (act_out == ACT_SILU) acc = acc / (1.f + __expf(-acc));
+    else if (act_out == ACT_GELU_ERF) acc = 0.5f * acc * (1.f + erff(acc * 0.7071067811865476f));
+    if (lane == 0) {
+      if (outf) outf[(size_t)m * ldo + n] = acc;
+      if (outb) outb[(size_t)m * ldo + n] = __float2bfloat16(acc);
+    }
+  }
+}
+
+int smallm_linear_f32(const float* x, int ldx, int M, const __nv_bfloat16* W, int ldw, const __nv_bfloat16* b, int N,
+                      int K, int act_in, int act_out, float* outf, __nv_bfloat16* outb, int ldo, cudaStream_t s) {
+  smallm_linear_kernel<float><<<(N + 7) / 8, 256, 0, s>>>(x, ldx, M, W, ldw, b, N, K, act_in, act_out, outf, outb, ldo);
+  return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
+}
+int smallm_linear_bf16(const __nv_bfloat16* x, int ldx, int M, const __nv_bfloat16* W, int ldw,
+                       const __nv_bfloat16* b, int N, int K, int act_in, int act_out, float* outf,
+                       __nv_bfloat16* outb, int ldo, cudaStream_t s) {
+  smallm_linear_kernel<__nv_bfloat16><<<(N + 7) / 8, 256, 0, s>>>(x, ldx, M, W, ldw, b, N, K, act_in, act_out, outf,
+                                                                   outb, ldo);
+  return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
+}
+
+// ------------------------------------------------------------------ time embedding helpers
+// Wan sinusoidal_embedding_1d of one timestep: [cos(t w_i), sin(t w_i)], w_i = 10000^(-i/half).
+__global__ void sinusoid_kernel(double t, int dim, float* out) {
+  const int half = dim / 2, i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < half) {
+    const double a = t * pow(10000.0, -(double)i / (double)half);
+    double sn, cs;
+    sincos(a, &sn, &cs);
+    out[i] = (float)cs;
+    out[i + half] = (float)sn;
+  }
+}
+int sinusoid(double t, int dim, float* out, cudaStream_t s) {
+  sinusoid_kernel<<<(dim / 2 + 127) / 128, 128, 0, s>>>(t, dim, out);
+  return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
+}
+
+// ee[l, j, :] = mods[l, j, :] + e0[j, :] (block adaLN tables, static.py:204);
+// head[j, :] = hmod[j, :] + e (head modulation).
+__global__ void modulation_kernel(const __nv_bfloat16* __restrict__ mods, const float* __restrict__ e0, int layers,
+                                  int D, float* __restrict__ ee, const __nv_bfloat16* __restrict__ hmod,
+                                  const float* __restrict__ e, float* __restrict__ head) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  const int n = layers * 6 * D;
+  if (i < n) ee[i] = __bfloat162float(mods[i]) + e0[i % (6 * D)];
+  if (i < 2 * D) head[i] = __bfloat162float(hmod[i]) + e[i % D];
+}
+int modulation(const __nv_bfloat16* mods, const float* e0, int layers, int D, float* ee, const __nv_bfloat16* hmod,
+               const float* e, float* head, cudaStream_t s) {
+  const int n = layers * 6 * D > 2 * D ? layers * 6 * D : 2 * D;
+  modulation_kernel<<<(n + 255) / 256, 256, 0, s>>>(mods, e0, layers, D, ee, hmod, e, head);
+  return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
+}
+
+// ------------------------------------------------------------------ patchify
+// A[token, c * 4 + i * 2 + j] = cat(x, cc)[c, f, 2 h + i, 2 w + j]  (Conv3d weight order).
+__global__ void patchify_kernel(const __nv_bfloat16* __restrict__ x, int C1, const __nv_bfloat16* __restrict__ cc,
+                                int C2, int F, int H, int W, __nv_bfloat16* __restrict__ A) {
+  const int th = H / 2, tw = W / 2, C = C1 + C2, Kp = C * 4;
+  const int L = F * th * tw;
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= L * Kp) return;
+  const int tok = idx / Kp, k = idx % Kp;
+  const int c = k >> 2, i = (k >> 1) & 1, j = k & 1;
+  const int f = tok / (th * tw), h = (tok / tw) % th, w = tok % tw;
+  const size_t off = (((size_t)f * H) + 2 * h + i) * W + 2 * w + j;
+  A[idx] = c < C1 ? x[(size_t)c * F * H * W + off] : cc[(size_t)(c - C1) * F * H * W + off];
+}
+int patchify(const __nv_bfloat16* x, int C1, const __nv_bfloat16* cc, int C2, int F, int H, int W, __nv_bfloat16* A,
+             cudaStream_t s) {
+  const int n = F * (H / 2) * (W / 2) * (C1 + C2) * 4;
+  patchify_kernel<<<(n + 255) / 256, 256, 0, s>>>(x, C1, cc, C2, F, H, W, A);
+  return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
+}
+
+// ------------------------------------------------------------------ unpatchify + scheduler
+// flow[c, f, h, w] = head[token(f, h/2, w/2), ((h%2) * 2 + (w%2)) * C + c];
+// den = bf16(x - sigma * flow); out = den (optional);
+// xnext = bf16((1 - sigma_n) * den + sigma_n * noise[f, c, h, w]) (optional).
+__global__ void scheduler_kernel(const float* __restrict__ head, const __nv_bfloat16* __restrict__ x, float sigma,
+                                 __nv_bfloat16* __restrict__ den, __nv_bfloat16* __restrict__ out_copy,
+                                 const __nv_bfloat16* __restrict__ noise, float sigma_n,
+                                 __nv_bfloat16* __restrict__ xnext, int C, int F, int H, int W) {
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  const int n = C * F * H * W;
+  if (idx >= n) return;
+  const int w = idx % W, h = (idx / W) % H, f = (idx / (W * H)) % F, c = idx / (W * H * F);
+  const int tw = W / 2, th = H / 2;
+  const int tok = (f * th + h / 2) * tw + w / 2;
+  const int feat = ((h & 1) * 2 + (w & 1)) * C + c;
+  const float flow = head[(size_t)tok * (4 * C) + feat];
+  const __nv_bfloat16 d = __float2bfloat16(__bfloat162float(x[idx]) - sigma * flow);
+  if (den) den[idx] = d;
+  if (out_copy) out_copy[idx] = d;
+  if (noise) {
+    const float nz = __bfloat162float(noise[(((size_t)f * C + c) * H + h) * W + w]);
+    xnext[idx] = __float2bfloat16((1.f - sigma_n) * __bfloat162float(d) + sigma_n * nz);
+  }
+}
+int scheduler(const float* head, const __nv_bfloat16* x, float sigma, __nv_bfloat16* den, __nv_bfloat16* out_copy,
+              const __nv_bfloat16* noise, float sigma_n, __nv_bfloat16* xnext, int C, int F, int H, int W,
+              cudaStream_t s) {
+  const int n = C * F * H * W;
+  scheduler_kernel<<<(n + 255) / 256, 256, 0, s>>>(head, x, sigma, den, out_copy, noise, sigma_n, xnext, C, F, H, W);
+  return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
+}
+
+// ------------------------------------------------------------------ action module
+// Per-head RMSNorm (64 dims, one pair per lane) + interleaved-pair RoPE.
+__device__ __forceinline__ float2 norm_rope64(float2 v, float wa, float wb, float c, float s, float eps) {
+  const float r = rsqrtf(warp_sum(v.x * v.x + v.y * v.y) * (1.f / 64.f) + eps);
+  const float a = v.x * r * wa, b = v.y * r * wb;
+  return make_float2(a * c - b * s, b * c + a * s);
+}
+__device__ __forceinline__ float2 ld2(const __nv_bfloat16* p) {
+  return unpack_bf16(*reinterpret_cast<const uint32_t*>(p));
+}
+__device__ __forceinline__ void st2(__nv_bfloat16* p, float2 v) {
+  *reinterpret_cast<uint32_t*>(p) = pack_bf16(v.x, v.y);
+}
+__device__ __forceinline__ float2 bround(float2 v) { return unpack_bf16(pack_bf16(v.x, v.y)); }
+
+// Mouse branch: one warp per (spatial position s, head h).  qkv [L, 3A] rows f * S + s;
+// history mk/mv [S, F, AH, 64]; out [L, A].  Keys: [history (unless first) | current].
+template <int F>
+__global__ void __launch_bounds__(256) mouse_attn_kernel(const __nv_bfloat16* __restrict__ qkv,
+                                                         const __nv_bfloat16* __restrict__ wq,
+                                                         const __nv_bfloat16* __restrict__ wk,
+                                                         const float* __restrict__ acos_,
+                                                         const float* __restrict__ asin_, __nv_bfloat16* mk,
+                                                         __nv_bfloat16* mv, int first, int write,
+                                                         __nv_bfloat16* __restrict__ out, int S, int AH, float eps) {
+  const int wid = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (wid >= S * AH) return;
+  const int s = wid / AH, h = wid % AH, A = AH * 64, d = 2 * lane;
+  const float2 wqv = ld2(wq + d), wkv = ld2(wk + d);
+  float2 q[F], kc[F], vc[F], kh[F], vh[F];
+#pragma unroll
+  for (int f = 0; f < F; ++f) {
+    const __nv_bfloat16* r = qkv + (size_t)(f * S + s) * 3 * A + h * 64 + d;
+    const float c = acos_[f * 64 + d], sn = asin_[f * 64 + d];
+    q[f] = bround(norm_rope64(ld2(r), wqv.x, wqv.y, c, sn, eps));
+    kc[f] = bround(norm_rope64(ld2(r + A), wkv.x, wkv.y, c, sn, eps));
+    vc[f] = ld2(r + 2 * A);
+    const size_t ho = (((size_t)s * F + f) * AH + h) * 64 + d;
+    kh[f] = first ? make_float2(0.f, 0.f) : ld2(mk + ho);
+    vh[f] = first ? make_float2(0.f, 0.f) : ld2(mv + ho);
+  }
+  const float scale = 0.125f;   // 1 / sqrt(64)
+#pragma unroll
+  for (int f = 0; f < F; ++f) {
+    float sc[2 * F];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < F; ++j) {
+      sc[j] = first ? -INFINITY : warp_sum(q[f].x * kh[j].x + q[f].y * kh[j].y) * scale;
+      sc[F + j] = warp_sum(q[f].x * kc[j].x + q[f].y * kc[j].y) * scale;
+      mx = fmaxf(mx, fmaxf(sc[j], sc[F + j]));
+    }
+    float den = 0.f, ox = 0.f, oy = 0.f;
+#pragma unroll
+    for (int j = 0; j < F; ++j) {
+      const float ph = __expf(sc[j] - mx), pc = __expf(sc[F + j] - mx);
+      den += ph + pc;
+      ox += ph * vh[j].x + pc * vc[j].x;
+      oy += ph * vh[j].y + pc * vc[j].y;
+    }
+    st2(out + (size_t)(f * S + s) * A + h * 64 + d, make_float2(ox / den, oy / den));
+  }
+  if (write) {
+#pragma unroll
+    for (int f = 0; f < F; ++f) {
+      const size_t ho = (((size_t)s * F + f) * AH + h) * 64 + d;
+      st2(mk + ho, kc[f]);
+      st2(mv + ho, vc[f]);
+    }
+  }
+}
+
+int mouse_attn(const __nv_bfloat16* qkv, const __nv_bfloat16* wq, const __nv_bfloat16* wk, const float* acos_,
+               const float* asin_, __nv_bfloat16* mk, __nv_bfloat16* mv, int first, int write, __nv_bfloat16* out,
+               int S, int F, int AH, float eps, cudaStream_t s) {
+  if (F != 3) return FW_ESHAPE;
+  mouse_attn_kernel<3><<<(S * AH + 7) / 8, 256, 0, s>>>(qkv, wq, wk, acos_, asin_, mk, mv, first, write, out, S, AH, eps);
+  return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
+}
+
+// Keyboard K/V of one block: kv [F, 2A] fp32 -> K = RoPE(RMSNorm(k) * wk) and V, bf16 [F, A].
+__global__ void kb_kv_kernel(const float* __restrict__ kv, const __nv_bfloat16* __restrict__ wk,
+                             const float* __restrict__ acos_, const float* __restrict__ asin_,
+                             __nv_bfloat16* __restrict__ kout, __nv_bfloat16* __restrict__ vout, int F, int AH,
+                             float eps) {
+  const int wid = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (wid >= F * AH) return;
+  const int f = wid / AH, h = wid % AH, A = AH * 64, d = 2 * lane;
+  const float2 w = ld2(wk + d);
+  const float* r = kv + (size_t)f * 2 * A + h * 64 + d;
+  const float2 k = norm_rope64(make_float2(r[0], r[1]), w.x, w.y, acos_[f * 64 + d], asin_[f * 64 + d], eps);
+  st2(kout + (size_t)f * A + h * 64 + d, k);
+  st2(vout + (size_t)f * A + h * 64 + d, make_float2(r[A], r[A + 1]));
+}
+int kb_kv(const float* kv, const __nv_bfloat16* wk, const float* acos_, const float* asin_, __nv_bfloat16* kout,
+          __nv_bfloat16* vout, int F, int AH, float eps, cudaStream_t s) {
+  kb_kv_kernel<<<(F * AH + 3) / 4, 128, 0, s>>>(kv, wk, acos_, asin_, kout, vout, F, AH, eps);
+  return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
+}
+
+// Keyboard attention: one warp per (token, head); q = RoPE(RMSNorm(mq) * wq) at the token's
+// frame; keys [kk (unless first) | current], F each, shared by all tokens.
+template <int F>
+__global__ void __launch_bounds__(256) kb_attn_kernel(const __nv_bfloat16* __restrict__ mq,
+                                                      const __nv_bfloat16* __restrict__ wq,
+                                                      const float* __restrict__ acos_,
+                                                      const float* __restrict__ asin_,
+                                                      const __nv_bfloat16* __restrict__ kh,
+                                                      const __nv_bfloat16* __restrict__ vh,
+                                                      const __nv_bfloat16* __restrict__ kc,
+                                                      const __nv_bfloat16* __restrict__ vc, int first,
+                                                      __nv_bfloat16* __restrict__ out, int L, int S, int AH, float eps) {
+  const int wid = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (wid >= L * AH) return;
+  const int row = wid / AH, h = wid % AH, f = row / S, A = AH * 64, d = 2 * lane;
+  const float2 w = ld2(wq + d);
+  const float2 q = bround(norm_rope64(ld2(mq + (size_t)row * A + h * 64 + d), w.x, w.y, acos_[f * 64 + d],
+                                      asin_[f * 64 + d], eps));
+  float sc[2 * F];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < F; ++j) {
+    const float2 a = ld2(kh + (size_t)j * A + h * 64 + d), b = ld2(kc + (size_t)j * A + h * 64 + d);
+    sc[j] = first ? -INFINITY : warp_sum(q.x * a.x + q.y * a.y) * 0.125f;
+    sc[F + j] = warp_sum(q.x * b.x + q.y * b.y) * 0.125f;
+    mx = fmaxf(mx, fmaxf(sc[j], sc[F + j]));
+  }
+  float den = 0.f, ox = 0.f, oy = 0.f;
+#pragma unroll
+  for (int j = 0; j < F; ++j) {
+    const float ph = __expf(sc[j] - mx), pc = __expf(sc[F + j] - mx);
+    const float2 a = ld2(vh + (size_t)j * A + h * 64 + d), b = ld2(vc + (size_t)j * A + h * 64 + d);
+    den += ph + pc;
+    ox += ph * a.x + pc * b.x;
+    oy += ph * a.y + pc * b.y;
+  }
+  st2(out + (size_t)row * A + h * 64 + d, make_float2(ox / den, oy / den));
+}
+int kb_attn(const __nv_bfloat16* mq, const __nv_bfloat16* wq, const float* acos_, const float* asin_,
+            const __nv_bfloat16* kh, const __nv_bfloat16* vh, const __nv_bfloat16* kc, const __nv_bfloat16* vc,
+            int first, __nv_bfloat16* out, int L, int S, int F, int AH, float eps, cudaStream_t s) {
+  if (F != 3) return FW_ESHAPE;
+  kb_attn_kernel<3><<<(L * AH + 7) / 8, 256, 0, s>>>(mq, wq, acos_, asin_, kh, vh, kc, vc, first, out, L, S, AH, eps);
+  return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
+}
+
+// ------------------------------------------------------------------ copies
+// Vectorised copy: 16-byte body (both pointers 16-byte aligned), byte tail.
+__global__ void __launch_bounds__(256) copy_kernel(uint4* __restrict__ dst, const uint4* __restrict__ src, size_t n16,
+                                                   uint8_t* __restrict__ dtail, const uint8_t* __restrict__ stail,
+                                                   int ntail) {
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  for (; i + 3 * stride < n16; i += 4 * stride) {
+    const uint4 a = __ldcs(src + i), b = __ldcs(src + i + stride), c = __ldcs(src + i + 2 * stride),
+                d = __ldcs(src + i + 3 * stride);
+    __stcs(dst + i, a);
+    __stcs(dst + i + stride, b);
+    __stcs(dst + i + 2 * stride, c);
+    __stcs(dst + i + 3 * stride, d);
+  }
+  for (; i < n16; i += stride) __stcs(dst + i, __ldcs(src + i));
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t < ntail) dtail[t] = stail[t];
+}
+int copy_bytes(void* dst, const void* src, size_t bytes, cudaStream_t s) {
+  if (!dst || !src) return FW_EINVAL;
+  if ((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src)) & 15u) return FW_EALIGN;
+  if (bytes == 0) return 0;
+  const size_t n16 = bytes / 16;
+  const int ntail = (int)(bytes % 16);
+  size_t want = (n16 + 255) / 256;
+  const size_t cap = (size_t)num_sms() * 8;
+  const int grid = (int)(want < 1 ? 1 : (want > cap ? cap : want));
+  copy_kernel<<<grid, 256, 0, s>>>(reinterpret_cast<uint4*>(dst), reinterpret_cast<const uint4*>(src), n16,
+                                   reinterpret_cast<uint8_t*>(dst) + n16 * 16,
+                                   reinterpret_cast<const uint8_t*>(src) + n16 * 16, ntail);
+  return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
+}
+
+}  // namespace fw

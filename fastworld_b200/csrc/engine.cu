@@ -1,0 +1,716 @@
+// Session engine: the chunk forward of the Matrix-Game-2-shaped causal Wan DiT as a fixed
+// sequence of sm_100a kernel launches over caller-owned buffers.
+//
+// Mirrors StaticMG (fastworld/models/mg2/static.py:27-284): static buffers bound once
+// (__init__, 28-73), `_net` (194-230) as fw_forward, `_chunk` (232-242) as fw_chunk and
+// `_prefill` (244-245) as fw_prefill.  All TMA descriptors and kernel arguments are built at
+// fw_finalize; a launch call only enqueues kernels, so every call is graph-capturable.
+//
+// Work hoisted out of the per-forward loop (exact: the inputs do not change within a chunk):
+// the image-context MLP and the per-block cross-attention K/V (static.py:201,190-191) and the
+// keyboard K/V of the action module (static.py:165-172) are computed once per chunk.
+#include <cmath>
+#include <cstring>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/fastworld_b200.h"
+#include "fw_elem.h"
+#include "fw_internal.h"
+
+namespace fw {
+
+struct Tensor {
+  std::string name;
+  int kind, dtype, ndim;
+  int64_t shape[5];
+  size_t bytes;
+  void* ptr = nullptr;
+};
+
+struct GemmOp {
+  CUtensorMap a, b;
+  int bn = 256;
+  GemmArgs args;
+  bool valid = false;
+};
+
+struct AttnOp {
+  CUtensorMap q, k0, v0, k1, v1;
+  AttnArgs args;
+};
+
+struct Layer {
+  int act = -1;   // index among action blocks, -1 if none
+  GemmOp qkv, o, caq, cakv, cao, ff0, ff2;
+  AttnOp self_first, self_steady, cross;
+  // action module
+  GemmOp mlp1, mlp2, tqkv, pmouse, mattq, pkb;
+};
+
+}  // namespace fw
+
+struct fw_handle {
+  fw_config cfg;
+  std::vector<fw::Tensor> tensors;
+  std::unordered_map<std::string, int> index;
+  bool finalized = false;
+  // dims
+  int L, S, F, D, H, HD, FF, A, AH, Mh, Kh, nA, th, tw, Ctx, Cd, Kp, OUT, KC, PAD;
+  size_t lat_elems;
+  // workspace layout (offsets into "workspace")
+  std::vector<std::pair<std::string, size_t>> ws_off;
+  size_t ws_bytes = 0;
+  // resolved pointers
+  float *xs, *headout, *rope, *acos_, *asin_, *tsin, *th_, *e, *e0, *ee, *hmod, *ke1, *ke, *kbkv, *fbias;
+  __nv_bfloat16 *y, *xbf, *q, *kcur, *vcur, *ao, *hb, *hb2, *patchA, *xa, *xb, *den, *den_ctx, *ctx_a, *ctx_h,
+      *ctx_o, *ctx, *ckv, *kbK, *kbV;
+  int* consts;
+  int* status;
+  std::vector<fw::Layer> layers;
+  fw::GemmOp patch, head, fc1, fc2;
+};
+
+namespace fw {
+
+static size_t dtype_size(int dt) { return dt == FW_BF16 ? 2 : (dt == FW_U8 ? 1 : 4); }
+
+static void add_tensor(fw_handle* h, const std::string& name, int kind, int dtype, std::vector<int64_t> shape) {
+  Tensor t;
+  t.name = name;
+  t.kind = kind;
+  t.dtype = dtype;
+  t.ndim = (int)shape.size();
+  size_t n = 1;
+  for (int i = 0; i < 5; ++i) t.shape[i] = i < t.ndim ? shape[i] : 0;
+  for (auto v : shape) n *= (size_t)v;
+  t.bytes = n * dtype_size(dtype);
+  h->index[name] = (int)h->tensors.size();
+  h->tensors.push_back(t);
+}
+
+static void* ptr_of(fw_handle* h, const std::string& name) {
+  auto it = h->index.find(name);
+  return it == h->index.end() ? nullptr : h->tensors[it->second].ptr;
+}
+template <typename T>
+static T* P(fw_handle* h, const std::string& name) {
+  return reinterpret_cast<T*>(ptr_of(h, name));
+}
+static const __nv_bfloat16* W(fw_handle* h, const std::string& name) { return P<const __nv_bfloat16>(h, name); }
+
+static size_t ws_add(fw_handle* h, const char* name, size_t bytes) {
+  h->ws_bytes = (h->ws_bytes + 1023) & ~(size_t)1023;
+  const size_t off = h->ws_bytes;
+  h->ws_off.push_back({name, off});
+  h->ws_bytes += bytes;
+  return off;
+}
+
+static int register_tensors(fw_handle* h) {
+  const fw_config& c = h->cfg;
+  const int D = h->D, FF = h->FF, A = h->A;
+  auto wt = [&](const std::string& n, std::vector<int64_t> s) { add_tensor(h, n, FW_KIND_WEIGHT, FW_BF16, s); };
+  wt("patch.w", {D, h->Kp});
+  wt("patch.b", {D});
+  wt("time.0.w", {D, c.freq_dim});
+  wt("time.0.b", {D});
+  wt("time.2.w", {D, D});
+  wt("time.2.b", {D});
+  wt("tproj.w", {6 * D, D});
+  wt("tproj.b", {6 * D});
+  wt("img.ln0.w", {h->Cd});
+  wt("img.ln0.b", {h->Cd});
+  wt("img.fc1.w", {h->Cd, h->Cd});
+  wt("img.fc1.b", {h->Cd});
+  wt("img.fc2.w", {D, h->Cd});
+  wt("img.fc2.b", {D});
+  wt("img.ln1.w", {D});
+  wt("img.ln1.b", {D});
+  wt("head.mod", {2, D});
+  wt("head.w", {h->OUT, D});
+  wt("head.b", {h->OUT});
+  wt("mods", {c.layers, 6, D});
+  for (int i = 0; i < c.layers; ++i) {
+    const std::string p = "b" + std::to_string(i) + ".";
+    wt(p + "sa.qkv.w", {3 * D, D});
+    wt(p + "sa.qkv.b", {3 * D});
+    wt(p + "sa.o.w", {D, D});
+    wt(p + "sa.o.b", {D});
+    wt(p + "sa.nq.w", {D});
+    wt(p + "sa.nk.w", {D});
+    wt(p + "n3.w", {D});
+    wt(p + "n3.b", {D});
+    wt(p + "ca.q.w", {D, D});
+    wt(p + "ca.q.b", {D});
+    wt(p + "ca.kv.w", {2 * D, D});
+    wt(p + "ca.kv.b", {2 * D});
+    wt(p + "ca.o.w", {D, D});
+    wt(p + "ca.o.b", {D});
+    wt(p + "ca.nq.w", {D});
+    wt(p + "ca.nk.w", {D});
+    wt(p + "ffn.0.w", {FF, D});
+    wt(p + "ffn.0.b", {FF});
+    wt(p + "ffn.2.w", {D, FF});
+    wt(p + "ffn.2.b", {D});
+    if (h->layers[i].act >= 0) {
+      const std::string a = p + "am.";
+      wt(a + "mlp1.w", {h->Mh, D + c.mouse_dim * h->PAD});
+      wt(a + "mlp1.b", {h->Mh});
+      wt(a + "mlp2.w", {h->Mh, h->Mh});
+      wt(a + "mlp2.b", {h->Mh});
+      wt(a + "mln.w", {h->Mh});
+      wt(a + "mln.b", {h->Mh});
+      wt(a + "tqkv.w", {3 * A, h->Mh});
+      wt(a + "tqkv.b", {3 * A});
+      wt(a + "mqn.w", {c.act_head_dim});
+      wt(a + "mkn.w", {c.act_head_dim});
+      wt(a + "pmouse.w", {D, A});
+      wt(a + "pmouse.b", {D});
+      wt(a + "kbe1.w", {h->Kh, c.keyboard_dim});
+      wt(a + "kbe1.b", {h->Kh});
+      wt(a + "kbe2.w", {h->Kh, h->Kh});
+      wt(a + "kbe2.b", {h->Kh});
+      wt(a + "mattq.w", {A, D});
+      wt(a + "mattq.b", {A});
+      wt(a + "kbkv.w", {2 * A, h->Kh * h->PAD});
+      wt(a + "kbkv.b", {2 * A});
+      wt(a + "kqn.w", {c.act_head_dim});
+      wt(a + "kkn.w", {c.act_head_dim});
+      wt(a + "pkb.w", {D, A});
+      wt(a + "pkb.b", {D});
+    }
+  }
+  // session state (static.py:47-54, 280-281)
+  for (int i = 0; i < c.layers; ++i) add_tensor(h, "hk." + std::to_string(i), FW_KIND_STATE, FW_BF16, {1, h->L, h->H, h->HD});
+  for (int i = 0; i < c.layers; ++i) add_tensor(h, "hv." + std::to_string(i), FW_KIND_STATE, FW_BF16, {1, h->L, h->H, h->HD});
+  const char* an[4] = {"mk.", "mv.", "kk.", "kv."};
+  for (int t = 0; t < 4; ++t)
+    for (int i = 0; i < c.layers; ++i)
+      if (h->layers[i].act >= 0)
+        add_tensor(h, an[t] + std::to_string(i), FW_KIND_STATE, FW_BF16,
+                   t < 2 ? std::vector<int64_t>{h->S, h->F, h->AH, 64} : std::vector<int64_t>{1, h->F, h->AH, 64});
+  // static inputs / outputs (static.py:58-72)
+  const std::vector<int64_t> lat = {1, c.lat_ch, h->F, c.lat_h, c.lat_w};
+  add_tensor(h, "x_in", FW_KIND_INPUT, FW_BF16, lat);
+  for (int i = 0; i + 1 < c.n_steps; ++i)
+    add_tensor(h, "noise." + std::to_string(i), FW_KIND_INPUT, FW_BF16, {h->F, c.lat_ch, c.lat_h, c.lat_w});
+  add_tensor(h, "cc", FW_KIND_INPUT, FW_BF16, {1, c.cond_ch, h->F, c.lat_h, c.lat_w});
+  add_tensor(h, "vis", FW_KIND_INPUT, FW_BF16, {1, h->Ctx, h->Cd});
+  add_tensor(h, "gm", FW_KIND_INPUT, FW_BF16, {1, h->F, h->PAD, c.mouse_dim});
+  add_tensor(h, "kc", FW_KIND_INPUT, FW_BF16, {1, h->KC, c.keyboard_dim});
+  add_tensor(h, "lat_in", FW_KIND_INPUT, FW_BF16, lat);
+  add_tensor(h, "chunk", FW_KIND_INPUT, FW_I32, {4});
+  add_tensor(h, "out", FW_KIND_OUTPUT, FW_BF16, lat);
+  add_tensor(h, "status", FW_KIND_STATUS, FW_I32, {4});
+  // workspace
+  const int L = h->L;
+  const size_t bf = 2, f4 = 4;
+  auto mx = [](std::initializer_list<int> v) { int m = 0; for (int x : v) m = x > m ? x : m; return m; };
+  ws_add(h, "xs", (size_t)L * D * f4);
+  ws_add(h, "y", (size_t)L * mx({D, h->Mh}) * bf);
+  ws_add(h, "xbf", (size_t)L * D * bf);
+  ws_add(h, "q", (size_t)L * D * bf);
+  ws_add(h, "kcur", (size_t)L * D * bf);
+  ws_add(h, "vcur", (size_t)L * D * bf);
+  ws_add(h, "ao", (size_t)L * mx({D, A}) * bf);
+  ws_add(h, "hb", (size_t)L * mx({FF, 3 * A, h->Mh}) * bf);
+  ws_add(h, "hb2", (size_t)L * mx({h->Mh, A}) * bf);
+  ws_add(h, "patchA", (size_t)L * h->Kp * bf);
+  ws_add(h, "headout", (size_t)L * h->OUT * f4);
+  ws_add(h, "xa", h->lat_elems * bf);
+  ws_add(h, "xb", h->lat_elems * bf);
+  ws_add(h, "den", h->lat_elems * bf);
+  ws_add(h, "den_ctx", h->lat_elems * bf);
+  ws_add(h, "ctx_a", (size_t)h->Ctx * h->Cd * bf);
+  ws_add(h, "ctx_h", (size_t)h->Ctx * h->Cd * bf);
+  ws_add(h, "ctx_o", (size_t)h->Ctx * D * bf);
+  ws_add(h, "ctx", (size_t)h->Ctx * D * bf);
+  ws_add(h, "ckv", (size_t)c.layers * 2 * h->Ctx * D * bf);
+  ws_add(h, "ke1", (size_t)h->KC * h->Kh * f4);
+  ws_add(h, "ke", (size_t)h->KC * h->Kh * f4);
+  ws_add(h, "kbkv", (size_t)h->F * 2 * A * f4);
+  ws_add(h, "kbK", (size_t)(h->nA ? h->nA : 1) * h->F * A * bf);
+  ws_add(h, "kbV", (size_t)(h->nA ? h->nA : 1) * h->F * A * bf);
+  ws_add(h, "fbias", (size_t)h->F * h->Mh * f4);
+  ws_add(h, "rope", (size_t)L * (h->HD / 2) * 2 * f4);
+  ws_add(h, "acos", (size_t)h->F * 64 * f4);
+  ws_add(h, "asin", (size_t)h->F * 64 * f4);
+  ws_add(h, "tsin", (size_t)c.freq_dim * f4);
+  ws_add(h, "th", (size_t)D * f4);
+  ws_add(h, "e", (size_t)D * f4);
+  ws_add(h, "e0", (size_t)6 * D * f4);
+  ws_add(h, "ee", (size_t)c.layers * 6 * D * f4);
+  ws_add(h, "hmod", (size_t)2 * D * f4);
+  ws_add(h, "consts", 64 * sizeof(int));
+  h->ws_bytes = (h->ws_bytes + 1023) & ~(size_t)1023;
+  add_tensor(h, "workspace", FW_KIND_WORKSPACE, FW_U8, {(int64_t)h->ws_bytes});
+  return 0;
+}
+
+static int config_check(const fw_config& c) {
+  if (c.dim <= 0 || c.heads <= 0 || c.head_dim != 128 || c.dim != c.heads * c.head_dim) return FW_ESHAPE;
+  if (c.layers <= 0 || c.ffn % 64 || c.dim % 256) return FW_ESHAPE;
+  if (c.frames != 3 || c.lat_h % 2 || c.lat_w % 2) return FW_ESHAPE;
+  if (c.act_head_dim != 64 || c.n_action < 0 || c.n_action > FW_MAX_ACTION_BLOCKS) return FW_ESHAPE;
+  if (c.n_steps < 1 || c.n_steps > FW_MAX_STEPS) return FW_EINVAL;
+  if (c.freq_dim % 2 || c.ctx_dim % 128) return FW_ESHAPE;
+  if (c.n_action && (c.mouse_hidden % 128 || c.keyboard_hidden <= 0 || c.mouse_dim * c.time_ratio * c.window % 8))
+    return FW_ESHAPE;
+  for (int i = 0; i < c.n_action; ++i)
+    if (c.action_blocks[i] < 0 || c.action_blocks[i] >= c.layers) return FW_EINVAL;
+  return 0;
+}
+
+// ---------------------------------------------------------------- op construction
+static int make_gemm(GemmOp& op, const void* A, int M, int K, int lda, const void* B, int N, int ldb, int bn,
+                     const GemmEpi& epi, int* status) {
+  op.bn = bn;
+  int rc = make_tmap_2d(&op.a, A, 2, M, K, lda, 128, 64, true);
+  if (rc) return rc;
+  rc = make_tmap_2d(&op.b, B, 2, N, K, ldb, bn, 64, true);
+  if (rc) return rc;
+  op.args.M = M;
+  op.args.N = N;
+  op.args.K = K;
+  op.args.epi = epi;
+  op.args.status = status;
+  op.valid = true;
+  return gemm_check(op.args, bn);
+}
+static int run(const GemmOp& op, cudaStream_t s) { return gemm_bf16_launch(op.a, op.b, op.bn, op.args, s); }
+static int pick_bn(int N) { return N >= 256 ? 256 : (N >= 128 ? 128 : 64); }
+
+static GemmEpi epi_bf16(void* out, int ld, const __nv_bfloat16* bias, int mode = EPI_BF16) {
+  GemmEpi e;
+  e.mode = mode;
+  e.out[0] = out;
+  e.ld_out = ld;
+  e.seg_w = 1 << 30;
+  e.bias = bias;
+  return e;
+}
+static GemmEpi epi_resid(float* xs, int ld, const __nv_bfloat16* bias, const float* gate, __nv_bfloat16* mirror) {
+  GemmEpi e;
+  e.mode = EPI_RESID_F32;
+  e.resid = xs;
+  e.ld_resid = ld;
+  e.bias = bias;
+  e.gate = gate;
+  e.gate_stride = 0;
+  e.mirror = mirror;
+  e.ld_mirror = ld;
+  return e;
+}
+
+static int make_attn(AttnOp& op, const void* q, int Lq, int heads, const void* k0, const void* v0, int cap0,
+                     const void* k1, const void* v1, int cap1, const int* meta, void* out, int* status) {
+  const int cols = heads * 128;
+  int rc = make_tmap_2d(&op.q, q, 2, Lq, cols, cols, 128, 64, true);
+  if (!rc) rc = make_tmap_2d(&op.k0, k0, 2, cap0, cols, cols, 128, 64, true);
+  if (!rc) rc = make_tmap_2d(&op.v0, v0, 2, cap0, cols, cols, 128, 64, true);
+  if (!rc) rc = make_tmap_2d(&op.k1, k1, 2, cap1, cols, cols, 128, 64, true);
+  if (!rc) rc = make_tmap_2d(&op.v1, v1, 2, cap1, cols, cols, 128, 64, true);
+  if (rc) return rc;
+  op.args.Lq = Lq;
+  op.args.heads = heads;
+  op.args.meta = meta;
+  op.args.max_keys0 = cap0;
+  op.args.max_keys1 = cap1;
+  op.args.out = reinterpret_cast<__nv_bfloat16*>(out);
+  op.args.ld_out = cols;
+  op.args.scale_log2 = (float)(1.4426950408889634 / std::sqrt(128.0));
+  op.args.status = status;
+  return 0;
+}
+static int run(const AttnOp& op, cudaStream_t s) { return attention_launch(op.q, op.k0, op.v0, op.k1, op.v1, op.args, s); }
+
+#define FW_TRY(x)         \
+  do {                    \
+    int _rc = (x);        \
+    if (_rc) return _rc;  \
+  } while (0)
+
+static int finalize(fw_handle* h) {
+  for (auto& t : h->tensors)
+    if (!t.ptr) return FW_ENOTBOUND;
+  if (!get_encode_fn()) return FW_ENODRIVER;
+  uint8_t* ws = P<uint8_t>(h, "workspace");
+  auto WS = [&](const char* n) -> void* {
+    for (auto& p : h->ws_off)
+      if (p.first == n) return ws + p.second;
+    return nullptr;
+  };
+  h->xs = (float*)WS("xs");
+  h->y = (__nv_bfloat16*)WS("y");
+  h->xbf = (__nv_bfloat16*)WS("xbf");
+  h->q = (__nv_bfloat16*)WS("q");
+  h->kcur = (__nv_bfloat16*)WS("kcur");
+  h->vcur = (__nv_bfloat16*)WS("vcur");
+  h->ao = (__nv_bfloat16*)WS("ao");
+  h->hb = (__nv_bfloat16*)WS("hb");
+  h->hb2 = (__nv_bfloat16*)WS("hb2");
+  h->patchA = (__nv_bfloat16*)WS("patchA");
+  h->headout = (float*)WS("headout");
+  h->xa = (__nv_bfloat16*)WS("xa");
+  h->xb = (__nv_bfloat16*)WS("xb");
+  h->den = (__nv_bfloat16*)WS("den");
+  h->den_ctx = (__nv_bfloat16*)WS("den_ctx");
+  h->ctx_a = (__nv_bfloat16*)WS("ctx_a");
+  h->ctx_h = (__nv_bfloat16*)WS("ctx_h");
+  h->ctx_o = (__nv_bfloat16*)WS("ctx_o");
+  h->ctx = (__nv_bfloat16*)WS("ctx");
+  h->ckv = (__nv_bfloat16*)WS("ckv");
+  h->ke1 = (float*)WS("ke1");
+  h->ke = (float*)WS("ke");
+  h->kbkv = (float*)WS("kbkv");
+  h->kbK = (__nv_bfloat16*)WS("kbK");
+  h->kbV = (__nv_bfloat16*)WS("kbV");
+  h->fbias = (float*)WS("fbias");
+  h->rope = (float*)WS("rope");
+  h->acos_ = (float*)WS("acos");
+  h->asin_ = (float*)WS("asin");
+  h->tsin = (float*)WS("tsin");
+  h->th_ = (float*)WS("th");
+  h->e = (float*)WS("e");
+  h->e0 = (float*)WS("e0");
+  h->ee = (float*)WS("ee");
+  h->hmod = (float*)WS("hmod");
+  h->consts = (int*)WS("consts");
+  h->status = P<int>(h, "status");
+  // constant device tables: attention segment lengths {first, steady, cross}
+  int consts[8] = {0, h->L, h->L, h->L, h->Ctx, 0, 0, 0};
+  if (cudaMemcpy(h->consts, consts, sizeof(consts), cudaMemcpyHostToDevice) != cudaSuccess) return FW_ECUDA;
+  const int L = h->L, D = h->D, Ctx = h->Ctx;
+  int* st = h->status;
+  // patch embedding and head
+  FW_TRY(make_gemm(h->patch, h->patchA, L, h->Kp, h->Kp, W(h, "patch.w"), D, h->Kp, pick_bn(D),
+                   [&] { GemmEpi e = epi_bf16(h->xs, D, W(h, "patch.b"), EPI_F32); return e; }(), st));
+  FW_TRY(make_gemm(h->head, h->y, L, D, D, W(h, "head.w"), h->OUT, D, pick_bn(h->OUT),
+                   epi_bf16(h->headout, h->OUT, W(h, "head.b"), EPI_F32), st));
+  // image-context MLP (M = Ctx)
+  FW_TRY(make_gemm(h->fc1, h->ctx_a, Ctx, h->Cd, h->Cd, W(h, "img.fc1.w"), h->Cd, h->Cd, 128,
+                   epi_bf16(h->ctx_h, h->Cd, W(h, "img.fc1.b"), EPI_GELU_ERF_BF16), st));
+  FW_TRY(make_gemm(h->fc2, h->ctx_h, Ctx, h->Cd, h->Cd, W(h, "img.fc2.w"), D, h->Cd, 128,
+                   epi_bf16(h->ctx_o, D, W(h, "img.fc2.b")), st));
+  for (int i = 0; i < h->cfg.layers; ++i) {
+    Layer& ly = h->layers[i];
+    const std::string p = "b" + std::to_string(i) + ".";
+    const float* ee = h->ee + (size_t)i * 6 * D;
+    {
+      GemmEpi e = epi_bf16(h->q, D, W(h, p + "sa.qkv.b"));
+      e.out[1] = h->kcur;
+      e.out[2] = h->vcur;
+      e.seg_w = D;
+      FW_TRY(make_gemm(ly.qkv, h->y, L, D, D, W(h, p + "sa.qkv.w"), 3 * D, D, 256, e, st));
+    }
+    FW_TRY(make_gemm(ly.o, h->ao, L, D, D, W(h, p + "sa.o.w"), D, D, 256,
+                     epi_resid(h->xs, D, W(h, p + "sa.o.b"), ee + 2 * D, nullptr), st));
+    FW_TRY(make_gemm(ly.caq, h->y, L, D, D, W(h, p + "ca.q.w"), D, D, 256, epi_bf16(h->q, D, W(h, p + "ca.q.b")), st));
+    {
+      __nv_bfloat16* ck = h->ckv + (size_t)i * 2 * Ctx * D;
+      GemmEpi e = epi_bf16(ck, D, W(h, p + "ca.kv.b"));
+      e.out[1] = ck + (size_t)Ctx * D;
+      e.seg_w = D;
+      FW_TRY(make_gemm(ly.cakv, h->ctx, Ctx, D, D, W(h, p + "ca.kv.w"), 2 * D, D, 256, e, st));
+    }
+    FW_TRY(make_gemm(ly.cao, h->ao, L, D, D, W(h, p + "ca.o.w"), D, D, 256,
+                     epi_resid(h->xs, D, W(h, p + "ca.o.b"), nullptr, ly.act >= 0 ? h->xbf : nullptr), st));
+    FW_TRY(make_gemm(ly.ff0, h->y, L, D, D, W(h, p + "ffn.0.w"), h->FF, D, 256,
+                     epi_bf16(h->hb, h->FF, W(h, p + "ffn.0.b"), EPI_GELU_BF16), st));
+    FW_TRY(make_gemm(ly.ff2, h->hb, L, h->FF, h->FF, W(h, p + "ffn.2.w"), D, h->FF, 256,
+                     epi_resid(h->xs, D, W(h, p + "ffn.2.b"), ee + 5 * D, nullptr), st));
+    const void* hk = ptr_of(h, "hk." + std::to_string(i));
+    const void* hv = ptr_of(h, "hv." + std::to_string(i));
+    FW_TRY(make_attn(ly.self_first, h->q, L, h->H, hk, hv, L, h->kcur, h->vcur, L, h->consts + 0, h->ao, st));
+    FW_TRY(make_attn(ly.self_steady, h->q, L, h->H, hk, hv, L, h->kcur, h->vcur, L, h->consts + 2, h->ao, st));
+    {
+      const __nv_bfloat16* ck = h->ckv + (size_t)i * 2 * Ctx * D;
+      FW_TRY(make_attn(ly.cross, h->q, L, h->H, ck, ck + (size_t)Ctx * D, Ctx, ck, ck + (size_t)Ctx * D, Ctx,
+                       h->consts + 4, h->ao, st));
+    }
+    if (ly.act >= 0) {
+      const std::string a = p + "am.";
+      const int A = h->A, Mh = h->Mh, K1 = D + h->cfg.mouse_dim * h->PAD;
+      GemmEpi e1 = epi_bf16(h->hb, Mh, nullptr, EPI_GELU_BF16);
+      e1.bias = nullptr;
+      e1.fbias = h->fbias;
+      e1.fbias_stride = Mh;
+      e1.rows_per_frame = h->S;
+      FW_TRY(make_gemm(ly.mlp1, h->xbf, L, D, D, W(h, a + "mlp1.w"), Mh, K1, pick_bn(Mh), e1, st));
+      FW_TRY(make_gemm(ly.mlp2, h->hb, L, Mh, Mh, W(h, a + "mlp2.w"), Mh, Mh, pick_bn(Mh),
+                       epi_bf16(h->hb2, Mh, W(h, a + "mlp2.b")), st));
+      FW_TRY(make_gemm(ly.tqkv, h->y, L, Mh, Mh, W(h, a + "tqkv.w"), 3 * A, Mh, pick_bn(3 * A),
+                       epi_bf16(h->hb, 3 * A, W(h, a + "tqkv.b")), st));
+      FW_TRY(make_gemm(ly.pmouse, h->ao, L, A, A, W(h, a + "pmouse.w"), D, A, 256,
+                       epi_resid(h->xs, D, W(h, a + "pmouse.b"), nullptr, h->xbf), st));
+      FW_TRY(make_gemm(ly.mattq, h->xbf, L, D, D, W(h, a + "mattq.w"), A, D, pick_bn(A),
+                       epi_bf16(h->hb2, A, W(h, a + "mattq.b")), st));
+      FW_TRY(make_gemm(ly.pkb, h->ao, L, A, A, W(h, a + "pkb.w"), D, A, 256,
+                       epi_resid(h->xs, D, W(h, a + "pkb.b"), nullptr, nullptr), st));
+    }
+  }
+  h->finalized = true;
+  return 0;
+}
+
+// ---------------------------------------------------------------- launch sequence
+// Per-chunk prologue: RoPE tables, image context + cross K/V, keyboard K/V.
+static int prologue(fw_handle* h, cudaStream_t s) {
+  const fw_config& c = h->cfg;
+  const int D = h->D, Ctx = h->Ctx;
+  FW_TRY(rope_tables(P<int>(h, "chunk"), h->F, h->th, h->tw, h->HD, (double)c.rope_theta,
+                     reinterpret_cast<float2*>(h->rope), 64, h->acos_, h->asin_, s));
+  FW_TRY(ln_bf16(P<__nv_bfloat16>(h, "vis"), h->Cd, Ctx, h->Cd, c.eps_ln, nullptr, nullptr, W(h, "img.ln0.w"),
+                 W(h, "img.ln0.b"), h->ctx_a, h->Cd, s));
+  FW_TRY(run(h->fc1, s));
+  FW_TRY(run(h->fc2, s));
+  FW_TRY(ln_bf16(h->ctx_o, D, Ctx, D, c.eps_ln, nullptr, nullptr, W(h, "img.ln1.w"), W(h, "img.ln1.b"), h->ctx, D, s));
+  for (int i = 0; i < c.layers; ++i) {
+    const std::string p = "b" + std::to_string(i) + ".";
+    __nv_bfloat16* ck = h->ckv + (size_t)i * 2 * Ctx * D;
+    FW_TRY(run(h->layers[i].cakv, s));
+    FW_TRY(rms_rope(ck, D, Ctx, D, c.eps, W(h, p + "ca.nk.w"), nullptr, 128, ck, D, s));
+  }
+  for (int i = 0; i < c.layers; ++i) {
+    const Layer& ly = h->layers[i];
+    if (ly.act < 0) continue;
+    const std::string a = "b" + std::to_string(i) + ".am.";
+    const int A = h->A, Kh = h->Kh;
+    FW_TRY(smallm_linear_bf16(P<__nv_bfloat16>(h, "kc"), c.keyboard_dim, h->KC, W(h, a + "kbe1.w"), c.keyboard_dim,
+                              W(h, a + "kbe1.b"), Kh, c.keyboard_dim, ACT_NONE, ACT_SILU, h->ke1, nullptr, Kh, s));
+    FW_TRY(smallm_linear_f32(h->ke1, Kh, h->KC, W(h, a + "kbe2.w"), Kh, W(h, a + "kbe2.b"), Kh, Kh, ACT_NONE, ACT_NONE,
+                             h->ke, nullptr, Kh, s));
+    // window of frame f = pixel-frame rows [ratio * f, ratio * f + pad_t) of the embedded keys
+    FW_TRY(smallm_linear_f32(h->ke, c.time_ratio * Kh, h->F, W(h, a + "kbkv.w"), Kh * h->PAD, W(h, a + "kbkv.b"),
+                             2 * A, Kh * h->PAD, ACT_NONE, ACT_NONE, h->kbkv, nullptr, 2 * A, s));
+    FW_TRY(kb_kv(h->kbkv, W(h, a + "kkn.w"), h->acos_, h->asin_, h->kbK + (size_t)ly.act * h->F * A,
+                 h->kbV + (size_t)ly.act * h->F * A, h->F, h->AH, c.eps, s));
+  }
+  return 0;
+}
+
+static int action(fw_handle* h, int i, int first, int write, cudaStream_t s) {
+  const fw_config& c = h->cfg;
+  const Layer& ly = h->layers[i];
+  const std::string a = "b" + std::to_string(i) + ".am.";
+  const std::string si = std::to_string(i);
+  const int D = h->D, A = h->A, Mh = h->Mh, K1 = D + c.mouse_dim * h->PAD;
+  // mouse window contribution of mouse_mlp[0], one row per frame: b + gm_f . W[:, D:]
+  FW_TRY(smallm_linear_bf16(P<__nv_bfloat16>(h, "gm"), c.mouse_dim * h->PAD, h->F, W(h, a + "mlp1.w") + D, K1,
+                            W(h, a + "mlp1.b"), Mh, c.mouse_dim * h->PAD, ACT_NONE, ACT_NONE, h->fbias, nullptr, Mh, s));
+  FW_TRY(run(ly.mlp1, s));
+  FW_TRY(run(ly.mlp2, s));
+  FW_TRY(ln_bf16(h->hb2, Mh, h->L, Mh, c.eps_ln, nullptr, nullptr, W(h, a + "mln.w"), W(h, a + "mln.b"), h->y, Mh, s));
+  FW_TRY(run(ly.tqkv, s));
+  FW_TRY(mouse_attn(h->hb, W(h, a + "mqn.w"), W(h, a + "mkn.w"), h->acos_, h->asin_, P<__nv_bfloat16>(h, "mk." + si),
+                    P<__nv_bfloat16>(h, "mv." + si), first, write, h->ao, h->S, h->F, h->AH, c.eps, s));
+  FW_TRY(run(ly.pmouse, s));
+  FW_TRY(run(ly.mattq, s));
+  const __nv_bfloat16* kc = h->kbK + (size_t)ly.act * h->F * A;
+  const __nv_bfloat16* vc = h->kbV + (size_t)ly.act * h->F * A;
+  FW_TRY(kb_attn(h->hb2, W(h, a + "kqn.w"), h->acos_, h->asin_, P<__nv_bfloat16>(h, "kk." + si),
+                 P<__nv_bfloat16>(h, "kv." + si), kc, vc, first, h->ao, h->L, h->S, h->F, h->AH, c.eps, s));
+  if (write) {
+    FW_TRY(copy_bytes(ptr_of(h, "kk." + si), kc, (size_t)h->F * A * 2, s));
+    FW_TRY(copy_bytes(ptr_of(h, "kv." + si), vc, (size_t)h->F * A * 2, s));
+  }
+  FW_TRY(run(ly.pkb, s));
+  return 0;
+}
+
+// One `_net` (static.py:194-230) from latent `x` at timestep index `step`; writes den and,
+// when `noise`, the next latent xnext = add_noise(den).
+static int forward(fw_handle* h, int step, int first, int write, const __nv_bfloat16* x, __nv_bfloat16* den,
+                   __nv_bfloat16* out_copy, const __nv_bfloat16* noise, float t_next, __nv_bfloat16* xnext,
+                   cudaStream_t s) {
+  const fw_config& c = h->cfg;
+  const int L = h->L, D = h->D;
+  const float t = step < c.n_steps ? c.steps[step] : 0.f;
+  const int ti = (int)t;   // the forward uses int(t) (static.py:39-40)
+  // time embedding and per-block adaLN tables
+  FW_TRY(sinusoid((double)ti, c.freq_dim, h->tsin, s));
+  FW_TRY(smallm_linear_f32(h->tsin, c.freq_dim, 1, W(h, "time.0.w"), c.freq_dim, W(h, "time.0.b"), D, c.freq_dim,
+                           ACT_NONE, ACT_SILU, h->th_, nullptr, D, s));
+  FW_TRY(smallm_linear_f32(h->th_, D, 1, W(h, "time.2.w"), D, W(h, "time.2.b"), D, D, ACT_NONE, ACT_NONE, h->e,
+                           nullptr, D, s));
+  FW_TRY(smallm_linear_f32(h->e, D, 1, W(h, "tproj.w"), D, W(h, "tproj.b"), 6 * D, D, ACT_SILU, ACT_NONE, h->e0,
+                           nullptr, 6 * D, s));
+  FW_TRY(modulation(W(h, "mods"), h->e0, c.layers, D, h->ee, W(h, "head.mod"), h->e, h->hmod, s));
+  // patch embedding of cat([x, cc])
+  FW_TRY(patchify(x, c.lat_ch, P<__nv_bfloat16>(h, "cc"), c.cond_ch, h->F, c.lat_h, c.lat_w, h->patchA, s));
+  FW_TRY(run(h->patch, s));
+  const float2* rope = reinterpret_cast<const float2*>(h->rope);
+  for (int i = 0; i < c.layers; ++i) {
+    const Layer& ly = h->layers[i];
+    const std::string p = "b" + std::to_string(i) + ".";
+    const float* ee = h->ee + (size_t)i * 6 * D;
+    FW_TRY(ln_f32(h->xs, D, L, D, c.eps, ee + 0 * D, ee + 1 * D, nullptr, nullptr, h->y, D, s));
+    FW_TRY(run(ly.qkv, s));
+    FW_TRY(rms_rope(h->q, D, L, D, c.eps, W(h, p + "sa.nq.w"), rope, h->HD, h->q, D, s));
+    FW_TRY(rms_rope(h->kcur, D, L, D, c.eps, W(h, p + "sa.nk.w"), rope, h->HD, h->kcur, D, s));
+    FW_TRY(run(first ? ly.self_first : ly.self_steady, s));
+    if (write) {   // the history is written after the attention read it (static.py:217-218)
+      FW_TRY(copy_bytes(ptr_of(h, "hk." + std::to_string(i)), h->kcur, (size_t)L * D * 2, s));
+      FW_TRY(copy_bytes(ptr_of(h, "hv." + std::to_string(i)), h->vcur, (size_t)L * D * 2, s));
+    }
+    FW_TRY(run(ly.o, s));
+    FW_TRY(ln_f32(h->xs, D, L, D, c.eps, nullptr, nullptr, W(h, p + "n3.w"), W(h, p + "n3.b"), h->y, D, s));
+    FW_TRY(run(ly.caq, s));
+    FW_TRY(rms_rope(h->q, D, L, D, c.eps, W(h, p + "ca.nq.w"), nullptr, h->HD, h->q, D, s));
+    FW_TRY(run(ly.cross, s));
+    FW_TRY(run(ly.cao, s));
+    if (ly.act >= 0) FW_TRY(action(h, i, first, write, s));
+    FW_TRY(ln_f32(h->xs, D, L, D, c.eps, ee + 3 * D, ee + 4 * D, nullptr, nullptr, h->y, D, s));
+    FW_TRY(run(ly.ff0, s));
+    FW_TRY(run(ly.ff2, s));
+  }
+  FW_TRY(ln_f32(h->xs, D, L, D, c.eps, h->hmod, h->hmod + D, nullptr, nullptr, h->y, D, s));
+  FW_TRY(run(h->head, s));
+  return scheduler(h->headout, x, (float)ti / 1000.f, den, out_copy, noise, t_next / 1000.f, xnext, c.lat_ch, h->F,
+                   c.lat_h, c.lat_w, s);
+}
+
+static int chunk(fw_handle* h, int first, cudaStream_t s) {
+  const fw_config& c = h->cfg;
+  FW_TRY(prologue(h, s));
+  const __nv_bfloat16* x = P<__nv_bfloat16>(h, "x_in");
+  __nv_bfloat16* bufs[2] = {h->xa, h->xb};
+  const int n = c.n_steps;
+  for (int i = 0; i < n; ++i) {
+    const bool last = i == n - 1;
+    __nv_bfloat16* xn = last ? nullptr : bufs[i & 1];
+    const __nv_bfloat16* nz = last ? nullptr : P<__nv_bfloat16>(h, "noise." + std::to_string(i));
+    FW_TRY(forward(h, i, first, 0, x, h->den, last ? P<__nv_bfloat16>(h, "out") : nullptr, nz,
+                   last ? 0.f : c.steps[i + 1], xn, s));
+    x = xn;
+  }
+  // context forward at t = 0 on the final denoised latent; writes the history
+  return forward(h, n, first, 1, h->den, h->den_ctx, nullptr, nullptr, 0.f, nullptr, s);
+}
+
+}  // namespace fw
+
+// ==================================================================== C ABI
+extern "C" {
+
+int fw_abi_version(void) { return FW_ABI_VERSION; }
+
+const char* fw_strerror(int code) {
+  switch (code) {
+    case FW_OK: return "ok";
+    case FW_EINVAL: return "invalid argument";
+    case FW_ESHAPE: return "unsupported or inconsistent shape";
+    case FW_EALIGN: return "pointer or stride not 16-byte aligned";
+    case FW_ECUDA: return "CUDA runtime error";
+    case FW_ENOTBOUND: return "a required tensor is not bound";
+    case FW_ENODRIVER: return "cuTensorMapEncodeTiled unavailable (driver entry point)";
+    case FW_ESTATE: return "call out of order (finalize first / already finalized)";
+    case FW_ESIZE: return "bound buffer smaller than required";
+    default: return "unknown error";
+  }
+}
+
+int fw_create(const fw_config* cfg, fw_handle** out) {
+  if (!cfg || !out) return FW_EINVAL;
+  int rc = fw::config_check(*cfg);
+  if (rc) return rc;
+  fw_handle* h = new fw_handle();
+  h->cfg = *cfg;
+  const fw_config& c = *cfg;
+  h->F = c.frames;
+  h->th = c.lat_h / 2;
+  h->tw = c.lat_w / 2;
+  h->S = h->th * h->tw;
+  h->L = h->F * h->S;
+  h->D = c.dim;
+  h->H = c.heads;
+  h->HD = c.head_dim;
+  h->FF = c.ffn;
+  h->AH = c.act_heads;
+  h->A = c.act_heads * c.act_head_dim;
+  h->Mh = c.mouse_hidden;
+  h->Kh = c.keyboard_hidden;
+  h->nA = c.n_action;
+  h->Ctx = c.ctx_tokens;
+  h->Cd = c.ctx_dim;
+  h->Kp = (c.lat_ch + c.cond_ch) * 4;
+  h->OUT = c.lat_ch * 4;
+  h->PAD = c.time_ratio * c.window;
+  h->KC = c.frames * c.time_ratio + h->PAD - 3;
+  h->lat_elems = (size_t)c.lat_ch * c.frames * c.lat_h * c.lat_w;
+  h->layers.resize(c.layers);
+  for (int j = 0; j < c.n_action; ++j) h->layers[c.action_blocks[j]].act = j;
+  fw::register_tensors(h);
+  *out = h;
+  return 0;
+}
+
+int fw_tensor_count(const fw_handle* h) { return h ? (int)h->tensors.size() : FW_EINVAL; }
+
+int fw_tensor_info_at(const fw_handle* h, int i, fw_tensor_info* info) {
+  if (!h || !info || i < 0 || i >= (int)h->tensors.size()) return FW_EINVAL;
+  const fw::Tensor& t = h->tensors[i];
+  info->name = t.name.c_str();
+  info->kind = t.kind;
+  info->dtype = t.dtype;
+  info->ndim = t.ndim;
+  for (int k = 0; k < 5; ++k) info->shape[k] = t.shape[k];
+  info->bytes = t.bytes;
+  return 0;
+}
+
+int fw_bind(fw_handle* h, const char* name, void* ptr, size_t bytes) {
+  if (!h || !name || !ptr) return FW_EINVAL;
+  if (h->finalized) return FW_ESTATE;
+  auto it = h->index.find(name);
+  if (it == h->index.end()) return FW_EINVAL;
+  fw::Tensor& t = h->tensors[it->second];
+  if (bytes < t.bytes) return FW_ESIZE;
+  if (reinterpret_cast<uintptr_t>(ptr) & 15u) return FW_EALIGN;
+  t.ptr = ptr;
+  return 0;
+}
+
+int fw_finalize(fw_handle* h) {
+  if (!h) return FW_EINVAL;
+  if (h->finalized) return FW_ESTATE;
+  return fw::finalize(h);
+}
+
+int fw_chunk(fw_handle* h, int first, void* stream) {
+  if (!h) return FW_EINVAL;
+  if (!h->finalized) return FW_ESTATE;
+  return fw::chunk(h, first, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int fw_prefill(fw_handle* h, int first, void* stream) {
+  if (!h) return FW_EINVAL;
+  if (!h->finalized) return FW_ESTATE;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  int rc = fw::prologue(h, s);
+  if (rc) return rc;
+  return fw::forward(h, h->cfg.n_steps, first, 1, fw::P<__nv_bfloat16>(h, "lat_in"), h->den_ctx, nullptr, nullptr,
+                     0.f, nullptr, s);
+}
+
+int fw_forward(fw_handle* h, int step, int first, int write, void* stream) {
+  if (!h) return FW_EINVAL;
+  if (!h->finalized) return FW_ESTATE;
+  if (step < 0 || step > h->cfg.n_steps) return FW_EINVAL;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  int rc = fw::prologue(h, s);
+  if (rc) return rc;
+  // one forward from x_in (or lat_in for the context step) into out
+  const __nv_bfloat16* x = fw::P<__nv_bfloat16>(h, step < h->cfg.n_steps ? "x_in" : "lat_in");
+  return fw::forward(h, step, first, write, x, h->den, fw::P<__nv_bfloat16>(h, "out"), nullptr, 0.f, nullptr, s);
+}
+
+void fw_destroy(fw_handle* h) { delete h; }
+
+int fw_copy(void* dst, const void* src, size_t bytes, void* stream) {
+  return fw::copy_bytes(dst, src, bytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

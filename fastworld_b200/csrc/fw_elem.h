@@ -1,0 +1,40 @@
+// Host launchers of the memory-bound kernels in elem.cu (all return 0 or a negative FW_E* code).
+#pragma once
+#include "fw_internal.h"
+
+namespace fw {
+
+enum : int { ACT_NONE = 0, ACT_SILU = 1, ACT_GELU_ERF = 2 };
+
+int ln_f32(const float* x, int ldx, int M, int D, float eps, const float* shift, const float* scale,
+           const __nv_bfloat16* w, const __nv_bfloat16* b, __nv_bfloat16* out, int ldo, cudaStream_t s);
+int ln_bf16(const __nv_bfloat16* x, int ldx, int M, int D, float eps, const float* shift, const float* scale,
+            const __nv_bfloat16* w, const __nv_bfloat16* b, __nv_bfloat16* out, int ldo, cudaStream_t s);
+int rms_rope(const __nv_bfloat16* x, int ldx, int M, int D, float eps, const __nv_bfloat16* w, const float2* rope,
+             int hd, __nv_bfloat16* out, int ldo, cudaStream_t s);
+int rope_tables(const int* chunk, int F, int th, int tw, int hd, double theta, float2* table, int act_hd,
+                float* act_cos, float* act_sin, cudaStream_t s);
+int smallm_linear_f32(const float* x, int ldx, int M, const __nv_bfloat16* W, int ldw, const __nv_bfloat16* b, int N,
+                      int K, int act_in, int act_out, float* outf, __nv_bfloat16* outb, int ldo, cudaStream_t s);
+int smallm_linear_bf16(const __nv_bfloat16* x, int ldx, int M, const __nv_bfloat16* W, int ldw,
+                       const __nv_bfloat16* b, int N, int K, int act_in, int act_out, float* outf,
+                       __nv_bfloat16* outb, int ldo, cudaStream_t s);
+int sinusoid(double t, int dim, float* out, cudaStream_t s);
+int modulation(const __nv_bfloat16* mods, const float* e0, int layers, int D, float* ee, const __nv_bfloat16* hmod,
+               const float* e, float* head, cudaStream_t s);
+int patchify(const __nv_bfloat16* x, int C1, const __nv_bfloat16* cc, int C2, int F, int H, int W, __nv_bfloat16* A,
+             cudaStream_t s);
+int scheduler(const float* head, const __nv_bfloat16* x, float sigma, __nv_bfloat16* den, __nv_bfloat16* out_copy,
+              const __nv_bfloat16* noise, float sigma_n, __nv_bfloat16* xnext, int C, int F, int H, int W,
+              cudaStream_t s);
+int mouse_attn(const __nv_bfloat16* qkv, const __nv_bfloat16* wq, const __nv_bfloat16* wk, const float* acos_,
+               const float* asin_, __nv_bfloat16* mk, __nv_bfloat16* mv, int first, int write, __nv_bfloat16* out,
+               int S, int F, int AH, float eps, cudaStream_t s);
+int kb_kv(const float* kv, const __nv_bfloat16* wk, const float* acos_, const float* asin_, __nv_bfloat16* kout,
+          __nv_bfloat16* vout, int F, int AH, float eps, cudaStream_t s);
+int kb_attn(const __nv_bfloat16* mq, const __nv_bfloat16* wq, const float* acos_, const float* asin_,
+            const __nv_bfloat16* kh, const __nv_bfloat16* vh, const __nv_bfloat16* kc, const __nv_bfloat16* vc,
+            int first, __nv_bfloat16* out, int L, int S, int F, int AH, float eps, cudaStream_t s);
+int copy_bytes(void* dst, const void* src, size_t bytes, cudaStream_t s);
+
+}  // namespace fw

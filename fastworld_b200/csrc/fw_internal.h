@@ -1,0 +1,76 @@
+// Internal (C++) interfaces shared by the translation units of libfastworld_b200.
+#pragma once
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace fw {
+
+// ---------------------------------------------------------------- host utilities
+typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+// Resolves cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
+PFN_encodeTiled get_encode_fn();
+// 2-D row-major tensor [rows, cols] of `elem_bytes` elements with row stride `ld` elements;
+// box = [box_rows, box_cols]; 128-byte swizzle (box_cols * elem_bytes must be 128) or none.
+// Returns 0 or a negative FW_E* code.
+int make_tmap_2d(CUtensorMap* out, const void* base, int elem_bytes, int64_t rows, int64_t cols, int64_t ld,
+                 int box_rows, int box_cols, bool swizzle128);
+int num_sms();
+
+// ---------------------------------------------------------------- GEMM
+enum EpiMode : int {
+  EPI_BF16 = 0,        // out_bf16 = acc + bias                                   (split by column segment)
+  EPI_GELU_BF16 = 1,   // out_bf16 = gelu_tanh(acc + bias)
+  EPI_RESID_F32 = 2,   // resid_f32 += gate[frame] * (acc + bias); optional bf16 mirror of resid
+  EPI_F32 = 3,         // out_f32 = acc + bias
+  EPI_GELU_ERF_BF16 = 4,   // out_bf16 = gelu_erf(acc + bias)
+};
+
+struct GemmEpi {
+  int mode = EPI_BF16;
+  void* out[3] = {nullptr, nullptr, nullptr};   // destinations by column segment
+  int ld_out = 0;                               // elements
+  int seg_w = 0;                                // column segment width (multiple of the tile N)
+  const __nv_bfloat16* bias = nullptr;          // [N] bf16 (optional)
+  const float* fbias = nullptr;                 // [frames, fbias_stride] fp32 per-frame bias (optional)
+  int fbias_stride = 0;
+  const float* gate = nullptr;                  // [frames, gate_stride] fp32 (EPI_RESID_F32, optional)
+  int gate_stride = 0;
+  float* resid = nullptr;                       // [M, ld_resid] fp32
+  int ld_resid = 0;
+  __nv_bfloat16* mirror = nullptr;              // [M, ld_mirror] bf16 copy of the new residual (optional)
+  int ld_mirror = 0;
+  int rows_per_frame = 1 << 30;
+};
+
+struct GemmArgs {
+  int M = 0, N = 0, K = 0;
+  GemmEpi epi;
+  int* status = nullptr;
+};
+
+// C[M,N] = A[M,K] * B[N,K]^T.  tmA: box [128 rows, 64 cols]; tmB: box [bn rows, 64 cols];
+// bn in {64, 128, 256}.  `ctas` = 0 uses one CTA per SM (persistent).
+int gemm_bf16_launch(const CUtensorMap& tmA, const CUtensorMap& tmB, int bn, const GemmArgs& a, cudaStream_t s,
+                     int ctas = 0);
+int gemm_check(const GemmArgs& a, int bn);
+
+// ---------------------------------------------------------------- attention
+struct AttnArgs {
+  int Lq = 0;           // query rows
+  int heads = 0;        // heads (head_dim 128)
+  const int* meta = nullptr;   // device int32 {n_keys_seg0, n_keys_seg1}
+  int max_keys0 = 0, max_keys1 = 0;   // capacity of each segment (host-known bound)
+  __nv_bfloat16* out = nullptr;       // [Lq, heads*128]
+  int ld_out = 0;
+  float scale_log2 = 0.f;             // softmax scale * log2(e)
+  int* status = nullptr;
+};
+// Q [Lq, heads*128] (tmQ box [128, 64]); K/V segments [keys, heads*128] (box [128, 64]).
+int attention_launch(const CUtensorMap& tmQ, const CUtensorMap& tmK0, const CUtensorMap& tmV0,
+                     const CUtensorMap& tmK1, const CUtensorMap& tmV1, const AttnArgs& a, cudaStream_t s);
+
+}  // namespace fw

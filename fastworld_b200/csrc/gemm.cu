@@ -1,0 +1,301 @@
+// tcgen05 / TMEM GEMM for sm_100a:  C[M,N] = A[M,K] * B[N,K]^T  (bf16 in, fp32 accumulate).
+//
+// Replaces the cuBLAS Linear calls of the reference forward (fastworld/models/mg2/static.py:
+// 198, 208-210, 219, 189-192, 224 and the action-module Linears 150-185).
+//
+// Design (one CTA per SM, persistent over output tiles):
+//   warp 0      TMA producer: A tile [128 x 64] and B tile [BN x 64] per stage, 128-byte swizzle
+//   warp 1      MMA issuer: 4 x tcgen05.mma (K = 16 each) per stage into a TMEM accumulator;
+//               tcgen05.commit releases the smem stage and, per tile, signals the epilogue
+//   warps 2..5  epilogue: tcgen05.ld 32 columns at a time (thread = output row), fused bias /
+//               GELU / gated fp32 residual update, direct vector stores
+// The TMEM accumulator is double-buffered (2 x BN columns) so the epilogue of tile i overlaps
+// the main loop of tile i + 1.  Tile order is M-fastest so consecutive CTAs share a weight
+// tile in L2.  M, N and K tails are zero-filled by TMA and masked in the epilogue.
+#include "../../include/fastworld_b200.h"
+#include "fw_internal.h"
+#include "fw_ptx.cuh"
+
+namespace fw {
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int BM = 128, BK = 64;
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE = A_BYTES + B_BYTES;
+  static constexpr int STAGES = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int SMEM = STAGES * STAGE + 1024 + 256;
+};
+
+__device__ __forceinline__ void add_bias(const GemmEpi& e, int frame, int col0, float (&v)[32]) {
+  if (e.bias) {
+    const uint4* bp = reinterpret_cast<const uint4*>(e.bias + col0);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint4 u = __ldg(bp + j);
+      float2 f0 = unpack_bf16(u.x), f1 = unpack_bf16(u.y), f2 = unpack_bf16(u.z), f3 = unpack_bf16(u.w);
+      v[8 * j + 0] += f0.x; v[8 * j + 1] += f0.y; v[8 * j + 2] += f1.x; v[8 * j + 3] += f1.y;
+      v[8 * j + 4] += f2.x; v[8 * j + 5] += f2.y; v[8 * j + 6] += f3.x; v[8 * j + 7] += f3.y;
+    }
+  }
+  if (e.fbias) {
+    const float4* fp = reinterpret_cast<const float4*>(e.fbias + (size_t)frame * e.fbias_stride + col0);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float4 b = __ldg(fp + j);
+      v[4 * j + 0] += b.x; v[4 * j + 1] += b.y; v[4 * j + 2] += b.z; v[4 * j + 3] += b.w;
+    }
+  }
+}
+
+__device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float (&v)[32]) {
+  uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    d4[j] = make_uint4(pack_bf16(v[8 * j + 0], v[8 * j + 1]), pack_bf16(v[8 * j + 2], v[8 * j + 3]),
+                       pack_bf16(v[8 * j + 4], v[8 * j + 5]), pack_bf16(v[8 * j + 6], v[8 * j + 7]));
+}
+
+__device__ __forceinline__ void epilogue_chunk(const GemmEpi& e, int row, int col0, const uint32_t (&r)[32]) {
+  float v[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+  const int frame = row / e.rows_per_frame;
+  add_bias(e, frame, col0, v);
+  if (e.mode == EPI_BF16 || e.mode == EPI_GELU_BF16 || e.mode == EPI_GELU_ERF_BF16) {
+    if (e.mode == EPI_GELU_BF16) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
+    } else if (e.mode == EPI_GELU_ERF_BF16) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = 0.5f * v[j] * (1.f + erff(v[j] * 0.7071067811865476f));
+    }
+    const int seg = col0 / e.seg_w;
+    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(e.out[seg]) + (size_t)row * e.ld_out + (col0 - seg * e.seg_w);
+    store_bf16x32(dst, v);
+  } else if (e.mode == EPI_F32) {
+    float4* d4 = reinterpret_cast<float4*>(reinterpret_cast<float*>(e.out[0]) + (size_t)row * e.ld_out + col0);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) d4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+  } else {   // EPI_RESID_F32
+    float4* rp = reinterpret_cast<float4*>(e.resid + (size_t)row * e.ld_resid + col0);
+    const float4* gp = e.gate ? reinterpret_cast<const float4*>(e.gate + (size_t)frame * e.gate_stride + col0) : nullptr;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float4 x = rp[j];
+      float4 g = gp ? __ldg(gp + j) : make_float4(1.f, 1.f, 1.f, 1.f);
+      x.x += g.x * v[4 * j + 0]; x.y += g.y * v[4 * j + 1]; x.z += g.z * v[4 * j + 2]; x.w += g.w * v[4 * j + 3];
+      rp[j] = x;
+      v[4 * j + 0] = x.x; v[4 * j + 1] = x.y; v[4 * j + 2] = x.z; v[4 * j + 3] = x.w;
+    }
+    if (e.mirror) store_bf16x32(e.mirror + (size_t)row * e.ld_mirror + col0, v);
+  }
+}
+
+template <int BN>
+__global__ void __launch_bounds__(192, 1)
+    gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const GemmArgs args) {
+  using C = GemmCfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
+  uint8_t* smem = smem_raw + pad;
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + C::STAGES * C::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE);
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* tfull = empty + C::STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int M = args.M, N = args.N, K = args.K;
+  const int num_m = (M + 127) / 128, num_n = (N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n, num_kb = (K + 63) / 64;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull + a, 1);
+      mbar_init(tempty + a, 128);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch(&tmA);
+    tma_prefetch(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0, used = 0, last_par = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        const int mb = t % num_m, nb = t / num_m;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(empty + stage, phase ^ 1u, abort_flag, args.status, DEV_TIMEOUT_PRODUCER)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(full + stage, C::STAGE);
+          tma_load_2d(sA + stage * C::A_BYTES, &tmA, full + stage, kb * 64, mb * 128);
+          tma_load_2d(sB + stage * C::B_BYTES, &tmB, full + stage, kb * 64, nb * BN);
+          used |= 1u << stage;
+          last_par = (last_par & ~(1u << stage)) | (phase << stage);
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // wait (bounded) for every load this thread issued to land before the CTA exits
+      volatile int no_abort = 0;
+      for (int s = 0; s < C::STAGES; ++s)
+        if (used >> s & 1u) mbar_wait(full + s, last_par >> s & 1u, &no_abort, args.status, DEV_TIMEOUT_DRAIN);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16(128, BN, false, false);
+      int stage = 0, acc = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        if (!mbar_wait(tempty + acc, acc_phase ^ 1u, abort_flag, args.status, DEV_TIMEOUT_MMA)) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(full + stage, phase, abort_flag, args.status, DEV_TIMEOUT_MMA)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + stage * C::A_BYTES), b0 = smem_u32(sB + stage * C::B_BYTES);
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            umma_bf16(d, sdesc_sw128(a0 + k * 32, 16, 1024), sdesc_sw128(b0 + k * 32, 16, 1024), idesc,
+                      (kb | k) != 0);
+          umma_commit(empty + stage);
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(tfull + acc);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+      // all MMAs issued by this thread must complete before TMEM is released
+      umma_commit(drain);
+      volatile int no_abort = 0;
+      mbar_wait(drain, 0, &no_abort, args.status, DEV_TIMEOUT_DRAIN);
+    }
+  } else {
+    const int q = warp & 3;   // TMEM lane quarter this warp may access
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+      const int mb = t % num_m, nb = t / num_m;
+      const bool ok = mbar_wait(tfull + acc, acc_phase, abort_flag, args.status, DEV_TIMEOUT_EPILOGUE);
+      if (!__all_sync(0xffffffffu, ok)) break;   // keep the warp converged for tcgen05.ld
+      tc_fence_after();
+      const int row = mb * 128 + q * 32 + lane;
+      const uint32_t tb = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        const int col0 = nb * BN + c * 32;
+        if (col0 >= N) break;
+        uint32_t r[32];
+        tmem_ld32(tb + (uint32_t)(c * 32), r);
+        tmem_ld_wait();
+        if (row < M) epilogue_chunk(args.epi, row, col0, r);
+      }
+      tc_fence_before();
+      mbar_arrive(tempty + acc);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+int gemm_check(const GemmArgs& a, int bn) {
+  const GemmEpi& e = a.epi;
+  if (a.M <= 0 || a.N <= 0 || a.K <= 0) return FW_EINVAL;
+  if (bn != 64 && bn != 128 && bn != 256) return FW_EINVAL;
+  if (a.N % 32 || a.K % 8) return FW_ESHAPE;
+  auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  if (e.bias && !al16(e.bias)) return FW_EALIGN;
+  if (e.fbias && (!al16(e.fbias) || e.fbias_stride % 4)) return FW_EALIGN;
+  if (e.rows_per_frame <= 0) return FW_EINVAL;
+  switch (e.mode) {
+    case EPI_BF16:
+    case EPI_GELU_BF16:
+    case EPI_GELU_ERF_BF16: {
+      if (e.seg_w <= 0 || e.seg_w % bn || e.ld_out % 8) return FW_ESHAPE;
+      const int nseg = (a.N + e.seg_w - 1) / e.seg_w;
+      if (nseg > 3) return FW_ESHAPE;
+      for (int i = 0; i < nseg; ++i)
+        if (!e.out[i] || !al16(e.out[i])) return FW_EALIGN;
+      break;
+    }
+    case EPI_F32:
+      if (!e.out[0] || !al16(e.out[0]) || e.ld_out % 4) return FW_EALIGN;
+      break;
+    case EPI_RESID_F32:
+      if (!e.resid || !al16(e.resid) || e.ld_resid % 4) return FW_EALIGN;
+      if (e.gate && (!al16(e.gate) || e.gate_stride % 4)) return FW_EALIGN;
+      if (e.mirror && (!al16(e.mirror) || e.ld_mirror % 8)) return FW_EALIGN;
+      break;
+    default:
+      return FW_EINVAL;
+  }
+  return 0;
+}
+
+template <int BN>
+static int launch_bn(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmArgs& a, cudaStream_t s, int grid) {
+  using C = GemmCfg<BN>;
+  cudaError_t err = cudaFuncSetAttribute(gemm_bf16_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+  if (err != cudaSuccess) return FW_ECUDA;
+  gemm_bf16_kernel<BN><<<grid, 192, C::SMEM, s>>>(tmA, tmB, a);
+  return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
+}
+
+int gemm_bf16_launch(const CUtensorMap& tmA, const CUtensorMap& tmB, int bn, const GemmArgs& a, cudaStream_t s,
+                     int ctas) {
+  int rc = gemm_check(a, bn);
+  if (rc) return rc;
+  const int tiles = ((a.M + 127) / 128) * ((a.N + bn - 1) / bn);
+  int grid = ctas > 0 ? ctas : num_sms();
+  if (grid > tiles) grid = tiles;
+  switch (bn) {
+    case 256: return launch_bn<256>(tmA, tmB, a, s, grid);
+    case 128: return launch_bn<128>(tmA, tmB, a, s, grid);
+    default: return launch_bn<64>(tmA, tmB, a, s, grid);
+  }
+}
+
+}  // namespace fw

@@ -1,0 +1,126 @@
+// Host utilities (TMA descriptors, device queries) and the op-level C ABI entry points.
+#include <cmath>
+
+#include "../../include/fastworld_b200.h"
+#include "fw_internal.h"
+
+namespace fw {
+
+PFN_encodeTiled get_encode_fn() {
+  static PFN_encodeTiled fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_encodeTiled>(p);
+  }
+  return fn;
+}
+
+int num_sms() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) return 148;
+  return n;
+}
+
+int make_tmap_2d(CUtensorMap* out, const void* base, int elem_bytes, int64_t rows, int64_t cols, int64_t ld,
+                 int box_rows, int box_cols, bool swizzle128) {
+  PFN_encodeTiled enc = get_encode_fn();
+  if (!enc) return FW_ENODRIVER;
+  if (!base || rows <= 0 || cols <= 0 || box_rows <= 0 || box_rows > 256 || box_cols <= 0) return FW_EINVAL;
+  if (reinterpret_cast<uintptr_t>(base) & 15u) return FW_EALIGN;
+  if ((ld * elem_bytes) % 16) return FW_EALIGN;
+  if (swizzle128 && box_cols * elem_bytes != 128) return FW_EINVAL;
+  CUtensorMapDataType dt = elem_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                           : elem_bytes == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                             : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * elem_bytes)};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(out, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : FW_EINVAL;
+}
+
+}  // namespace fw
+
+extern "C" {
+
+int fw_gemm_bf16(const void* A, const void* B, const void* bias, void* out, int M, int N, int K, int epilogue,
+                 int tile_n, void* stream) {
+  using namespace fw;
+  if (!A || !B || !out) return FW_EINVAL;
+  if (epilogue != EPI_BF16 && epilogue != EPI_GELU_BF16 && epilogue != EPI_F32 && epilogue != EPI_GELU_ERF_BF16)
+    return FW_EINVAL;
+  const int bn = tile_n > 0 ? tile_n : (N >= 256 ? 256 : (N >= 128 ? 128 : 64));
+  if (bn != 64 && bn != 128 && bn != 256) return FW_EINVAL;
+  CUtensorMap ta, tb;
+  int rc = make_tmap_2d(&ta, A, 2, M, K, K, 128, 64, true);
+  if (!rc) rc = make_tmap_2d(&tb, B, 2, N, K, K, bn, 64, true);
+  if (rc) return rc;
+  GemmArgs a;
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.epi.mode = epilogue;
+  a.epi.out[0] = out;
+  a.epi.ld_out = N;
+  a.epi.seg_w = 1 << 30;
+  a.epi.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
+  return gemm_bf16_launch(ta, tb, bn, a, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int fw_gemm_bf16_resid(const void* A, const void* B, const void* bias, float* resid, const float* gate,
+                       int rows_per_frame, int M, int N, int K, void* stream) {
+  using namespace fw;
+  if (!A || !B || !resid || rows_per_frame <= 0) return FW_EINVAL;
+  const int bn = N >= 256 ? 256 : (N >= 128 ? 128 : 64);
+  CUtensorMap ta, tb;
+  int rc = make_tmap_2d(&ta, A, 2, M, K, K, 128, 64, true);
+  if (!rc) rc = make_tmap_2d(&tb, B, 2, N, K, K, bn, 64, true);
+  if (rc) return rc;
+  GemmArgs a;
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.epi.mode = EPI_RESID_F32;
+  a.epi.resid = resid;
+  a.epi.ld_resid = N;
+  a.epi.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
+  a.epi.gate = gate;
+  a.epi.gate_stride = N;
+  a.epi.rows_per_frame = rows_per_frame;
+  return gemm_bf16_launch(ta, tb, bn, a, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int fw_attention(const void* q, int Lq, int heads, const void* k0, const void* v0, int max_keys0, const void* k1,
+                 const void* v1, int max_keys1, const int* meta, void* out, int* status, void* stream) {
+  using namespace fw;
+  if (!q || !k0 || !v0 || !k1 || !v1 || !meta || !out || Lq <= 0 || heads <= 0 || max_keys0 <= 0 || max_keys1 <= 0)
+    return FW_EINVAL;
+  const int cols = heads * 128;
+  CUtensorMap tq, tk0, tv0, tk1, tv1;
+  int rc = make_tmap_2d(&tq, q, 2, Lq, cols, cols, 128, 64, true);
+  if (!rc) rc = make_tmap_2d(&tk0, k0, 2, max_keys0, cols, cols, 128, 64, true);
+  if (!rc) rc = make_tmap_2d(&tv0, v0, 2, max_keys0, cols, cols, 128, 64, true);
+  if (!rc) rc = make_tmap_2d(&tk1, k1, 2, max_keys1, cols, cols, 128, 64, true);
+  if (!rc) rc = make_tmap_2d(&tv1, v1, 2, max_keys1, cols, cols, 128, 64, true);
+  if (rc) return rc;
+  AttnArgs a;
+  a.Lq = Lq;
+  a.heads = heads;
+  a.meta = meta;
+  a.max_keys0 = max_keys0;
+  a.max_keys1 = max_keys1;
+  a.out = reinterpret_cast<__nv_bfloat16*>(out);
+  a.ld_out = cols;
+  a.scale_log2 = (float)(1.4426950408889634 / std::sqrt(128.0));
+  a.status = status;
+  return attention_launch(tq, tk0, tv0, tk1, tv1, a, reinterpret_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

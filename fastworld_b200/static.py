@@ -1,0 +1,227 @@
+"""``B200StaticMG``: the reference's ``StaticMG`` session object on the sm_100a engine.
+
+Drop-in for ``fastworld/models/mg2/static.py:27-284``: the same public methods
+(``capture``, ``gen_chunk``, ``prefill``, ``state``, ``load``, ``state_bytes``, ``_prep``,
+``_chunk``, ``_prefill``, ``_state_tensors``) and the same static-buffer discipline: torch
+allocates every buffer once, ``_prep`` fills the static inputs, and one launch call (or one
+CUDA-graph replay) runs the whole chunk.  The chunk itself is the C ABI's ``fw_chunk``:
+tcgen05 GEMMs, tcgen05 flash attention and fused elementwise kernels, no torch compute.
+
+Differences from the reference, by design:
+* constructed from a :class:`~fastworld_b200.config.DiTConfig` and a state dict (the
+  official ``Model`` is not needed); images are registered with :meth:`add_image`;
+* the session state lives in one contiguous device buffer (``state()`` returns a
+  :class:`SessionState`, a list of views into one snapshot buffer), so save / restore is a
+  single vectorised copy kernel;
+* the history attention reads device-resident segment lengths, so the "first" and "steady"
+  graphs differ only in which constant length table they point at.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Dict, List, Optional, Sequence
+
+import torch
+
+from . import _lib, graph as fw_graph
+from ._lib import check, lib, ptr, stream_ptr
+from .config import MG2, DiTConfig
+from .prep import action_windows, path_seed, synthetic_image
+
+_DT = {_lib.DT_BF16: torch.bfloat16, _lib.DT_F32: torch.float32, _lib.DT_I32: torch.int32, _lib.DT_U8: torch.uint8}
+
+
+def pack_weights(cfg: DiTConfig, sd: Dict[str, torch.Tensor]) -> Dict[str, torch.Tensor]:
+    """Map the flat state dict (``fastworld_b200.weights``) to the engine's tensor names:
+    q/k/v and cross k/v are packed row-wise so each is one GEMM, block modulations are
+    stacked into one [layers, 6, dim] table."""
+    out: Dict[str, torch.Tensor] = {}
+    for k, v in sd.items():
+        if ".sa.q." in k or ".sa.k." in k or ".sa.v." in k or ".ca.k." in k or ".ca.v." in k or k.endswith(".mod") \
+                and k.startswith("b"):
+            continue
+        out[k] = v
+    out["mods"] = torch.stack([sd[f"b{i}.mod"] for i in range(cfg.layers)], 0)
+    for i in range(cfg.layers):
+        p = f"b{i}"
+        for s in ("w", "b"):
+            out[f"{p}.sa.qkv.{s}"] = torch.cat([sd[f"{p}.sa.q.{s}"], sd[f"{p}.sa.k.{s}"], sd[f"{p}.sa.v.{s}"]], 0)
+            out[f"{p}.ca.kv.{s}"] = torch.cat([sd[f"{p}.ca.k.{s}"], sd[f"{p}.ca.v.{s}"]], 0)
+    return out
+
+
+class SessionState(list):
+    """Snapshot of a session's state: views (one per state tensor, reference order) into one
+    contiguous device buffer ``blob``."""
+
+    def __init__(self, blob: torch.Tensor, views: List[torch.Tensor]):
+        super().__init__(views)
+        self.blob = blob
+
+
+class B200StaticMG:
+    def __init__(self, cfg: DiTConfig = MG2, weights: Optional[Dict[str, torch.Tensor]] = None, device="cuda",
+                 seed: int = 0):
+        cfg.validate()
+        self.cfg = cfg
+        self.dev = torch.device(device)
+        if self.dev.type != "cuda":
+            raise RuntimeError("B200StaticMG runs on a CUDA device (sm_100a) only")
+        if weights is None:
+            from .weights import synthetic_state_dict
+            weights = synthetic_state_dict(cfg, seed, device=self.dev)
+        packed = pack_weights(cfg, weights)
+        self._ccfg = _lib.make_config(cfg)
+        h = ctypes.c_void_p()
+        check(lib().fw_create(ctypes.byref(self._ccfg), ctypes.byref(h)), "fw_create")
+        self._h = h
+        self.buffers: Dict[str, torch.Tensor] = {}
+        infos = []
+        for i in range(lib().fw_tensor_count(h)):
+            info = _lib.FwTensorInfo()
+            check(lib().fw_tensor_info_at(h, i, ctypes.byref(info)), "fw_tensor_info_at")
+            shape = tuple(info.shape[j] for j in range(info.ndim))
+            infos.append((info.name.decode(), info.kind, _DT[info.dtype], shape, info.bytes))
+        # session state: one contiguous blob, views in the reference order (static.py:280-281)
+        st = [x for x in infos if x[1] == _lib.KIND_STATE]
+        total = sum((b + 255) // 256 * 256 for *_, b in st)
+        self._blob = torch.zeros(total, dtype=torch.uint8, device=self.dev)
+        off, self._state_names = 0, []
+        for name, _, dt, shape, nb in st:
+            self.buffers[name] = self._blob[off:off + nb].view(dt).view(shape)
+            self._state_names.append(name)
+            off += (nb + 255) // 256 * 256
+        for name, kind, dt, shape, nb in infos:
+            if kind == _lib.KIND_STATE:
+                continue
+            if kind == _lib.KIND_WEIGHT:
+                w = packed[name]
+                if tuple(w.shape) != shape:
+                    raise ValueError(f"weight {name}: shape {tuple(w.shape)} != {shape}")
+                t = w.to(self.dev, torch.bfloat16).contiguous()
+            else:
+                t = torch.zeros(shape, dtype=dt, device=self.dev)
+            self.buffers[name] = t
+        for name, t in self.buffers.items():
+            check(lib().fw_bind(h, name.encode(), ptr(t), t.numel() * t.element_size()), f"fw_bind({name})")
+        check(lib().fw_finalize(h), "fw_finalize")
+        torch.cuda.synchronize(self.dev)
+        B = self.buffers
+        self.hk = [B[f"hk.{i}"] for i in range(cfg.layers)]
+        self.hv = [B[f"hv.{i}"] for i in range(cfg.layers)]
+        self.mk = {i: B[f"mk.{i}"] for i in cfg.action_blocks}
+        self.mv = {i: B[f"mv.{i}"] for i in cfg.action_blocks}
+        self.kk = {i: B[f"kk.{i}"] for i in cfg.action_blocks}
+        self.kv = {i: B[f"kv.{i}"] for i in cfg.action_blocks}
+        self.x_in, self.cc, self.vis, self.gm, self.kc = B["x_in"], B["cc"], B["vis"], B["gm"], B["kc"]
+        self.noise = [B[f"noise.{i}"] for i in range(len(cfg.steps) - 1)]
+        self.lat_in, self.out, self.chunk_info, self.status = B["lat_in"], B["out"], B["chunk"], B["status"]
+        self.steps = [int(t) for t in cfg.steps]
+        self.images: Dict[str, Dict[str, torch.Tensor]] = {}
+        self.graphs, self.cur_img = {}, None
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h is not None and h.value:
+            lib().fw_destroy(h)
+            self._h = None
+
+    # ------------------------------------------------------------------ images
+    def add_image(self, name: str, image: Optional[Dict[str, torch.Tensor]] = None, seed: int = 0,
+                  max_chunks: int = 24) -> None:
+        """Register a start image: ``cond_concat`` [1, 20, frames * max_chunks, H, W] and
+        ``visual_context`` [1, 257, ctx_dim] (``Model.add_image``, model.py:53-68); a seeded
+        synthetic image when ``image`` is None."""
+        img = image if image is not None else synthetic_image(self.cfg, seed, max_chunks)
+        self.images[name] = {k: v.to(self.dev, torch.bfloat16) for k, v in img.items()}
+
+    # ------------------------------------------------------------------ inputs
+    def _prep(self, path: Sequence, k: int, noise: bool = True) -> None:
+        """Fill the static inputs for chunk k of `path` (static.py:76-127)."""
+        c = self.cfg
+        img_name = path[0][0]
+        img = self.images[img_name]
+        if self.cur_img != img_name:
+            self.vis.copy_(img["visual_context"])
+            self.cur_img = img_name
+        s = c.frames * k
+        self.cc.copy_(img["cond_concat"][:, :, s:s + c.frames])
+        kc, gm = action_windows(c, path, k)
+        self.kc.copy_(kc[None], non_blocking=True)
+        self.gm.copy_(gm[None], non_blocking=True)
+        self.chunk_info.copy_(torch.tensor([k, s, 0, 0], dtype=torch.int32), non_blocking=True)
+        if not noise:
+            return
+        g = torch.Generator(device=self.dev).manual_seed(path_seed(path[:k + 1]))
+        self.x_in.copy_(torch.randn(self.x_in.shape, generator=g, device=self.dev, dtype=torch.bfloat16))
+        for nb in self.noise:
+            nb.copy_(torch.randn(nb.shape, generator=g, device=self.dev, dtype=torch.bfloat16))
+
+    # ------------------------------------------------------------------ network
+    def _chunk(self, first: bool) -> None:
+        check(lib().fw_chunk(self._h, int(bool(first)), stream_ptr()), "fw_chunk")
+
+    def _prefill(self, first: bool) -> None:
+        check(lib().fw_prefill(self._h, int(bool(first)), stream_ptr()), "fw_prefill")
+
+    def _net_step(self, step: int, first: bool, write: bool) -> None:
+        """One forward from ``x_in`` (``lat_in`` for the context step) into ``out``."""
+        check(lib().fw_forward(self._h, step, int(bool(first)), int(bool(write)), stream_ptr()), "fw_forward")
+
+    # ------------------------------------------------------------------ public
+    def capture(self, warmup: int = 2) -> None:
+        """Record the four graphs (first | steady) x (generate | prefill) (static.py:248-252)."""
+        fns = {(True, "gen"): lambda: self._chunk(True), (False, "gen"): lambda: self._chunk(False),
+               (True, "pre"): lambda: self._prefill(True), (False, "pre"): lambda: self._prefill(False)}
+        self.graphs = fw_graph.capture(fns, warmup=warmup, save=self.state, load=self.load)
+
+    @torch.no_grad()
+    def gen_chunk(self, path, k: int, graph: bool = True) -> torch.Tensor:
+        self._prep(path, k)
+        if graph:
+            self.graphs[(k == 0, "gen")].replay()
+        else:
+            self._chunk(k == 0)
+        return self.out.clone()
+
+    @torch.no_grad()
+    def prefill(self, lat: torch.Tensor, path, k: int, graph: bool = True) -> None:
+        """Advance the state by chunk k whose latent is already known (one context forward)."""
+        self._prep(path, k, noise=False)
+        self.lat_in.copy_(lat)
+        if graph:
+            self.graphs[(k == 0, "pre")].replay()
+        else:
+            self._prefill(k == 0)
+
+    def state(self) -> SessionState:
+        """Snapshot of the history buffers: one copy kernel into a new device buffer."""
+        blob = torch.empty_like(self._blob)
+        check(lib().fw_copy(ptr(blob), ptr(self._blob), self._blob.numel(), stream_ptr()), "fw_copy")
+        views, off = [], 0
+        for name in self._state_names:
+            t = self.buffers[name]
+            nb = t.numel() * t.element_size()
+            views.append(blob[off:off + nb].view(t.dtype).view(t.shape))
+            off += (nb + 255) // 256 * 256
+        return SessionState(blob, views)
+
+    def load(self, st) -> None:
+        """Restore a snapshot into the live buffers (pointers baked into graphs stay valid)."""
+        if isinstance(st, SessionState) and st.blob.numel() == self._blob.numel():
+            check(lib().fw_copy(ptr(self._blob), ptr(st.blob), self._blob.numel(), stream_ptr()), "fw_copy")
+            return
+        for d, s in zip(self._state_tensors(), st):
+            s = s.to(d.device).contiguous()
+            check(lib().fw_copy(ptr(d), ptr(s), d.numel() * d.element_size(), stream_ptr()), "fw_copy")
+
+    def _state_tensors(self) -> List[torch.Tensor]:
+        return self.hk + self.hv + list(self.mk.values()) + list(self.mv.values()) + list(self.kk.values()) + \
+            list(self.kv.values())
+
+    def state_bytes(self) -> int:
+        return fw_graph.state_bytes(self._state_tensors())
+
+    def device_status(self) -> List[int]:
+        """Device status words (0 = ok; otherwise a bounded wait gave up).  Synchronises."""
+        return [int(v) for v in self.status.cpu()]

@@ -1,0 +1,132 @@
+/* fastworld_b200: C ABI of the B200 (sm_100a) chunk-forward engine for the Matrix-Game-2-shaped
+ * causal Wan DiT.
+ *
+ * The engine replaces the device work behind the reference's session object
+ * (fastworld/models/mg2/static.py, class StaticMG) and keeps its calling convention: the
+ * caller allocates every buffer (weights, session state, static inputs, workspace), binds
+ * raw pointers once, and then launches whole chunks or single forwards on a stream.  The
+ * library owns no device memory, never allocates, never synchronises inside a launch call,
+ * and every launch is capturable into a CUDA graph (fastworld/graph.py:13-33).
+ *
+ * Return values: 0 on success, a negative FW_E* code on a host-side error.  Device-side
+ * errors (a bounded wait that ran out) are written to the bound "status" word (int32[4]),
+ * which the caller reads after synchronising.
+ *
+ * Reference interfaces replaced (file:line in StevenCYLu/fastworld):
+ *   fw_create / fw_tensor_* / fw_bind / fw_finalize  StaticMG.__init__        static.py:28-73
+ *   fw_chunk                                         StaticMG._chunk          static.py:232-242
+ *   fw_prefill                                       StaticMG._prefill        static.py:244-245
+ *   fw_forward                                       StaticMG._net            static.py:194-230
+ *   fw_copy                                          StaticMG.state / load    static.py:273-278
+ *   fw_gemm_bf16, fw_attention, fw_* ops             the torch / flash-attn calls inside _net
+ */
+#ifndef FASTWORLD_B200_H
+#define FASTWORLD_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FW_ABI_VERSION 1
+
+/* error codes */
+#define FW_OK 0
+#define FW_EINVAL (-1)      /* bad argument (null pointer, unknown name, bad enum) */
+#define FW_ESHAPE (-2)      /* unsupported or inconsistent shape */
+#define FW_EALIGN (-3)      /* pointer or stride alignment (16 bytes for TMA / vector access) */
+#define FW_ECUDA (-4)       /* a CUDA runtime call failed */
+#define FW_ENOTBOUND (-5)   /* fw_finalize: a required tensor was not bound */
+#define FW_ENODRIVER (-6)   /* cuTensorMapEncodeTiled unavailable */
+#define FW_ESTATE (-7)      /* call out of order (e.g. launch before fw_finalize) */
+#define FW_ESIZE (-8)       /* bound buffer smaller than required */
+
+/* tensor kinds (fw_tensor_info.kind) */
+#define FW_KIND_WEIGHT 0
+#define FW_KIND_STATE 1     /* session state: history K/V and action-module K/V */
+#define FW_KIND_INPUT 2     /* static per-chunk inputs written by the host before a launch */
+#define FW_KIND_OUTPUT 3
+#define FW_KIND_WORKSPACE 4
+#define FW_KIND_STATUS 5
+
+/* dtypes */
+#define FW_BF16 0
+#define FW_F32 1
+#define FW_I32 2
+#define FW_U8 3
+
+#define FW_MAX_ACTION_BLOCKS 64
+#define FW_MAX_STEPS 16
+
+/* Model + schedule.  Mirrors fastworld_b200.config.DiTConfig. */
+typedef struct fw_config {
+  int dim, heads, head_dim, ffn, layers, freq_dim;
+  int lat_ch, cond_ch, frames, lat_h, lat_w;          /* patch is fixed to (1, 2, 2) */
+  int ctx_tokens, ctx_dim;
+  int n_action, action_blocks[FW_MAX_ACTION_BLOCKS];
+  int act_heads, act_head_dim, mouse_hidden, keyboard_hidden, mouse_dim, keyboard_dim;
+  int time_ratio, window;
+  int n_steps;
+  float steps[FW_MAX_STEPS];                          /* denoising timesteps; context forward at t = 0 */
+  float eps;                                          /* block LayerNorm / RMSNorm eps */
+  float eps_ln;                                       /* img_emb / mouse_mlp LayerNorm eps */
+  float rope_theta;
+} fw_config;
+
+typedef struct fw_tensor_info {
+  const char* name;
+  int kind, dtype, ndim;
+  int64_t shape[5];
+  size_t bytes;
+} fw_tensor_info;
+
+typedef struct fw_handle fw_handle;
+
+int fw_abi_version(void);
+const char* fw_strerror(int code);
+
+/* ---- session engine (StaticMG, static.py:27-284) ---- */
+int fw_create(const fw_config* cfg, fw_handle** out);
+int fw_tensor_count(const fw_handle* h);
+int fw_tensor_info_at(const fw_handle* h, int index, fw_tensor_info* info);
+/* Bind a caller-owned device buffer of at least the reported size to a tensor name. */
+int fw_bind(fw_handle* h, const char* name, void* ptr, size_t bytes);
+/* Validate bindings, build TMA descriptors, upload constant tables (synchronous, once). */
+int fw_finalize(fw_handle* h);
+/* One chunk: n_steps denoising forwards with the flow-matching update between them, then
+ * the context forward at t = 0 that writes the history (static.py:232-242).  Reads the
+ * inputs x_in, noise.*, cc, vis, gm, kc, chunk; writes out and the state tensors.
+ * first != 0: chunk 0 (no history keys). */
+int fw_chunk(fw_handle* h, int first, void* stream);
+/* Context forward over the bound lat_in only (static.py:244-245). */
+int fw_prefill(fw_handle* h, int first, void* stream);
+/* One forward (static.py:194-230) at timestep index `step` (n_steps = the context forward
+ * at t = 0) from latent x_cur into den; write != 0 updates the history. */
+int fw_forward(fw_handle* h, int step, int first, int write, void* stream);
+void fw_destroy(fw_handle* h);
+
+/* ---- checkpoint copies (state save / restore / migrate; static.py:273-278) ----
+ * Vectorised device copy of `bytes` (16-byte aligned pointers; any size).  `src` may be a
+ * peer GPU's memory when peer access is enabled. */
+int fw_copy(void* dst, const void* src, size_t bytes, void* stream);
+
+/* ---- individual kernels (used by the engine; exported for tests and reuse) ---- */
+/* C[M,N] = A[M,K] B[N,K]^T (+ bias[N]) with A, B, C bf16 row-major, fp32 accumulate.
+ * epilogue: 0 = store bf16, 1 = GELU(tanh) then bf16, 3 = store fp32 (out is float*). */
+int fw_gemm_bf16(const void* A, const void* B, const void* bias, void* out, int M, int N, int K, int epilogue,
+                 int tile_n, void* stream);
+/* resid[M,N] (fp32) += gate[row / rows_per_frame, N] * (A B^T + bias); gate may be NULL. */
+int fw_gemm_bf16_resid(const void* A, const void* B, const void* bias, float* resid, const float* gate,
+                       int rows_per_frame, int M, int N, int K, void* stream);
+/* Non-causal attention, head_dim 128: out[Lq, H*128] = softmax(q k^T / sqrt(128)) v over the
+ * keys of segment 0 then segment 1.  meta = device int32 {n_keys0, n_keys1}.  max_keys0/1
+ * are the row capacities of the segment buffers. */
+int fw_attention(const void* q, int Lq, int heads, const void* k0, const void* v0, int max_keys0, const void* k1,
+                 const void* v1, int max_keys1, const int* meta, void* out, int* status, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* FASTWORLD_B200_H */

@@ -1,0 +1,79 @@
+"""PrefixCache semantics (fastworld/prefix_cache.py:47-92) with a deterministic fake runtime:
+sharing, checkpoint restore and replay must reproduce generating every request from scratch."""
+import hashlib
+
+import torch
+
+from fastworld_b200.prefix_cache import PrefixCache
+
+
+class FakeRuntime:
+    """State = running hash of the chunks advanced; a chunk's latent depends on the state and key."""
+
+    def __init__(self):
+        self.h = b""
+        self.calls = {"gen": 0, "prefill": 0, "load": 0}
+
+    def _adv(self, key):
+        self.h = hashlib.sha1(self.h + repr(key).encode()).digest()
+
+    def gen_chunk(self, path, k):
+        self.calls["gen"] += 1
+        self._adv(path[k])
+        return torch.tensor(list(self.h[:8]), dtype=torch.float32)
+
+    def prefill(self, lat, path, k):
+        self.calls["prefill"] += 1
+        self._adv(path[k])
+
+    def state(self):
+        return self.h
+
+    def load(self, st):
+        self.calls["load"] += 1
+        self.h = st
+
+    def reset(self):
+        self.h = b""
+
+
+class FakeDecoder:
+    def __init__(self):
+        self.n = 0
+
+    def decode(self, lat):
+        return (lat / 255.0)[None, None, None, :].expand(1, 3, 1, 8) * 2 - 1
+
+    def reset(self):
+        pass
+
+    def state(self):
+        return None
+
+    def load(self, st):
+        pass
+
+
+def test_sharing_matches_scratch():
+    paths = [[("img", a) for a in p] for p in (
+        "wwww", "wwss", "wwsa", "wadd", "wwww", "ww", "wwsaq")]
+    ref_rt = FakeRuntime()
+    scratch = PrefixCache(ref_rt, FakeDecoder(), every=None)
+    rt = FakeRuntime()
+    cache = PrefixCache(rt, FakeDecoder(), every=2)
+    for p in paths:
+        a, _ = scratch.serve(p)
+        b, st = cache.serve(p)
+        assert len(a) == len(b) == len(p)
+        assert all(torch.equal(x, y) for x, y in zip(a, b))
+    assert rt.calls["gen"] < ref_rt.calls["gen"]
+    assert rt.calls["load"] > 0 and cache.n_ckpt > 0
+
+
+def test_stats_of_a_rewind():
+    rt = FakeRuntime()
+    cache = PrefixCache(rt, FakeDecoder(), every=2)
+    main = [("img", c) for c in "wwwwwwww"]
+    cache.serve(main)
+    _, st = cache.serve(main[:5] + [("img", "a")] * 3)
+    assert st["hit"] == 5 and st["restored"] == 1 and st["replayed"] == 1 and st["generated"] == 3
