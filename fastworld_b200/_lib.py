@@ -41,6 +41,7 @@ class FwTensorInfo(ctypes.Structure):
 
 _SIGS = {
     "fw_abi_version": (ctypes.c_int, []),
+    "fw_launch_count": (ctypes.c_ulonglong, []),
     "fw_strerror": (ctypes.c_char_p, [ctypes.c_int]),
     "fw_create": (ctypes.c_int, [ctypes.POINTER(FwConfig), ctypes.POINTER(ctypes.c_void_p)]),
     "fw_tensor_count": (ctypes.c_int, [ctypes.c_void_p]),

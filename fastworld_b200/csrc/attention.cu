@@ -286,6 +286,7 @@ int attention_launch(const CUtensorMap& tmQ, const CUtensorMap& tmK0, const CUte
   if (err != cudaSuccess) return FW_ECUDA;
   dim3 grid((a.Lq + attn::BQ - 1) / attn::BQ, a.heads);
   attention_kernel<<<grid, 192, attn::SMEM, s>>>(tmQ, tmK0, tmV0, tmK1, tmV1, a);
+  note_launch();
   return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
 }
 

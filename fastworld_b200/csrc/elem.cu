@@ -106,7 +106,7 @@ static int ln_dispatch(const Tin* x, int ldx, int M, int D, float eps, const flo
   const dim3 grid((M + 7) / 8), block(256);
   switch (D / 128) {
 #define FW_LN_CASE(n) \
-  case n: ln_kernel<Tin, n><<<grid, block, 0, s>>>(x, ldx, M, eps, shift, scale, w, b, out, ldo); break;
+  case n: ln_kernel<Tin, n><<<grid, block, 0, s>>>(x, ldx, M, eps, shift, scale, w, b, out, ldo); note_launch(); break;
     FW_LN_CASE(1) FW_LN_CASE(2) FW_LN_CASE(3) FW_LN_CASE(4) FW_LN_CASE(5) FW_LN_CASE(6) FW_LN_CASE(7)
     FW_LN_CASE(8) FW_LN_CASE(9) FW_LN_CASE(10) FW_LN_CASE(11) FW_LN_CASE(12) FW_LN_CASE(16)
 #undef FW_LN_CASE
@@ -172,7 +172,7 @@ int rms_rope(const __nv_bfloat16* x, int ldx, int M, int D, float eps, const __n
   const dim3 grid((M + 7) / 8), block(256);
   switch (D / 128) {
 #define FW_RMS_CASE(n) \
-  case n: rms_rope_kernel<n><<<grid, block, 0, s>>>(x, ldx, M, eps, w, rope, hd, out, ldo); break;
+  case n: rms_rope_kernel<n><<<grid, block, 0, s>>>(x, ldx, M, eps, w, rope, hd, out, ldo); note_launch(); break;
     FW_RMS_CASE(1) FW_RMS_CASE(2) FW_RMS_CASE(3) FW_RMS_CASE(4) FW_RMS_CASE(6) FW_RMS_CASE(8)
     FW_RMS_CASE(10) FW_RMS_CASE(12) FW_RMS_CASE(16)
 #undef FW_RMS_CASE
@@ -220,6 +220,7 @@ int rope_tables(const int* chunk, int F, int th, int tw, int hd, double theta, f
   const int n = F * th * tw * (hd / 2);
   const int m = n > F * act_hd ? n : F * act_hd;
   rope_table_kernel<<<(m + 255) / 256, 256, 0, s>>>(chunk, F, th, tw, hd, theta, table, act_hd, act_cos, act_sin);
+  note_launch();
   return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
 }
 
@@ -256,6 +257,7 @@ __global__ void __launch_bounds__(256) smallm_linear_kernel(const Tx* __restrict
 int smallm_linear_f32(const float* x, int ldx, int M, const __nv_bfloat16* W, int ldw, const __nv_bfloat16* b, int N,
                       int K, int act_in, int act_out, float* outf, __nv_bfloat16* outb, int ldo, cudaStream_t s) {
   smallm_linear_kernel<float><<<(N + 7) / 8, 256, 0, s>>>(x, ldx, M, W, ldw, b, N, K, act_in, act_out, outf, outb, ldo);
+  note_launch();
   return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
 }
 int smallm_linear_bf16(const __nv_bfloat16* x, int ldx, int M, const __nv_bfloat16* W, int ldw,
@@ -280,6 +282,7 @@ __global__ void sinusoid_kernel(double t, int dim, float* out) {
 }
 int sinusoid(double t, int dim, float* out, cudaStream_t s) {
   sinusoid_kernel<<<(dim / 2 + 127) / 128, 128, 0, s>>>(t, dim, out);
+  note_launch();
   return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
 }
 
@@ -297,6 +300,7 @@ int modulation(const __nv_bfloat16* mods, const float* e0, int layers, int D, fl
                const float* e, float* head, cudaStream_t s) {
   const int n = layers * 6 * D > 2 * D ? layers * 6 * D : 2 * D;
   modulation_kernel<<<(n + 255) / 256, 256, 0, s>>>(mods, e0, layers, D, ee, hmod, e, head);
+  note_launch();
   return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
 }
 
@@ -318,6 +322,7 @@ int patchify(const __nv_bfloat16* x, int C1, const __nv_bfloat16* cc, int C2, in
              cudaStream_t s) {
   const int n = F * (H / 2) * (W / 2) * (C1 + C2) * 4;
   patchify_kernel<<<(n + 255) / 256, 256, 0, s>>>(x, C1, cc, C2, F, H, W, A);
+  note_launch();
   return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
 }
 
@@ -350,6 +355,7 @@ int scheduler(const float* head, const __nv_bfloat16* x, float sigma, __nv_bfloa
               cudaStream_t s) {
   const int n = C * F * H * W;
   scheduler_kernel<<<(n + 255) / 256, 256, 0, s>>>(head, x, sigma, den, out_copy, noise, sigma_n, xnext, C, F, H, W);
+  note_launch();
   return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
 }
 
@@ -430,6 +436,7 @@ int mouse_attn(const __nv_bfloat16* qkv, const __nv_bfloat16* wq, const __nv_bfl
                int S, int F, int AH, float eps, cudaStream_t s) {
   if (F != 3) return FW_ESHAPE;
   mouse_attn_kernel<3><<<(S * AH + 7) / 8, 256, 0, s>>>(qkv, wq, wk, acos_, asin_, mk, mv, first, write, out, S, AH, eps);
+  note_launch();
   return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
 }
 
@@ -450,6 +457,7 @@ __global__ void kb_kv_kernel(const float* __restrict__ kv, const __nv_bfloat16* 
 int kb_kv(const float* kv, const __nv_bfloat16* wk, const float* acos_, const float* asin_, __nv_bfloat16* kout,
           __nv_bfloat16* vout, int F, int AH, float eps, cudaStream_t s) {
   kb_kv_kernel<<<(F * AH + 3) / 4, 128, 0, s>>>(kv, wk, acos_, asin_, kout, vout, F, AH, eps);
+  note_launch();
   return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
 }
 
@@ -496,6 +504,7 @@ int kb_attn(const __nv_bfloat16* mq, const __nv_bfloat16* wq, const float* acos_
             int first, __nv_bfloat16* out, int L, int S, int F, int AH, float eps, cudaStream_t s) {
   if (F != 3) return FW_ESHAPE;
   kb_attn_kernel<3><<<(L * AH + 7) / 8, 256, 0, s>>>(mq, wq, acos_, asin_, kh, vh, kc, vc, first, out, L, S, AH, eps);
+  note_launch();
   return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
 }
 

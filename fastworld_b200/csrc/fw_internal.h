@@ -19,6 +19,8 @@ PFN_encodeTiled get_encode_fn();
 int make_tmap_2d(CUtensorMap* out, const void* base, int elem_bytes, int64_t rows, int64_t cols, int64_t ld,
                  int box_rows, int box_cols, bool swizzle128);
 int num_sms();
+// Counts kernel launches enqueued by this library (all threads); read with fw_launch_count().
+void note_launch();
 
 // ---------------------------------------------------------------- GEMM
 enum EpiMode : int {

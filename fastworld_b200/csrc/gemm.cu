@@ -281,6 +281,7 @@ static int launch_bn(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmA
   cudaError_t err = cudaFuncSetAttribute(gemm_bf16_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (err != cudaSuccess) return FW_ECUDA;
   gemm_bf16_kernel<BN><<<grid, 192, C::SMEM, s>>>(tmA, tmB, a);
+  note_launch();
   return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
 }
 

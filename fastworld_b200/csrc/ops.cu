@@ -1,4 +1,5 @@
 // Host utilities (TMA descriptors, device queries) and the op-level C ABI entry points.
+#include <atomic>
 #include <cmath>
 
 #include "../../include/fastworld_b200.h"
@@ -17,6 +18,9 @@ PFN_encodeTiled get_encode_fn() {
   }
   return fn;
 }
+
+static std::atomic<unsigned long long> g_launches{0};
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 int num_sms() {
   int dev = 0, n = 0;
@@ -49,6 +53,8 @@ int make_tmap_2d(CUtensorMap* out, const void* base, int elem_bytes, int64_t row
 }  // namespace fw
 
 extern "C" {
+
+unsigned long long fw_launch_count(void) { return fw::g_launches.load(std::memory_order_relaxed); }
 
 int fw_gemm_bf16(const void* A, const void* B, const void* bias, void* out, int M, int N, int K, int epilogue,
                  int tile_n, void* stream) {

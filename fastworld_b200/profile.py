@@ -1,0 +1,59 @@
+"""Small, self-terminating workloads for ncu captures (run them plain first, then under ncu).
+
+    python -m fastworld_b200.profile chunk [--chunks 2]   eager MG2 chunks (chunk 0, then steady)
+    python -m fastworld_b200.profile gemm  [--reps 3]     FFN-up GEMM, MG2 shape, GELU epilogue
+    python -m fastworld_b200.profile attn  [--reps 3]     steady self-attention, 12 heads, 2640 + 2640 keys
+"""
+from __future__ import annotations
+
+import argparse
+
+import torch
+
+
+def chunk(n: int) -> None:
+    from fastworld_b200 import _lib
+    from fastworld_b200.config import MG2
+    from fastworld_b200.static import B200StaticMG
+    S = B200StaticMG(MG2, seed=0)
+    S.add_image("img0", seed=3, max_chunks=n + 1)
+    path = [("img0", ("w", "u"))] * (n + 1)
+    for k in range(n):
+        S._prep(path, k)
+        c0 = _lib.lib().fw_launch_count()
+        S._chunk(k == 0)
+        torch.cuda.synchronize()
+        print(f"chunk {k}: {_lib.lib().fw_launch_count() - c0} launches, status {S.device_status()}")
+
+
+def gemm(reps: int) -> None:
+    from fastworld_b200 import ops
+    g = torch.Generator(device="cuda").manual_seed(0)
+    A = torch.randn(2640, 1536, device="cuda", generator=g).to(torch.bfloat16)
+    B = (torch.randn(8960, 1536, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    bias = torch.zeros(8960, device="cuda", dtype=torch.bfloat16)
+    for _ in range(reps):
+        ops.gemm(A, B, bias, "gelu_tanh")
+    torch.cuda.synchronize()
+    print("gemm ok")
+
+
+def attn(reps: int) -> None:
+    from fastworld_b200 import ops
+    g = torch.Generator(device="cuda").manual_seed(0)
+    r = lambda n: torch.randn(n, 12, 128, device="cuda", generator=g).to(torch.bfloat16)
+    q, k0, v0, k1, v1 = r(2640), r(2640), r(2640), r(2640), r(2640)
+    meta = torch.tensor([2640, 2640], dtype=torch.int32, device="cuda")
+    for _ in range(reps):
+        ops.attention(q, k0, v0, k1, v1, meta)
+    torch.cuda.synchronize()
+    print("attn ok")
+
+
+if __name__ == "__main__":
+    ap = argparse.ArgumentParser()
+    ap.add_argument("what", choices=["chunk", "gemm", "attn"])
+    ap.add_argument("--chunks", type=int, default=2)
+    ap.add_argument("--reps", type=int, default=3)
+    a = ap.parse_args()
+    {"chunk": lambda: chunk(a.chunks), "gemm": lambda: gemm(a.reps), "attn": lambda: attn(a.reps)}[a.what]()

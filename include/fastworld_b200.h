@@ -86,6 +86,8 @@ typedef struct fw_handle fw_handle;
 
 int fw_abi_version(void);
 const char* fw_strerror(int code);
+/* Number of kernels this library has enqueued so far (all threads; monotonic). */
+unsigned long long fw_launch_count(void);
 
 /* ---- session engine (StaticMG, static.py:27-284) ---- */
 int fw_create(const fw_config* cfg, fw_handle** out);
