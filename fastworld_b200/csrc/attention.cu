@@ -7,14 +7,18 @@
 // so one captured graph serves chunk 0 (no history) and steady chunks, with no host cu_seqlens
 // and no concatenation.
 //
-// One CTA per (128-query tile, head); 192 threads:
-//   warps 0-3  softmax: thread = query row.  Loads its S row from TMEM, online softmax in the
-//              exp2 domain, rescales its O row in TMEM when the running max grows, writes P
-//              (bf16) into a 128-byte-swizzled K-major smem tile, final O / l and store.
-//   warp 4     TMA producer: Q once; K and V blocks of 128 keys, double-buffered.
-//   warp 5     MMA issuer: S_j = Q K_j^T (SS, N = 128) into one of two TMEM S buffers, and
-//              O += P_{j-1} V_{j-1} (A = P from smem K-major, B = V from smem MN-major).
-// TMEM: S0 cols [0,128), S1 [128,256), O [256,384) of a 512-column allocation.
+// One CTA per (pair of 128-query tiles A and B, head); 320 threads:
+//   warps 0-3  softmax of tile A, warps 4-7 softmax of tile B: thread = query row (TMEM lane).
+//              Loads its S row from TMEM, online softmax in the exp2 domain with a lazy O
+//              rescale (only when the running max grows by more than 2^8), writes P (bf16)
+//              into its tile's 128-byte-swizzled K-major smem buffer, final O / l and store.
+//   warp 8     TMA producer: both Q tiles once; then K_0, V_0, K_1, V_1, ... through a ring of
+//              three 32 KB slots (K_{j+1} lands while V_j is still in use).
+//   warp 9     MMA issuer, ping-pong between the tiles so the tensor core works on one tile
+//              while the other tile's softmax runs:
+//                S_A(j+1) = Q_A K_{j+1}^T,  O_A += P_A(j) V_j,  S_B(j+1),  O_B += P_B(j) V_j.
+// TMEM (512 columns): S_A [0,128), O_A [128,256), S_B [256,384), O_B [384,512).
+// SMEM: Q_A, Q_B (2 x 32 KB), K/V ring (3 x 32 KB), P_A, P_B (2 x 32 KB) = 224 KB.
 #include "../../include/fastworld_b200.h"
 #include "fw_internal.h"
 #include "fw_ptx.cuh"
@@ -23,17 +27,19 @@ namespace fw {
 
 namespace attn {
 constexpr int BQ = 128, BKV = 128, HD = 128;
-constexpr int TILE = 128 * 64 * 2;          // one [128 rows x 64 cols] bf16 swizzled sub-tile
-constexpr int Q_OFF = 0;                    // 2 sub-tiles
-constexpr int K_OFF = Q_OFF + 2 * TILE;     // 2 stages x 2 sub-tiles
-constexpr int V_OFF = K_OFF + 4 * TILE;     // 2 stages x 2 sub-tiles
-constexpr int P_OFF = V_OFF + 4 * TILE;     // 2 sub-tiles
-constexpr int BAR_OFF = P_OFF + 2 * TILE;
+constexpr int THREADS = 320;
+constexpr int TILE = 128 * 64 * 2;          // one [128 rows x 64 cols] bf16 swizzled sub-tile (16 KB)
+constexpr int Q_OFF = 0;                    // tile t: 2 sub-tiles at Q_OFF + t * 2 * TILE
+constexpr int KV_OFF = Q_OFF + 4 * TILE;    // slot s: 2 sub-tiles at KV_OFF + s * 2 * TILE
+constexpr int P_OFF = KV_OFF + 6 * TILE;    // tile t: 2 sub-tiles at P_OFF + t * 2 * TILE
+constexpr int BAR_OFF = P_OFF + 4 * TILE;
 constexpr int SMEM = BAR_OFF + 256 + 1024;
-constexpr uint32_t TMEM_COLS = 512, S_COL = 0, O_COL = 256;
+constexpr uint32_t TMEM_COLS = 512;
+__host__ __device__ constexpr uint32_t s_col(int t) { return (uint32_t)(t * 256); }
+__host__ __device__ constexpr uint32_t o_col(int t) { return (uint32_t)(t * 256 + 128); }
 }  // namespace attn
 
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(attn::THREADS, 1)
     attention_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK0,
                      const __grid_constant__ CUtensorMap tmV0, const __grid_constant__ CUtensorMap tmK1,
                      const __grid_constant__ CUtensorMap tmV1, const AttnArgs args) {
@@ -43,19 +49,19 @@ __global__ void __launch_bounds__(192, 1)
   uint8_t* smem = smem_raw + pad;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + BAR_OFF);
   uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;      // [2]
-  uint64_t* v_full = bars + 3;      // [2]
-  uint64_t* kv_empty = bars + 5;    // [2]
-  uint64_t* s_full = bars + 7;      // [2]
+  uint64_t* kv_full = bars + 1;     // [3] ring slots
+  uint64_t* kv_free = bars + 4;     // [3]
+  uint64_t* s_full = bars + 7;      // [2] per tile
   uint64_t* s_free = bars + 9;      // [2]
-  uint64_t* p_full = bars + 11;
-  uint64_t* o_done = bars + 12;
-  uint64_t* drain = bars + 13;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+  uint64_t* p_full = bars + 11;     // [2]
+  uint64_t* o_done = bars + 13;     // [2]
+  uint64_t* drain = bars + 15;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int q0 = blockIdx.x * BQ, head = blockIdx.y;
+  const int q0 = blockIdx.x * 2 * BQ, head = blockIdx.y;
+  const int ntile = (q0 + BQ < args.Lq) ? 2 : 1;   // tile B exists only if it has query rows
   int n0 = __ldg(args.meta), n1 = __ldg(args.meta + 1);
   n0 = min(max(n0, 0), args.max_keys0);
   n1 = min(max(n1, 0), args.max_keys1);
@@ -63,20 +69,21 @@ __global__ void __launch_bounds__(192, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(k_full + s, 1);
-      mbar_init(v_full + s, 1);
-      mbar_init(kv_empty + s, 1);
-      mbar_init(s_full + s, 1);
-      mbar_init(s_free + s, 128);
+    for (int s = 0; s < 3; ++s) {
+      mbar_init(kv_full + s, 1);
+      mbar_init(kv_free + s, 1);
     }
-    mbar_init(p_full, 128);
-    mbar_init(o_done, 1);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(s_full + t, 1);
+      mbar_init(s_free + t, 128);
+      mbar_init(p_full + t, 128);
+      mbar_init(o_done + t, 1);
+    }
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 5) {
+  if (warp == 9) {
     tmem_alloc(tmem_slot, TMEM_COLS);
     tmem_relinquish();
   }
@@ -86,143 +93,151 @@ __global__ void __launch_bounds__(192, 1)
   const uint32_t tmem = *tmem_slot;
   const int col = head * HD;
 
-  if (warp == 4) {
+  if (warp == 8) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0 && nblk > 0) {
       uint32_t used = 0, last_par = 0;
-      mbar_arrive_expect_tx(q_full, 2 * TILE);
-      tma_load_2d(smem + Q_OFF, &tmQ, q_full, col, q0);
-      tma_load_2d(smem + Q_OFF + TILE, &tmQ, q_full, col + 64, q0);
-      for (int j = 0; j < nblk; ++j) {
-        const int s = j & 1;
-        const uint32_t par = (uint32_t)(j >> 1) & 1u;
-        if (!mbar_wait(kv_empty + s, par ^ 1u, abort_flag, args.status, DEV_TIMEOUT_PRODUCER)) break;
+      mbar_arrive_expect_tx(q_full, ntile * 2 * TILE);
+      for (int t = 0; t < ntile; ++t) {
+        tma_load_2d(smem + Q_OFF + t * 2 * TILE, &tmQ, q_full, col, q0 + t * BQ);
+        tma_load_2d(smem + Q_OFF + t * 2 * TILE + TILE, &tmQ, q_full, col + 64, q0 + t * BQ);
+      }
+      for (int i = 0; i < 2 * nblk; ++i) {   // load i: K_{i/2} (even) or V_{i/2} (odd)
+        const int s = i % 3;
+        const uint32_t par = (uint32_t)(i / 3) & 1u;
+        if (!mbar_wait(kv_free + s, par ^ 1u, abort_flag, args.status, DEV_TIMEOUT_PRODUCER)) break;
+        const int j = i >> 1;
         const bool seg0 = j < nb0;
-        const CUtensorMap* mk = seg0 ? &tmK0 : &tmK1;
-        const CUtensorMap* mv = seg0 ? &tmV0 : &tmV1;
+        const CUtensorMap* m = (i & 1) ? (seg0 ? &tmV0 : &tmV1) : (seg0 ? &tmK0 : &tmK1);
         const int key0 = (seg0 ? j : j - nb0) * BKV;
-        uint8_t* sk = smem + K_OFF + s * 2 * TILE;
-        uint8_t* sv = smem + V_OFF + s * 2 * TILE;
-        mbar_arrive_expect_tx(k_full + s, 2 * TILE);
-        tma_load_2d(sk, mk, k_full + s, col, key0);
-        tma_load_2d(sk + TILE, mk, k_full + s, col + 64, key0);
-        mbar_arrive_expect_tx(v_full + s, 2 * TILE);
-        tma_load_2d(sv, mv, v_full + s, col, key0);
-        tma_load_2d(sv + TILE, mv, v_full + s, col + 64, key0);
+        uint8_t* dst = smem + KV_OFF + s * 2 * TILE;
+        mbar_arrive_expect_tx(kv_full + s, 2 * TILE);
+        tma_load_2d(dst, m, kv_full + s, col, key0);
+        tma_load_2d(dst + TILE, m, kv_full + s, col + 64, key0);
         used |= 1u << s;
         last_par = (last_par & ~(1u << s)) | (par << s);
       }
       volatile int no_abort = 0;
       mbar_wait(q_full, 0, &no_abort, args.status, DEV_TIMEOUT_DRAIN);
-      for (int s = 0; s < 2; ++s)
-        if (used >> s & 1u) {
-          mbar_wait(k_full + s, last_par >> s & 1u, &no_abort, args.status, DEV_TIMEOUT_DRAIN);
-          mbar_wait(v_full + s, last_par >> s & 1u, &no_abort, args.status, DEV_TIMEOUT_DRAIN);
-        }
+      for (int s = 0; s < 3; ++s)
+        if (used >> s & 1u) mbar_wait(kv_full + s, last_par >> s & 1u, &no_abort, args.status, DEV_TIMEOUT_DRAIN);
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && nblk > 0) {
       constexpr uint32_t idesc_s = idesc_bf16(128, 128, false, false);   // Q K^T: both K-major
       constexpr uint32_t idesc_o = idesc_bf16(128, 128, false, true);    // P V: V is MN-major
-      const uint32_t sq = smem_u32(smem + Q_OFF), sp = smem_u32(smem + P_OFF);
       bool ok = mbar_wait(q_full, 0, abort_flag, args.status, DEV_TIMEOUT_MMA);
-      auto issue_s = [&](int j) -> bool {
-        const int s = j & 1;
-        const uint32_t par = (uint32_t)(j >> 1) & 1u;
-        if (!mbar_wait(k_full + s, par, abort_flag, args.status, DEV_TIMEOUT_MMA)) return false;
-        if (!mbar_wait(s_free + s, par ^ 1u, abort_flag, args.status, DEV_TIMEOUT_MMA)) return false;
+      // S_t(j) = Q_t K_j^T into the tile's S columns; needs K_j landed and S_t(j-1) read out
+      auto issue_s = [&](int t, int j) -> bool {
+        const int s = (2 * j) % 3;
+        if (!mbar_wait(kv_full + s, (uint32_t)((2 * j) / 3) & 1u, abort_flag, args.status, DEV_TIMEOUT_MMA))
+          return false;
+        if (!mbar_wait(s_free + t, ((uint32_t)j & 1u) ^ 1u, abort_flag, args.status, DEV_TIMEOUT_MMA)) return false;
         tc_fence_after();
-        const uint32_t sk = smem_u32(smem + K_OFF + s * 2 * TILE);
-        const uint32_t d = tmem + S_COL + (uint32_t)(s * 128);
+        const uint32_t sq = smem_u32(smem + Q_OFF + t * 2 * TILE);
+        const uint32_t sk = smem_u32(smem + KV_OFF + s * 2 * TILE);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t off = (uint32_t)((kk >> 2) * TILE + (kk & 3) * 32);
-          umma_bf16(d, sdesc_sw128(sq + off, 16, 1024), sdesc_sw128(sk + off, 16, 1024), idesc_s, kk != 0);
+          umma_bf16(tmem + s_col(t), sdesc_sw128(sq + off, 16, 1024), sdesc_sw128(sk + off, 16, 1024), idesc_s,
+                    kk != 0);
         }
-        umma_commit(s_full + s);
+        umma_commit(s_full + t);
+        if (t == ntile - 1) umma_commit(kv_free + s);   // K_j no longer needed once the last tile read it
         return true;
       };
-      auto issue_o = [&](int j) -> bool {
-        const int s = j & 1;
-        const uint32_t par = (uint32_t)(j >> 1) & 1u;
-        if (!mbar_wait(p_full, (uint32_t)j & 1u, abort_flag, args.status, DEV_TIMEOUT_MMA)) return false;
-        if (!mbar_wait(v_full + s, par, abort_flag, args.status, DEV_TIMEOUT_MMA)) return false;
+      // O_t += P_t(j) V_j; needs P_t(j) written and V_j landed
+      auto issue_o = [&](int t, int j) -> bool {
+        const int s = (2 * j + 1) % 3;
+        if (!mbar_wait(p_full + t, (uint32_t)j & 1u, abort_flag, args.status, DEV_TIMEOUT_MMA)) return false;
+        if (!mbar_wait(kv_full + s, (uint32_t)((2 * j + 1) / 3) & 1u, abort_flag, args.status, DEV_TIMEOUT_MMA))
+          return false;
         tc_fence_after();
-        const uint32_t sv = smem_u32(smem + V_OFF + s * 2 * TILE);
+        const uint32_t sp = smem_u32(smem + P_OFF + t * 2 * TILE);
+        const uint32_t sv = smem_u32(smem + KV_OFF + s * 2 * TILE);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t aoff = (uint32_t)((kk >> 2) * TILE + (kk & 3) * 32);
           // V sub-tiles hold 64 head-dim columns each (LBO = TILE); 16 keys = 2 atoms of 8 rows.
-          umma_bf16(tmem + O_COL, sdesc_sw128(sp + aoff, 16, 1024), sdesc_sw128(sv + (uint32_t)(kk * 2048), TILE, 1024),
-                    idesc_o, (j | kk) != 0);
+          umma_bf16(tmem + o_col(t), sdesc_sw128(sp + aoff, 16, 1024),
+                    sdesc_sw128(sv + (uint32_t)(kk * 2048), TILE, 1024), idesc_o, (j | kk) != 0);
         }
-        umma_commit(o_done);
-        umma_commit(kv_empty + s);
+        umma_commit(o_done + t);
+        if (t == ntile - 1) umma_commit(kv_free + s);   // V_j done
         return true;
       };
-      if (ok) ok = issue_s(0);
+      for (int t = 0; ok && t < ntile; ++t) ok = issue_s(t, 0);
       for (int j = 0; ok && j < nblk; ++j) {
-        if (j + 1 < nblk) ok = issue_s(j + 1);
-        if (ok) ok = issue_o(j);
+        for (int t = 0; ok && t < ntile; ++t) {
+          if (j + 1 < nblk) ok = issue_s(t, j + 1);
+          if (ok) ok = issue_o(t, j);
+        }
       }
       umma_commit(drain);
       volatile int no_abort = 0;
       mbar_wait(drain, 0, &no_abort, args.status, DEV_TIMEOUT_DRAIN);
     }
-  } else {
+  } else if ((warp >> 2) < ntile) {
     // ------------------------------------------------------------ softmax / correction / epilogue
-    const int row = warp * 32 + lane;                       // query row within the tile == TMEM lane
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    const int t = warp >> 2, q = warp & 3;
+    const int row = q * 32 + lane;                            // query row within the tile == TMEM lane
+    const uint32_t lane_off = (uint32_t)(q * 32) << 16;
     const float sl2 = args.scale_log2;
     float m = -INFINITY, l = 0.f;
-    uint8_t* sP = smem + P_OFF;
+    uint8_t* sP = smem + P_OFF + t * 2 * TILE;
     bool ok = true;
     for (int j = 0; j < nblk; ++j) {
-      const int s = j & 1;
-      const uint32_t par = (uint32_t)(j >> 1) & 1u;
-      ok = mbar_wait(s_full + s, par, abort_flag, args.status, DEV_TIMEOUT_SOFTMAX);
+      ok = mbar_wait(s_full + t, (uint32_t)j & 1u, abort_flag, args.status, DEV_TIMEOUT_SOFTMAX);
       if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
       tc_fence_after();
       float sv[128];
       {
-        uint32_t r[32];
+        uint32_t* r = reinterpret_cast<uint32_t*>(sv);
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          tmem_ld32(tmem + lane_off + S_COL + (uint32_t)(s * 128 + c * 32), r);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) sv[c * 32 + i] = __uint_as_float(r[i]);
-        }
+        for (int c = 0; c < 4; ++c)
+          tmem_ld32(tmem + lane_off + s_col(t) + (uint32_t)(c * 32), *reinterpret_cast<uint32_t(*)[32]>(r + 32 * c));
+        tmem_ld_wait();
       }
       tc_fence_before();
-      mbar_arrive(s_free + s);
+      mbar_arrive(s_free + t);
       const int valid = (j < nb0) ? min(BKV, n0 - j * BKV) : min(BKV, n1 - (j - nb0) * BKV);
-      float mx = -INFINITY;
+      if (valid < BKV) {   // ragged last block of a segment
+#pragma unroll
+        for (int i = 0; i < 128; ++i)
+          if (i >= valid) sv[i] = -INFINITY;
+      }
+      float mx8[8];
+#pragma unroll
+      for (int a = 0; a < 8; ++a) mx8[a] = sv[a];
+#pragma unroll
+      for (int i = 8; i < 128; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], sv[i]);
+      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]))) * sl2;
+      // lazy rescale: keep the running max unless it grows by more than 2^8 (p stays <= 256)
+      float alpha = 1.f;
+      if (mx > m + 8.f) {
+        alpha = ex2(m - mx);   // 0 on the first block (m = -inf)
+        m = mx;
+      }
+      float rs8[8];
+#pragma unroll
+      for (int a = 0; a < 8; ++a) rs8[a] = 0.f;
 #pragma unroll
       for (int i = 0; i < 128; ++i) {
-        sv[i] = (i < valid) ? sv[i] * sl2 : -INFINITY;
-        mx = fmaxf(mx, sv[i]);
+        sv[i] = ex2(fmaf(sv[i], sl2, -m));
+        rs8[i & 7] += sv[i];
       }
-      const float m_new = fmaxf(m, mx);
-      const float alpha = ex2(m - m_new);   // 0 on the first block (m = -inf)
-      float rs = 0.f;
-#pragma unroll
-      for (int i = 0; i < 128; ++i) {
-        sv[i] = ex2(sv[i] - m_new);
-        rs += sv[i];
-      }
-      l = l * alpha + rs;
-      m = m_new;
-      if (j > 0) {
-        ok = mbar_wait(o_done, (uint32_t)(j - 1) & 1u, abort_flag, args.status, DEV_TIMEOUT_SOFTMAX);
+      l = l * alpha + (((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7])));
+      if (j > 0) {   // P buffer and O are free once the previous P V finished
+        ok = mbar_wait(o_done + t, (uint32_t)(j - 1) & 1u, abort_flag, args.status, DEV_TIMEOUT_SOFTMAX);
         if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
         tc_fence_after();
         if (__any_sync(0xffffffffu, alpha < 1.f)) {
           uint32_t r[32];
 #pragma unroll 1
           for (int c = 0; c < 4; ++c) {
-            const uint32_t ta = tmem + lane_off + O_COL + (uint32_t)(c * 32);
+            const uint32_t ta = tmem + lane_off + o_col(t) + (uint32_t)(c * 32);
             tmem_ld32(ta, r);
             tmem_ld_wait();
 #pragma unroll
@@ -243,18 +258,18 @@ __global__ void __launch_bounds__(192, 1)
       }
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive(p_full + t);
     }
     if (ok && nblk > 0) {
-      ok = mbar_wait(o_done, (uint32_t)(nblk - 1) & 1u, abort_flag, args.status, DEV_TIMEOUT_SOFTMAX);
+      ok = mbar_wait(o_done + t, (uint32_t)(nblk - 1) & 1u, abort_flag, args.status, DEV_TIMEOUT_SOFTMAX);
       if (__all_sync(0xffffffffu, ok)) {
         tc_fence_after();
         const float inv = 1.f / l;
-        const int grow = q0 + row;
+        const int grow = q0 + t * BQ + row;
         uint32_t r[32];
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
-          tmem_ld32(tmem + lane_off + O_COL + (uint32_t)(c * 32), r);
+          tmem_ld32(tmem + lane_off + o_col(t) + (uint32_t)(c * 32), r);
           tmem_ld_wait();
           if (grow < args.Lq) {
             uint4* dst = reinterpret_cast<uint4*>(args.out + (size_t)grow * args.ld_out + col + c * 32);
@@ -271,7 +286,7 @@ __global__ void __launch_bounds__(192, 1)
     }
   }
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     tc_fence_after();
     tmem_dealloc(tmem, TMEM_COLS);
   }
@@ -284,8 +299,8 @@ int attention_launch(const CUtensorMap& tmQ, const CUtensorMap& tmK0, const CUte
   cudaError_t err =
       cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, attn::SMEM);
   if (err != cudaSuccess) return FW_ECUDA;
-  dim3 grid((a.Lq + attn::BQ - 1) / attn::BQ, a.heads);
-  attention_kernel<<<grid, 192, attn::SMEM, s>>>(tmQ, tmK0, tmV0, tmK1, tmV1, a);
+  dim3 grid((a.Lq + 2 * attn::BQ - 1) / (2 * attn::BQ), a.heads);
+  attention_kernel<<<grid, attn::THREADS, attn::SMEM, s>>>(tmQ, tmK0, tmV0, tmK1, tmV1, a);
   note_launch();
   return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
 }

@@ -127,13 +127,20 @@ int ln_bf16(const __nv_bfloat16* x, int ldx, int M, int D, float eps, const floa
 // ------------------------------------------------------------------ RMSNorm (+ RoPE)
 // out = RMSNorm(x) * w over D = 128 * NG, then (optionally) each (even, odd) pair of every
 // head is rotated by rope[row, pair % (hd / 2)] = (cos, sin).
+struct RmsPair {
+  const __nv_bfloat16* x[2];
+  const __nv_bfloat16* w[2];
+  __nv_bfloat16* out[2];
+};
+
 template <int NG>
-__global__ void __launch_bounds__(256) rms_rope_kernel(const __nv_bfloat16* __restrict__ x, int ldx, int M,
-                                                       float eps, const __nv_bfloat16* __restrict__ w,
-                                                       const float2* __restrict__ rope, int hd,
-                                                       __nv_bfloat16* __restrict__ out, int ldo) {
+__global__ void __launch_bounds__(256) rms_rope_kernel(RmsPair pr, int ldx, int M, float eps,
+                                                       const float2* __restrict__ rope, int hd, int ldo) {
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (row >= M) return;
+  const __nv_bfloat16* __restrict__ x = pr.x[blockIdx.y];
+  const __nv_bfloat16* __restrict__ w = pr.w[blockIdx.y];
+  __nv_bfloat16* __restrict__ out = pr.out[blockIdx.y];
   constexpr int D = 128 * NG;
   float v[NG][4];
   float q = 0.f;
@@ -166,19 +173,26 @@ __global__ void __launch_bounds__(256) rms_rope_kernel(const __nv_bfloat16* __re
   }
 }
 
-int rms_rope(const __nv_bfloat16* x, int ldx, int M, int D, float eps, const __nv_bfloat16* w, const float2* rope,
-             int hd, __nv_bfloat16* out, int ldo, cudaStream_t s) {
+int rms_rope2(const __nv_bfloat16* x, const __nv_bfloat16* w, __nv_bfloat16* out, const __nv_bfloat16* x2,
+              const __nv_bfloat16* w2, __nv_bfloat16* out2, int ldx, int M, int D, float eps, const float2* rope, int hd,
+              int ldo, cudaStream_t s) {
   if (D % 128 || ldx % 4 || ldo % 4 || (rope && (hd % 4 || D % hd))) return FW_ESHAPE;
-  const dim3 grid((M + 7) / 8), block(256);
+  RmsPair pr{{x, x2}, {w, w2}, {out, out2}};
+  const dim3 grid((M + 7) / 8, x2 ? 2 : 1), block(256);
   switch (D / 128) {
 #define FW_RMS_CASE(n) \
-  case n: rms_rope_kernel<n><<<grid, block, 0, s>>>(x, ldx, M, eps, w, rope, hd, out, ldo); note_launch(); break;
+  case n: rms_rope_kernel<n><<<grid, block, 0, s>>>(pr, ldx, M, eps, rope, hd, ldo); note_launch(); break;
     FW_RMS_CASE(1) FW_RMS_CASE(2) FW_RMS_CASE(3) FW_RMS_CASE(4) FW_RMS_CASE(6) FW_RMS_CASE(8)
     FW_RMS_CASE(10) FW_RMS_CASE(12) FW_RMS_CASE(16)
 #undef FW_RMS_CASE
     default: return FW_ESHAPE;
   }
   return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
+}
+
+int rms_rope(const __nv_bfloat16* x, int ldx, int M, int D, float eps, const __nv_bfloat16* w, const float2* rope,
+             int hd, __nv_bfloat16* out, int ldo, cudaStream_t s) {
+  return rms_rope2(x, w, out, nullptr, nullptr, nullptr, ldx, M, D, eps, rope, hd, ldo, s);
 }
 
 // ------------------------------------------------------------------ RoPE tables

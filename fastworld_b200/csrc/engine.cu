@@ -548,8 +548,8 @@ static int forward(fw_handle* h, int step, int first, int write, const __nv_bflo
     const float* ee = h->ee + (size_t)i * 6 * D;
     FW_TRY(ln_f32(h->xs, D, L, D, c.eps, ee + 0 * D, ee + 1 * D, nullptr, nullptr, h->y, D, s));
     FW_TRY(run(ly.qkv, s));
-    FW_TRY(rms_rope(h->q, D, L, D, c.eps, W(h, p + "sa.nq.w"), rope, h->HD, h->q, D, s));
-    FW_TRY(rms_rope(h->kcur, D, L, D, c.eps, W(h, p + "sa.nk.w"), rope, h->HD, h->kcur, D, s));
+    FW_TRY(rms_rope2(h->q, W(h, p + "sa.nq.w"), h->q, h->kcur, W(h, p + "sa.nk.w"), h->kcur, D, L, D, c.eps, rope,
+                     h->HD, D, s));
     FW_TRY(run(first ? ly.self_first : ly.self_steady, s));
     if (write) {   // the history is written after the attention read it (static.py:217-218)
       FW_TRY(copy_bytes(ptr_of(h, "hk." + std::to_string(i)), h->kcur, (size_t)L * D * 2, s));

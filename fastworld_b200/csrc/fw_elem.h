@@ -12,6 +12,10 @@ int ln_bf16(const __nv_bfloat16* x, int ldx, int M, int D, float eps, const floa
             const __nv_bfloat16* w, const __nv_bfloat16* b, __nv_bfloat16* out, int ldo, cudaStream_t s);
 int rms_rope(const __nv_bfloat16* x, int ldx, int M, int D, float eps, const __nv_bfloat16* w, const float2* rope,
              int hd, __nv_bfloat16* out, int ldo, cudaStream_t s);
+// Two tensors of the same shape in one launch (x2 may be null).
+int rms_rope2(const __nv_bfloat16* x, const __nv_bfloat16* w, __nv_bfloat16* out, const __nv_bfloat16* x2,
+              const __nv_bfloat16* w2, __nv_bfloat16* out2, int ldx, int M, int D, float eps, const float2* rope, int hd,
+              int ldo, cudaStream_t s);
 int rope_tables(const int* chunk, int F, int th, int tw, int hd, double theta, float2* table, int act_hd,
                 float* act_cos, float* act_sin, cudaStream_t s);
 int smallm_linear_f32(const float* x, int ldx, int M, const __nv_bfloat16* W, int ldw, const __nv_bfloat16* b, int N,

@@ -7,8 +7,10 @@
 //   warp 0      TMA producer: A tile [128 x 64] and B tile [BN x 64] per stage, 128-byte swizzle
 //   warp 1      MMA issuer: 4 x tcgen05.mma (K = 16 each) per stage into a TMEM accumulator;
 //               tcgen05.commit releases the smem stage and, per tile, signals the epilogue
-//   warps 2..5  epilogue: tcgen05.ld 32 columns at a time (thread = output row), fused bias /
-//               GELU / gated fp32 residual update, direct vector stores
+//   warps 2..9  epilogue (thread = output row, two warps per TMEM lane quarter splitting the
+//               tile's columns): all accumulator columns loaded with tcgen05.ld, TMEM released,
+//               then fused bias / GELU / gated fp32 residual update and direct vector stores;
+//               the residual rows are prefetched into L2 while the main loop still runs
 // The TMEM accumulator is double-buffered (2 x BN columns) so the epilogue of tile i overlaps
 // the main loop of tile i + 1.  Tile order is M-fastest so consecutive CTAs share a weight
 // tile in L2.  M, N and K tails are zero-filled by TMA and masked in the epilogue.
@@ -26,7 +28,7 @@ struct GemmCfg {
   static constexpr int STAGE = A_BYTES + B_BYTES;
   static constexpr int STAGES = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int SMEM = STAGES * STAGE + 1024 + 256;
+  static constexpr int SMEM = STAGES * STAGE + 256 + 8 * 4096 + 1024;   // stages, barriers, epilogue staging, align
 };
 
 __device__ __forceinline__ void add_bias(const GemmEpi& e, int frame, int col0, float (&v)[32]) {
@@ -58,44 +60,64 @@ __device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float (&
                        pack_bf16(v[8 * j + 4], v[8 * j + 5]), pack_bf16(v[8 * j + 6], v[8 * j + 7]));
 }
 
-__device__ __forceinline__ void epilogue_chunk(const GemmEpi& e, int row, int col0, const uint32_t (&r)[32]) {
+// One 32 x 32 chunk of the output tile per warp (thread `lane` holds row row0 + lane, columns
+// col0 .. col0 + 31 in r).  Bias and activation are applied per thread; the chunk is then
+// staged through the warp's 4 KB shared-memory buffer (16-byte granules XOR-swizzled by row so
+// both phases are bank-conflict free) and written out row-contiguously: each warp instruction
+// covers 4 rows x 128 bytes, so the fp32 residual read-modify-write and the stores move whole
+// cache lines instead of 32 scattered 16-byte pieces.
+__device__ __forceinline__ void epilogue_chunk(const GemmEpi& e, int row0, int M, int col0, const uint32_t (&r)[32],
+                                               float4* stage, int lane) {
   float v[32];
 #pragma unroll
   for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-  const int frame = row / e.rows_per_frame;
-  add_bias(e, frame, col0, v);
-  if (e.mode == EPI_BF16 || e.mode == EPI_GELU_BF16 || e.mode == EPI_GELU_ERF_BF16) {
-    if (e.mode == EPI_GELU_BF16) {
+  const int my_row = row0 + lane;
+  add_bias(e, (my_row < M ? my_row : 0) / e.rows_per_frame, col0, v);
+  if (e.mode == EPI_GELU_BF16) {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
-    } else if (e.mode == EPI_GELU_ERF_BF16) {
+    for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
+  } else if (e.mode == EPI_GELU_ERF_BF16) {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = 0.5f * v[j] * (1.f + erff(v[j] * 0.7071067811865476f));
+    for (int j = 0; j < 32; ++j) v[j] = 0.5f * v[j] * (1.f + erff(v[j] * 0.7071067811865476f));
+  }
+  __syncwarp();
+#pragma unroll
+  for (int k = 0; k < 8; ++k)
+    stage[lane * 8 + (k ^ (lane & 7))] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+  __syncwarp();
+  const int k = lane & 7;                    // this lane's 4 columns: col0 + 4k .. +3
+  const int col = col0 + 4 * k;
+#pragma unroll
+  for (int it = 0; it < 8; ++it) {
+    const int rr = it * 4 + (lane >> 3);     // row within the chunk
+    const int grow = row0 + rr;
+    if (grow >= M) continue;
+    float4 a = stage[rr * 8 + (k ^ (rr & 7))];
+    if (e.mode == EPI_RESID_F32) {
+      float4* rp = reinterpret_cast<float4*>(e.resid + (size_t)grow * e.ld_resid + col);
+      float4 x = *rp;
+      if (e.gate) {
+        const float4 g = __ldg(reinterpret_cast<const float4*>(e.gate + (size_t)(grow / e.rows_per_frame) * e.gate_stride + col));
+        x.x += g.x * a.x; x.y += g.y * a.y; x.z += g.z * a.z; x.w += g.w * a.w;
+      } else {
+        x.x += a.x; x.y += a.y; x.z += a.z; x.w += a.w;
+      }
+      *rp = x;
+      if (e.mirror)
+        *reinterpret_cast<uint2*>(e.mirror + (size_t)grow * e.ld_mirror + col) =
+            make_uint2(pack_bf16(x.x, x.y), pack_bf16(x.z, x.w));
+    } else if (e.mode == EPI_F32) {
+      *reinterpret_cast<float4*>(reinterpret_cast<float*>(e.out[0]) + (size_t)grow * e.ld_out + col) = a;
+    } else {
+      const int seg = col0 / e.seg_w;
+      __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(e.out[seg]) + (size_t)grow * e.ld_out + (col - seg * e.seg_w);
+      *reinterpret_cast<uint2*>(dst) = make_uint2(pack_bf16(a.x, a.y), pack_bf16(a.z, a.w));
     }
-    const int seg = col0 / e.seg_w;
-    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(e.out[seg]) + (size_t)row * e.ld_out + (col0 - seg * e.seg_w);
-    store_bf16x32(dst, v);
-  } else if (e.mode == EPI_F32) {
-    float4* d4 = reinterpret_cast<float4*>(reinterpret_cast<float*>(e.out[0]) + (size_t)row * e.ld_out + col0);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) d4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-  } else {   // EPI_RESID_F32
-    float4* rp = reinterpret_cast<float4*>(e.resid + (size_t)row * e.ld_resid + col0);
-    const float4* gp = e.gate ? reinterpret_cast<const float4*>(e.gate + (size_t)frame * e.gate_stride + col0) : nullptr;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      float4 x = rp[j];
-      float4 g = gp ? __ldg(gp + j) : make_float4(1.f, 1.f, 1.f, 1.f);
-      x.x += g.x * v[4 * j + 0]; x.y += g.y * v[4 * j + 1]; x.z += g.z * v[4 * j + 2]; x.w += g.w * v[4 * j + 3];
-      rp[j] = x;
-      v[4 * j + 0] = x.x; v[4 * j + 1] = x.y; v[4 * j + 2] = x.z; v[4 * j + 3] = x.w;
-    }
-    if (e.mirror) store_bf16x32(e.mirror + (size_t)row * e.ld_mirror + col0, v);
   }
 }
 
 template <int BN>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const GemmArgs args) {
   using C = GemmCfg<BN>;
@@ -111,8 +133,9 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* drain = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // per-epilogue-warp 4 KB staging buffers for coalesced output (after the 256-byte barrier area)
+  float4* stage = reinterpret_cast<float4*>(smem + C::STAGES * C::STAGE + 256) + (warp >= 2 ? (warp - 2) * 256 : 0);
   const int M = args.M, N = args.N, K = args.K;
   const int num_m = (M + 127) / 128, num_n = (N + BN - 1) / BN;
   const int num_tiles = num_m * num_n, num_kb = (K + 63) / 64;
@@ -124,7 +147,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(tfull + a, 1);
-      mbar_init(tempty + a, 128);
+      mbar_init(tempty + a, 256);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -209,27 +232,37 @@ __global__ void __launch_bounds__(192, 1)
       mbar_wait(drain, 0, &no_abort, args.status, DEV_TIMEOUT_DRAIN);
     }
   } else {
-    const int q = warp & 3;   // TMEM lane quarter this warp may access
+    // 8 epilogue warps: warp w reads TMEM lane quarter (w % 4) and column half (w - 2) / 4 of
+    // the tile.  All of a thread's accumulator columns are loaded at once, the TMEM buffer is
+    // released, and the bias / activation / residual math and the stores run from registers.
+    constexpr int NC = BN / 64;                   // 32-column chunks per thread
+    const int q = warp & 3, h = (warp - 2) >> 2;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
       const int mb = t % num_m, nb = t / num_m;
+      const int row = mb * 128 + q * 32 + lane;
+      const int colh = nb * BN + h * (BN / 2);
+      if (args.epi.mode == EPI_RESID_F32 && row < M && colh < N) {   // warm L2 with this thread's residual row part
+        const char* p = reinterpret_cast<const char*>(args.epi.resid + (size_t)row * args.epi.ld_resid + colh);
+#pragma unroll
+        for (int b = 0; b < BN * 2; b += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(p + b));
+      }
       const bool ok = mbar_wait(tfull + acc, acc_phase, abort_flag, args.status, DEV_TIMEOUT_EPILOGUE);
       if (!__all_sync(0xffffffffu, ok)) break;   // keep the warp converged for tcgen05.ld
       tc_fence_after();
-      const int row = mb * 128 + q * 32 + lane;
-      const uint32_t tb = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        const int col0 = nb * BN + c * 32;
-        if (col0 >= N) break;
-        uint32_t r[32];
-        tmem_ld32(tb + (uint32_t)(c * 32), r);
-        tmem_ld_wait();
-        if (row < M) epilogue_chunk(args.epi, row, col0, r);
-      }
+      const uint32_t tb = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + h * (BN / 2));
+      uint32_t r[NC][32];
+#pragma unroll
+      for (int c = 0; c < NC; ++c) tmem_ld32(tb + (uint32_t)(c * 32), r[c]);
+      tmem_ld_wait();
       tc_fence_before();
-      mbar_arrive(tempty + acc);
+      mbar_arrive(tempty + acc);                 // the accumulator buffer is free again
+#pragma unroll
+      for (int c = 0; c < NC; ++c) {
+        const int col0 = colh + c * 32;
+        if (col0 < N) epilogue_chunk(args.epi, row - lane, M, col0, r[c], stage, lane);
+      }
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
@@ -280,7 +313,7 @@ static int launch_bn(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmA
   using C = GemmCfg<BN>;
   cudaError_t err = cudaFuncSetAttribute(gemm_bf16_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (err != cudaSuccess) return FW_ECUDA;
-  gemm_bf16_kernel<BN><<<grid, 192, C::SMEM, s>>>(tmA, tmB, a);
+  gemm_bf16_kernel<BN><<<grid, 320, C::SMEM, s>>>(tmA, tmB, a);
   note_launch();
   return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
 }

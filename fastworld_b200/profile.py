@@ -2,6 +2,7 @@
 
     python -m fastworld_b200.profile chunk [--chunks 2]   eager MG2 chunks (chunk 0, then steady)
     python -m fastworld_b200.profile gemm  [--reps 3]     FFN-up GEMM, MG2 shape, GELU epilogue
+    python -m fastworld_b200.profile gemm_resid           O-projection GEMM (N = K = 1536) with the gated residual
     python -m fastworld_b200.profile attn  [--reps 3]     steady self-attention, 12 heads, 2640 + 2640 keys
 """
 from __future__ import annotations
@@ -38,6 +39,20 @@ def gemm(reps: int) -> None:
     print("gemm ok")
 
 
+def gemm_resid(reps: int) -> None:
+    from fastworld_b200 import ops
+    g = torch.Generator(device="cuda").manual_seed(0)
+    A = torch.randn(2640, 1536, device="cuda", generator=g).to(torch.bfloat16)
+    B = (torch.randn(1536, 1536, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    bias = torch.zeros(1536, device="cuda", dtype=torch.bfloat16)
+    resid = torch.zeros(2640, 1536, device="cuda")
+    gate = torch.ones(3, 1536, device="cuda")
+    for _ in range(reps):
+        ops.gemm_resid_(resid, A, B, bias, gate, 880)
+    torch.cuda.synchronize()
+    print("gemm_resid ok")
+
+
 def attn(reps: int) -> None:
     from fastworld_b200 import ops
     g = torch.Generator(device="cuda").manual_seed(0)
@@ -52,8 +67,9 @@ def attn(reps: int) -> None:
 
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["chunk", "gemm", "attn"])
+    ap.add_argument("what", choices=["chunk", "gemm", "gemm_resid", "attn"])
     ap.add_argument("--chunks", type=int, default=2)
     ap.add_argument("--reps", type=int, default=3)
     a = ap.parse_args()
-    {"chunk": lambda: chunk(a.chunks), "gemm": lambda: gemm(a.reps), "attn": lambda: attn(a.reps)}[a.what]()
+    {"chunk": lambda: chunk(a.chunks), "gemm": lambda: gemm(a.reps), "gemm_resid": lambda: gemm_resid(a.reps),
+     "attn": lambda: attn(a.reps)}[a.what]()
