@@ -156,6 +156,39 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def steady_chunk_ms(cfg, args, rank, world, local):
+    """Build a session, run chunk 0, capture, warm up, and time steady-chunk graph replays."""
+    from fastworld_b200.static import B200StaticMG
+    S = B200StaticMG(cfg, device=f"cuda:{local}", seed=0)
+    S.add_image("img0", seed=11 + rank, max_chunks=2)
+    path = [("img0", ("w", "u")), ("img0", ("a", "l"))]
+    S._prep(path, 0)
+    S._chunk(True)
+    S.capture(warmup=1)
+    S._prep(path, 1)
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        S.graphs[(False, "gen")].replay()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        S.graphs[(False, "gen")].replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t)
+    S.graphs = {}
+    del S
+    torch.cuda.empty_cache()
+    return ms
+
+
 def run_ours(args):
     rank, world, local = dist_env()
     torch.cuda.set_device(local)
@@ -163,7 +196,7 @@ def run_ours(args):
         import datetime
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
     from fastworld_b200 import _lib, ops
-    from fastworld_b200.config import MG2
+    from fastworld_b200.config import MG2, MG2_FP8
     from fastworld_b200.static import B200StaticMG
     cfg = MG2
     S = B200StaticMG(cfg, device=f"cuda:{local}", seed=0)
@@ -249,6 +282,15 @@ def run_ours(args):
     if os.path.exists(prof):
         traffic = json.load(open(prof)).get("dram_bytes_per_launch")
     flops_all, flops_main = chunk_flops(cfg)
+    h2d = S.gm.numel() * 2 + S.kc.numel() * 2 + 16
+    d2h = S.out.numel() * 2
+    variants = {}
+    if not args.no_fp8:   # same chunk with e4m3 block linears
+        del S
+        torch.cuda.empty_cache()
+        ms8 = steady_chunk_ms(MG2_FP8, args, rank, world, local)
+        variants["fp8"] = {"ms_per_step": ms8, "value": world * FRAMES_PER_CHUNK / (ms8 / 1e3), "unit": "frames/s",
+                           "speedup_vs_bf16": ms / ms8, "linear": "e4m3, per-channel weight / per-token scales"}
     line = None
     if rank == 0:
         fps = world * FRAMES_PER_CHUNK / (ms / 1e3)
@@ -259,7 +301,6 @@ def run_ours(args):
             cpu = {"value": FRAMES_PER_CHUNK / cpu_chunk_s, "unit": "frames/s", "cores": threads, "kind": "port",
                    "sample": f"one forward of a 2-block MG2-width slice (1 action block), {sample_s:.1f} s, "
                              "x15 slices x5 forwards per chunk"}
-        h2d = S.gm.numel() * 2 + S.kc.numel() * 2 + 16
         line = {"metric": METRIC, "value": fps, "unit": "frames/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
@@ -270,13 +311,13 @@ def run_ours(args):
                            "per forward)", "chunk_tflop": flops_all / 1e12,
                            "chunk_tflops_achieved": flops_all / 1e12 / (ms / 1e3)},
                 "e2e": {"value": e2e_fps, "unit": "frames/s", "ms_per_step": e2e_ms, "h2d_bytes_per_step": h2d,
-                        "d2h_bytes_per_step": S.out.numel() * 2},
+                        "d2h_bytes_per_step": d2h},
                 "gpu_launches": launches_per_chunk * args.steps,
                 "roofline": {"bound": "tensor", "kernel": "gemm_bf16_kernel<256> (FFN-up 2640x8960x1536, GELU)",
                              "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s", "frac": achieved / peak_tf,
                              "peak_kind": f"{peak_kind} bf16 burst", "traffic": traffic,
                              "launch_ms": gemm_ms, "algorithmic_gflop": gflop},
-                "cpu_baseline": cpu, "clocks": clk.summary(), "device_status": status}
+                "cpu_baseline": cpu, "clocks": clk.summary(), "device_status": status, "variants": variants}
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.barrier()
@@ -291,6 +332,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--no-fp8", action="store_true", help="skip the e4m3 variant (configs[2])")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

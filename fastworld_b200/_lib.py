@@ -13,7 +13,7 @@ LIB_PATH = os.path.join(HERE, "libfastworld_b200.so")
 
 FW_MAX_ACTION_BLOCKS = 64
 FW_MAX_STEPS = 16
-KIND_WEIGHT, KIND_STATE, KIND_INPUT, KIND_OUTPUT, KIND_WORKSPACE, KIND_STATUS = range(6)
+KIND_WEIGHT, KIND_STATE, KIND_INPUT, KIND_OUTPUT, KIND_WORKSPACE, KIND_STATUS, KIND_DERIVED = range(7)
 DT_BF16, DT_F32, DT_I32, DT_U8 = range(4)
 EPI_BF16, EPI_GELU_BF16, EPI_RESID_F32, EPI_F32, EPI_GELU_ERF_BF16 = range(5)
 
@@ -31,6 +31,7 @@ class FwConfig(ctypes.Structure):
         ("time_ratio", ctypes.c_int), ("window", ctypes.c_int),
         ("n_steps", ctypes.c_int), ("steps", ctypes.c_float * FW_MAX_STEPS),
         ("eps", ctypes.c_float), ("eps_ln", ctypes.c_float), ("rope_theta", ctypes.c_float),
+        ("linear_fp8", ctypes.c_int),
     ]
 
 
@@ -55,6 +56,11 @@ _SIGS = {
     "fw_copy": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
     "fw_gemm_bf16": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
                                     ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]),
+    "fw_gemm_e4m3": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                    ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                    ctypes.c_void_p]),
+    "fw_quant_e4m3": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
+                                     ctypes.c_void_p]),
     "fw_gemm_bf16_resid": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                           ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                           ctypes.c_void_p]),
@@ -105,6 +111,9 @@ def make_config(cfg) -> FwConfig:
     for i, t in enumerate(cfg.steps):
         c.steps[i] = float(t)
     c.eps, c.eps_ln, c.rope_theta = float(cfg.eps), 1e-5, float(cfg.rope_theta)
+    if cfg.linear not in ("bf16", "fp8"):
+        raise ValueError(f"linear dtype {cfg.linear!r}")
+    c.linear_fp8 = int(cfg.linear == "fp8")
     return c
 
 

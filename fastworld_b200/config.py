@@ -61,6 +61,9 @@ class DiTConfig:
     eps: float = 1e-6
     rope_theta: float = 10000.0
     max_frames: int = 1024      # RoPE table rows (Wan rope_params max_seq_len)
+    # block linears: "bf16", or "fp8" = e4m3 with per-output-channel weight scales (absmax/448)
+    # and per-token activation scales; attention and norms stay bf16
+    linear: str = "bf16"
 
     # ---- derived
     @property
@@ -136,4 +139,7 @@ TINY = DiTConfig(name="tiny", dim=128, heads=2, head_dim=64, ffn=256, layers=2, 
 SMALL = DiTConfig(name="small", dim=256, heads=2, head_dim=128, ffn=512, layers=2, ctx_dim=256,
                   action_blocks=(1,), act_heads=4, mouse_hidden=256, keyboard_hidden=64)
 
-PRESETS = {c.name: c for c in (BLOCK, MG2, WAN14B, TINY, SMALL)}
+# config[1] with e4m3 block linears.
+MG2_FP8 = MG2.replace(name="mg2_fp8", linear="fp8")
+
+PRESETS = {c.name: c for c in (BLOCK, MG2, MG2_FP8, WAN14B, TINY, SMALL)}

@@ -15,6 +15,7 @@
 //                        [mk | current] frames + history write (151-161)
 //   kb_kv_kernel         keyboard K/V norm + RoPE (171-175)
 //   kb_attn_kernel       keyboard attention over [kk | current] (173-184)
+#include <cuda_fp8.h>
 #include <math.h>
 
 #include "../../include/fastworld_b200.h"
@@ -49,12 +50,19 @@ __device__ __forceinline__ void store4(__nv_bfloat16* p, const float (&v)[4]) {
 
 // ------------------------------------------------------------------ LayerNorm
 // out = LN(x) [* w + b] [* (1 + scale) + shift], one warp per row, D = 128 * NG.
+// Four floats -> four e4m3 bytes (memory order) after multiplying by `inv`, saturating.
+__device__ __forceinline__ uint32_t pack4_e4m3(float a, float b, float c, float d, float inv) {
+  const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(a * inv, b * inv), __NV_SATFINITE, __NV_E4M3);
+  const uint32_t hi = __nv_cvt_float2_to_fp8x2(make_float2(c * inv, d * inv), __NV_SATFINITE, __NV_E4M3);
+  return lo | (hi << 16);
+}
+
 template <typename Tin, int NG>
 __global__ void __launch_bounds__(256) ln_kernel(const Tin* __restrict__ x, int ldx, int M, float eps,
                                                  const float* __restrict__ shift, const float* __restrict__ scale,
                                                  const __nv_bfloat16* __restrict__ w,
                                                  const __nv_bfloat16* __restrict__ b, __nv_bfloat16* __restrict__ out,
-                                                 int ldo) {
+                                                 int ldo, uint8_t* __restrict__ out8, float* __restrict__ sa) {
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (row >= M) return;
   constexpr int D = 128 * NG;
@@ -75,12 +83,13 @@ __global__ void __launch_bounds__(256) ln_kernel(const Tin* __restrict__ x, int 
       q += d * d;
     }
   const float rstd = rsqrtf(warp_sum(q) * (1.f / D) + eps);
+  float amax = 0.f;
 #pragma unroll
   for (int g = 0; g < NG; ++g) {
     const int c = g * 128 + lane * 4;
-    float y[4];
+    float* y = v[g];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) y[i] = (v[g][i] - mean) * rstd;
+    for (int i = 0; i < 4; ++i) y[i] = (y[i] - mean) * rstd;
     if (w) {
       float wv[4], bv[4];
       load4(w + c, wv);
@@ -95,18 +104,34 @@ __global__ void __launch_bounds__(256) ln_kernel(const Tin* __restrict__ x, int 
 #pragma unroll
       for (int i = 0; i < 4; ++i) y[i] = y[i] * (1.f + sc[i]) + sh[i];
     }
-    store4(out + (size_t)row * ldo + c, y);
+    if (out8) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) amax = fmaxf(amax, fabsf(y[i]));
+    } else {
+      store4(out + (size_t)row * ldo + c, v[g]);
+    }
+  }
+  if (out8) {   // e4m3 output with a per-row scale absmax / 448
+    amax = warp_max(amax);
+    const float sc = amax > 0.f ? amax * (1.f / 448.f) : 1.f;
+    const float inv = 1.f / sc;
+#pragma unroll
+    for (int g = 0; g < NG; ++g)
+      *reinterpret_cast<uint32_t*>(out8 + (size_t)row * ldo + g * 128 + lane * 4) =
+          pack4_e4m3(v[g][0], v[g][1], v[g][2], v[g][3], inv);
+    if (lane == 0) sa[row] = sc;
   }
 }
 
 template <typename Tin>
 static int ln_dispatch(const Tin* x, int ldx, int M, int D, float eps, const float* shift, const float* scale,
-                       const __nv_bfloat16* w, const __nv_bfloat16* b, __nv_bfloat16* out, int ldo, cudaStream_t s) {
-  if (D % 128 || ldx % 4 || ldo % 4) return FW_ESHAPE;
+                       const __nv_bfloat16* w, const __nv_bfloat16* b, __nv_bfloat16* out, int ldo, cudaStream_t s,
+                       uint8_t* out8 = nullptr, float* sa = nullptr) {
+  if (D % 128 || ldx % 4 || ldo % 4 || (out8 && !sa)) return FW_ESHAPE;
   const dim3 grid((M + 7) / 8), block(256);
   switch (D / 128) {
 #define FW_LN_CASE(n) \
-  case n: ln_kernel<Tin, n><<<grid, block, 0, s>>>(x, ldx, M, eps, shift, scale, w, b, out, ldo); note_launch(); break;
+  case n: ln_kernel<Tin, n><<<grid, block, 0, s>>>(x, ldx, M, eps, shift, scale, w, b, out, ldo, out8, sa); note_launch(); break;
     FW_LN_CASE(1) FW_LN_CASE(2) FW_LN_CASE(3) FW_LN_CASE(4) FW_LN_CASE(5) FW_LN_CASE(6) FW_LN_CASE(7)
     FW_LN_CASE(8) FW_LN_CASE(9) FW_LN_CASE(10) FW_LN_CASE(11) FW_LN_CASE(12) FW_LN_CASE(16)
 #undef FW_LN_CASE
@@ -122,6 +147,51 @@ int ln_f32(const float* x, int ldx, int M, int D, float eps, const float* shift,
 int ln_bf16(const __nv_bfloat16* x, int ldx, int M, int D, float eps, const float* shift, const float* scale,
             const __nv_bfloat16* w, const __nv_bfloat16* b, __nv_bfloat16* out, int ldo, cudaStream_t s) {
   return ln_dispatch<__nv_bfloat16>(x, ldx, M, D, eps, shift, scale, w, b, out, ldo, s);
+}
+int ln_f32_q8(const float* x, int ldx, int M, int D, float eps, const float* shift, const float* scale,
+              const __nv_bfloat16* w, const __nv_bfloat16* b, uint8_t* out8, float* sa, int ldo, cudaStream_t s) {
+  return ln_dispatch<float>(x, ldx, M, D, eps, shift, scale, w, b, nullptr, ldo, s, out8, sa);
+}
+int ln_bf16_q8(const __nv_bfloat16* x, int ldx, int M, int D, float eps, const float* shift, const float* scale,
+               const __nv_bfloat16* w, const __nv_bfloat16* b, uint8_t* out8, float* sa, int ldo, cudaStream_t s) {
+  return ln_dispatch<__nv_bfloat16>(x, ldx, M, D, eps, shift, scale, w, b, nullptr, ldo, s, out8, sa);
+}
+
+// ------------------------------------------------------------------ e4m3 row quantisation
+// q[row, :] = e4m3(x[row, :] / scale[row]), scale = absmax(x[row, :]) / 448 (1 for an all-zero row).
+// Per-token activation scales for the e4m3 GEMMs, and per-output-channel weight scales when
+// applied to a weight [N, K].  One warp per row, two passes (the second hits L1/L2).
+__global__ void __launch_bounds__(256) quant_rows_kernel(const __nv_bfloat16* __restrict__ x, int ldx, int M, int K,
+                                                         uint8_t* __restrict__ q, int ldq, float* __restrict__ scale) {
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (row >= M) return;
+  const __nv_bfloat16* xr = x + (size_t)row * ldx;
+  float amax = 0.f;
+  for (int c = lane * 8; c < K; c += 256) {
+    const uint4 u = *reinterpret_cast<const uint4*>(xr + c);
+    const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = unpack_bf16(w4[i]);
+      amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
+    }
+  }
+  amax = warp_max(amax);
+  const float sc = amax > 0.f ? amax * (1.f / 448.f) : 1.f;
+  const float inv = 1.f / sc;
+  for (int c = lane * 8; c < K; c += 256) {
+    const uint4 u = *reinterpret_cast<const uint4*>(xr + c);
+    const float2 a = unpack_bf16(u.x), b = unpack_bf16(u.y), cc = unpack_bf16(u.z), d = unpack_bf16(u.w);
+    *reinterpret_cast<uint2*>(q + (size_t)row * ldq + c) =
+        make_uint2(pack4_e4m3(a.x, a.y, b.x, b.y, inv), pack4_e4m3(cc.x, cc.y, d.x, d.y, inv));
+  }
+  if (lane == 0) scale[row] = sc;
+}
+int quant_rows(const __nv_bfloat16* x, int ldx, int M, int K, uint8_t* q, int ldq, float* scale, cudaStream_t s) {
+  if (K % 8 || ldx % 8 || ldq % 16) return FW_ESHAPE;
+  quant_rows_kernel<<<(M + 7) / 8, 256, 0, s>>>(x, ldx, M, K, q, ldq, scale);
+  note_launch();
+  return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
 }
 
 // ------------------------------------------------------------------ RMSNorm (+ RoPE)

@@ -67,6 +67,9 @@ struct fw_handle {
   __nv_bfloat16 *y, *xbf, *q, *kcur, *vcur, *ao, *hb, *hb2, *patchA, *xa, *xb, *den, *den_ctx, *ctx_a, *ctx_h,
       *ctx_o, *ctx, *ckv, *kbK, *kbV;
   int* consts;
+  bool fp8 = false;         // e4m3 block linears (per-channel weight / per-token activation scales)
+  uint8_t* a8 = nullptr;    // e4m3 operand of the next block linear
+  float* sa = nullptr;      // its per-row scales
   int* status;
   std::vector<fw::Layer> layers;
   fw::GemmOp patch, head, fc1, fc2;
@@ -182,6 +185,30 @@ static int register_tensors(fw_handle* h) {
       wt(a + "pkb.b", {D});
     }
   }
+  if (h->fp8) {   // e4m3 copies of the block linears, derived at fw_finalize
+    auto der = [&](const std::string& n, int64_t N, int64_t K) {
+      add_tensor(h, n + ".q8", FW_KIND_DERIVED, FW_U8, {N, K});
+      add_tensor(h, n + ".sw", FW_KIND_DERIVED, FW_F32, {N});
+    };
+    for (int i = 0; i < c.layers; ++i) {
+      const std::string p = "b" + std::to_string(i) + ".";
+      der(p + "sa.qkv", 3 * D, D);
+      der(p + "sa.o", D, D);
+      der(p + "ca.q", D, D);
+      der(p + "ca.o", D, D);
+      der(p + "ffn.0", FF, D);
+      der(p + "ffn.2", D, FF);
+      if (h->layers[i].act >= 0) {
+        const std::string a = p + "am.";
+        der(a + "mlp1", h->Mh, D);
+        der(a + "mlp2", h->Mh, h->Mh);
+        der(a + "tqkv", 3 * A, h->Mh);
+        der(a + "pmouse", D, A);
+        der(a + "mattq", A, D);
+        der(a + "pkb", D, A);
+      }
+    }
+  }
   // session state (static.py:47-54, 280-281)
   for (int i = 0; i < c.layers; ++i) add_tensor(h, "hk." + std::to_string(i), FW_KIND_STATE, FW_BF16, {1, h->L, h->H, h->HD});
   for (int i = 0; i < c.layers; ++i) add_tensor(h, "hv." + std::to_string(i), FW_KIND_STATE, FW_BF16, {1, h->L, h->H, h->HD});
@@ -244,6 +271,10 @@ static int register_tensors(fw_handle* h) {
   ws_add(h, "ee", (size_t)c.layers * 6 * D * f4);
   ws_add(h, "hmod", (size_t)2 * D * f4);
   ws_add(h, "consts", 64 * sizeof(int));
+  if (h->fp8) {
+    ws_add(h, "a8", (size_t)L * mx({D, FF, h->Mh, A}));
+    ws_add(h, "sa", (size_t)L * f4);
+  }
   h->ws_bytes = (h->ws_bytes + 1023) & ~(size_t)1023;
   add_tensor(h, "workspace", FW_KIND_WORKSPACE, FW_U8, {(int64_t)h->ws_bytes});
   return 0;
@@ -281,6 +312,12 @@ static int make_gemm(GemmOp& op, const void* A, int M, int K, int lda, const voi
 }
 static int run(const GemmOp& op, cudaStream_t s) { return gemm_bf16_launch(op.a, op.b, op.bn, op.args, s); }
 static int pick_bn(int N) { return N >= 256 ? 256 : (N >= 128 ? 128 : 64); }
+
+// A block linear `wname` (weight `wname.w` [N, ldb]) whose bf16 operand is A [M, lda].  With
+// e4m3 linears the GEMM instead reads the handle's e4m3 activation buffer (row stride K bytes,
+// per-row scales) and the derived per-channel-quantised weight `wname.q8` / `wname.sw`.
+static int make_lin(fw_handle* h, GemmOp& op, const std::string& wname, const void* A, int lda, int M, int K, int N,
+                    int ldb, int bn, const GemmEpi& epi);
 
 static GemmEpi epi_bf16(void* out, int ld, const __nv_bfloat16* bias, int mode = EPI_BF16) {
   GemmEpi e;
@@ -332,6 +369,37 @@ static int run(const AttnOp& op, cudaStream_t s) { return attention_launch(op.q,
     if (_rc) return _rc;  \
   } while (0)
 
+static int make_lin(fw_handle* h, GemmOp& op, const std::string& wname, const void* A, int lda, int M, int K, int N,
+                    int ldb, int bn, const GemmEpi& epi) {
+  if (!h->fp8) return make_gemm(op, A, M, K, lda, W(h, wname + ".w"), N, ldb, bn, epi, h->status);
+  op.bn = bn;
+  FW_TRY(make_tmap_2d(&op.a, h->a8, 1, M, K, K, 128, 128, true));
+  FW_TRY(make_tmap_2d(&op.b, P<uint8_t>(h, wname + ".q8"), 1, N, K, K, bn, 128, true));
+  op.args.M = M;
+  op.args.N = N;
+  op.args.K = K;
+  op.args.epi = epi;
+  op.args.sa = h->sa;
+  op.args.sw = P<float>(h, wname + ".sw");
+  op.args.status = h->status;
+  op.valid = true;
+  return gemm_check(op.args, bn);
+}
+
+// The operand of an e4m3 GEMM is quantised from `src` (bf16 [M, ld]) with per-token scales;
+// in bf16 mode the GEMM reads `src` directly and this only launches the GEMM.
+static int run_from(fw_handle* h, const GemmOp& op, const __nv_bfloat16* src, int ld, cudaStream_t s) {
+  if (h->fp8) FW_TRY(quant_rows(src, ld, op.args.M, op.args.K, h->a8, op.args.K, h->sa, s));
+  return run(op, s);
+}
+
+// LayerNorm of the fp32 residual into the next GEMM's operand (bf16 y, or e4m3 a8 + scales).
+static int ln_op(fw_handle* h, int M, int D, float eps, const float* shift, const float* scale,
+                 const __nv_bfloat16* w, const __nv_bfloat16* b, cudaStream_t s) {
+  if (h->fp8) return ln_f32_q8(h->xs, D, M, D, eps, shift, scale, w, b, h->a8, h->sa, D, s);
+  return ln_f32(h->xs, D, M, D, eps, shift, scale, w, b, h->y, D, s);
+}
+
 static int finalize(fw_handle* h) {
   for (auto& t : h->tensors)
     if (!t.ptr) return FW_ENOTBOUND;
@@ -378,6 +446,8 @@ static int finalize(fw_handle* h) {
   h->ee = (float*)WS("ee");
   h->hmod = (float*)WS("hmod");
   h->consts = (int*)WS("consts");
+  h->a8 = (uint8_t*)WS("a8");
+  h->sa = (float*)WS("sa");
   h->status = P<int>(h, "status");
   // constant device tables: attention segment lengths {first, steady, cross}
   int consts[8] = {0, h->L, h->L, h->L, h->Ctx, 0, 0, 0};
@@ -403,11 +473,11 @@ static int finalize(fw_handle* h) {
       e.out[1] = h->kcur;
       e.out[2] = h->vcur;
       e.seg_w = D;
-      FW_TRY(make_gemm(ly.qkv, h->y, L, D, D, W(h, p + "sa.qkv.w"), 3 * D, D, 256, e, st));
+      FW_TRY(make_lin(h, ly.qkv, p + "sa.qkv", h->y, D, L, D, 3 * D, D, 256, e));
     }
-    FW_TRY(make_gemm(ly.o, h->ao, L, D, D, W(h, p + "sa.o.w"), D, D, 256,
-                     epi_resid(h->xs, D, W(h, p + "sa.o.b"), ee + 2 * D, nullptr), st));
-    FW_TRY(make_gemm(ly.caq, h->y, L, D, D, W(h, p + "ca.q.w"), D, D, 256, epi_bf16(h->q, D, W(h, p + "ca.q.b")), st));
+    FW_TRY(make_lin(h, ly.o, p + "sa.o", h->ao, D, L, D, D, D, 256,
+                    epi_resid(h->xs, D, W(h, p + "sa.o.b"), ee + 2 * D, nullptr)));
+    FW_TRY(make_lin(h, ly.caq, p + "ca.q", h->y, D, L, D, D, D, 256, epi_bf16(h->q, D, W(h, p + "ca.q.b"))));
     {
       __nv_bfloat16* ck = h->ckv + (size_t)i * 2 * Ctx * D;
       GemmEpi e = epi_bf16(ck, D, W(h, p + "ca.kv.b"));
@@ -415,12 +485,12 @@ static int finalize(fw_handle* h) {
       e.seg_w = D;
       FW_TRY(make_gemm(ly.cakv, h->ctx, Ctx, D, D, W(h, p + "ca.kv.w"), 2 * D, D, 256, e, st));
     }
-    FW_TRY(make_gemm(ly.cao, h->ao, L, D, D, W(h, p + "ca.o.w"), D, D, 256,
-                     epi_resid(h->xs, D, W(h, p + "ca.o.b"), nullptr, ly.act >= 0 ? h->xbf : nullptr), st));
-    FW_TRY(make_gemm(ly.ff0, h->y, L, D, D, W(h, p + "ffn.0.w"), h->FF, D, 256,
-                     epi_bf16(h->hb, h->FF, W(h, p + "ffn.0.b"), EPI_GELU_BF16), st));
-    FW_TRY(make_gemm(ly.ff2, h->hb, L, h->FF, h->FF, W(h, p + "ffn.2.w"), D, h->FF, 256,
-                     epi_resid(h->xs, D, W(h, p + "ffn.2.b"), ee + 5 * D, nullptr), st));
+    FW_TRY(make_lin(h, ly.cao, p + "ca.o", h->ao, D, L, D, D, D, 256,
+                    epi_resid(h->xs, D, W(h, p + "ca.o.b"), nullptr, ly.act >= 0 ? h->xbf : nullptr)));
+    FW_TRY(make_lin(h, ly.ff0, p + "ffn.0", h->y, D, L, D, h->FF, D, 256,
+                    epi_bf16(h->hb, h->FF, W(h, p + "ffn.0.b"), EPI_GELU_BF16)));
+    FW_TRY(make_lin(h, ly.ff2, p + "ffn.2", h->hb, h->FF, L, h->FF, D, h->FF, 256,
+                    epi_resid(h->xs, D, W(h, p + "ffn.2.b"), ee + 5 * D, nullptr)));
     const void* hk = ptr_of(h, "hk." + std::to_string(i));
     const void* hv = ptr_of(h, "hv." + std::to_string(i));
     FW_TRY(make_attn(ly.self_first, h->q, L, h->H, hk, hv, L, h->kcur, h->vcur, L, h->consts + 0, h->ao, st));
@@ -438,18 +508,30 @@ static int finalize(fw_handle* h) {
       e1.fbias = h->fbias;
       e1.fbias_stride = Mh;
       e1.rows_per_frame = h->S;
-      FW_TRY(make_gemm(ly.mlp1, h->xbf, L, D, D, W(h, a + "mlp1.w"), Mh, K1, pick_bn(Mh), e1, st));
-      FW_TRY(make_gemm(ly.mlp2, h->hb, L, Mh, Mh, W(h, a + "mlp2.w"), Mh, Mh, pick_bn(Mh),
-                       epi_bf16(h->hb2, Mh, W(h, a + "mlp2.b")), st));
-      FW_TRY(make_gemm(ly.tqkv, h->y, L, Mh, Mh, W(h, a + "tqkv.w"), 3 * A, Mh, pick_bn(3 * A),
-                       epi_bf16(h->hb, 3 * A, W(h, a + "tqkv.b")), st));
-      FW_TRY(make_gemm(ly.pmouse, h->ao, L, A, A, W(h, a + "pmouse.w"), D, A, 256,
-                       epi_resid(h->xs, D, W(h, a + "pmouse.b"), nullptr, h->xbf), st));
-      FW_TRY(make_gemm(ly.mattq, h->xbf, L, D, D, W(h, a + "mattq.w"), A, D, pick_bn(A),
-                       epi_bf16(h->hb2, A, W(h, a + "mattq.b")), st));
-      FW_TRY(make_gemm(ly.pkb, h->ao, L, A, A, W(h, a + "pkb.w"), D, A, 256,
-                       epi_resid(h->xs, D, W(h, a + "pkb.b"), nullptr, nullptr), st));
+      FW_TRY(make_lin(h, ly.mlp1, a + "mlp1", h->xbf, D, L, D, Mh, K1, pick_bn(Mh), e1));
+      FW_TRY(make_lin(h, ly.mlp2, a + "mlp2", h->hb, Mh, L, Mh, Mh, Mh, pick_bn(Mh),
+                      epi_bf16(h->hb2, Mh, W(h, a + "mlp2.b"))));
+      FW_TRY(make_lin(h, ly.tqkv, a + "tqkv", h->y, Mh, L, Mh, 3 * A, Mh, pick_bn(3 * A),
+                      epi_bf16(h->hb, 3 * A, W(h, a + "tqkv.b"))));
+      FW_TRY(make_lin(h, ly.pmouse, a + "pmouse", h->ao, A, L, A, D, A, 256,
+                      epi_resid(h->xs, D, W(h, a + "pmouse.b"), nullptr, h->xbf)));
+      FW_TRY(make_lin(h, ly.mattq, a + "mattq", h->xbf, D, L, D, A, D, pick_bn(A),
+                      epi_bf16(h->hb2, A, W(h, a + "mattq.b"))));
+      FW_TRY(make_lin(h, ly.pkb, a + "pkb", h->ao, A, L, A, D, A, 256,
+                      epi_resid(h->xs, D, W(h, a + "pkb.b"), nullptr, nullptr)));
     }
+  }
+  if (h->fp8) {   // derive the per-output-channel e4m3 weights of every block linear
+    for (auto& t : h->tensors) {
+      if (t.kind != FW_KIND_DERIVED || t.name.size() < 3 || t.name.compare(t.name.size() - 3, 3, ".q8")) continue;
+      const std::string base = t.name.substr(0, t.name.size() - 3);
+      const int idx = h->index[base + ".w"];
+      const Tensor& w = h->tensors[idx];
+      const int N = (int)t.shape[0], K = (int)t.shape[1];
+      FW_TRY(quant_rows(reinterpret_cast<const __nv_bfloat16*>(w.ptr), (int)w.shape[1], N, K,
+                        reinterpret_cast<uint8_t*>(t.ptr), K, P<float>(h, base + ".sw"), 0));
+    }
+    if (cudaDeviceSynchronize() != cudaSuccess) return FW_ECUDA;
   }
   h->finalized = true;
   return 0;
@@ -500,14 +582,19 @@ static int action(fw_handle* h, int i, int first, int write, cudaStream_t s) {
   // mouse window contribution of mouse_mlp[0], one row per frame: b + gm_f . W[:, D:]
   FW_TRY(smallm_linear_bf16(P<__nv_bfloat16>(h, "gm"), c.mouse_dim * h->PAD, h->F, W(h, a + "mlp1.w") + D, K1,
                             W(h, a + "mlp1.b"), Mh, c.mouse_dim * h->PAD, ACT_NONE, ACT_NONE, h->fbias, nullptr, Mh, s));
-  FW_TRY(run(ly.mlp1, s));
-  FW_TRY(run(ly.mlp2, s));
-  FW_TRY(ln_bf16(h->hb2, Mh, h->L, Mh, c.eps_ln, nullptr, nullptr, W(h, a + "mln.w"), W(h, a + "mln.b"), h->y, Mh, s));
+  FW_TRY(run_from(h, ly.mlp1, h->xbf, D, s));
+  FW_TRY(run_from(h, ly.mlp2, h->hb, Mh, s));
+  if (h->fp8)
+    FW_TRY(ln_bf16_q8(h->hb2, Mh, h->L, Mh, c.eps_ln, nullptr, nullptr, W(h, a + "mln.w"), W(h, a + "mln.b"), h->a8,
+                      h->sa, Mh, s));
+  else
+    FW_TRY(ln_bf16(h->hb2, Mh, h->L, Mh, c.eps_ln, nullptr, nullptr, W(h, a + "mln.w"), W(h, a + "mln.b"), h->y, Mh,
+                   s));
   FW_TRY(run(ly.tqkv, s));
   FW_TRY(mouse_attn(h->hb, W(h, a + "mqn.w"), W(h, a + "mkn.w"), h->acos_, h->asin_, P<__nv_bfloat16>(h, "mk." + si),
                     P<__nv_bfloat16>(h, "mv." + si), first, write, h->ao, h->S, h->F, h->AH, c.eps, s));
-  FW_TRY(run(ly.pmouse, s));
-  FW_TRY(run(ly.mattq, s));
+  FW_TRY(run_from(h, ly.pmouse, h->ao, A, s));
+  FW_TRY(run_from(h, ly.mattq, h->xbf, D, s));
   const __nv_bfloat16* kc = h->kbK + (size_t)ly.act * h->F * A;
   const __nv_bfloat16* vc = h->kbV + (size_t)ly.act * h->F * A;
   FW_TRY(kb_attn(h->hb2, W(h, a + "kqn.w"), h->acos_, h->asin_, P<__nv_bfloat16>(h, "kk." + si),
@@ -516,7 +603,7 @@ static int action(fw_handle* h, int i, int first, int write, cudaStream_t s) {
     FW_TRY(copy_bytes(ptr_of(h, "kk." + si), kc, (size_t)h->F * A * 2, s));
     FW_TRY(copy_bytes(ptr_of(h, "kv." + si), vc, (size_t)h->F * A * 2, s));
   }
-  FW_TRY(run(ly.pkb, s));
+  FW_TRY(run_from(h, ly.pkb, h->ao, A, s));
   return 0;
 }
 
@@ -546,7 +633,7 @@ static int forward(fw_handle* h, int step, int first, int write, const __nv_bflo
     const Layer& ly = h->layers[i];
     const std::string p = "b" + std::to_string(i) + ".";
     const float* ee = h->ee + (size_t)i * 6 * D;
-    FW_TRY(ln_f32(h->xs, D, L, D, c.eps, ee + 0 * D, ee + 1 * D, nullptr, nullptr, h->y, D, s));
+    FW_TRY(ln_op(h, L, D, c.eps, ee + 0 * D, ee + 1 * D, nullptr, nullptr, s));
     FW_TRY(run(ly.qkv, s));
     FW_TRY(rms_rope2(h->q, W(h, p + "sa.nq.w"), h->q, h->kcur, W(h, p + "sa.nk.w"), h->kcur, D, L, D, c.eps, rope,
                      h->HD, D, s));
@@ -555,16 +642,16 @@ static int forward(fw_handle* h, int step, int first, int write, const __nv_bflo
       FW_TRY(copy_bytes(ptr_of(h, "hk." + std::to_string(i)), h->kcur, (size_t)L * D * 2, s));
       FW_TRY(copy_bytes(ptr_of(h, "hv." + std::to_string(i)), h->vcur, (size_t)L * D * 2, s));
     }
-    FW_TRY(run(ly.o, s));
-    FW_TRY(ln_f32(h->xs, D, L, D, c.eps, nullptr, nullptr, W(h, p + "n3.w"), W(h, p + "n3.b"), h->y, D, s));
+    FW_TRY(run_from(h, ly.o, h->ao, D, s));
+    FW_TRY(ln_op(h, L, D, c.eps, nullptr, nullptr, W(h, p + "n3.w"), W(h, p + "n3.b"), s));
     FW_TRY(run(ly.caq, s));
     FW_TRY(rms_rope(h->q, D, L, D, c.eps, W(h, p + "ca.nq.w"), nullptr, h->HD, h->q, D, s));
     FW_TRY(run(ly.cross, s));
-    FW_TRY(run(ly.cao, s));
+    FW_TRY(run_from(h, ly.cao, h->ao, D, s));
     if (ly.act >= 0) FW_TRY(action(h, i, first, write, s));
-    FW_TRY(ln_f32(h->xs, D, L, D, c.eps, ee + 3 * D, ee + 4 * D, nullptr, nullptr, h->y, D, s));
+    FW_TRY(ln_op(h, L, D, c.eps, ee + 3 * D, ee + 4 * D, nullptr, nullptr, s));
     FW_TRY(run(ly.ff0, s));
-    FW_TRY(run(ly.ff2, s));
+    FW_TRY(run_from(h, ly.ff2, h->hb, h->FF, s));
   }
   FW_TRY(ln_f32(h->xs, D, L, D, c.eps, h->hmod, h->hmod + D, nullptr, nullptr, h->y, D, s));
   FW_TRY(run(h->head, s));
@@ -640,6 +727,7 @@ int fw_create(const fw_config* cfg, fw_handle** out) {
   h->PAD = c.time_ratio * c.window;
   h->KC = c.frames * c.time_ratio + h->PAD - 3;
   h->lat_elems = (size_t)c.lat_ch * c.frames * c.lat_h * c.lat_w;
+  h->fp8 = c.linear_fp8 != 0;
   h->layers.resize(c.layers);
   for (int j = 0; j < c.n_action; ++j) h->layers[c.action_blocks[j]].act = j;
   fw::register_tensors(h);

@@ -10,6 +10,13 @@ int ln_f32(const float* x, int ldx, int M, int D, float eps, const float* shift,
            const __nv_bfloat16* w, const __nv_bfloat16* b, __nv_bfloat16* out, int ldo, cudaStream_t s);
 int ln_bf16(const __nv_bfloat16* x, int ldx, int M, int D, float eps, const float* shift, const float* scale,
             const __nv_bfloat16* w, const __nv_bfloat16* b, __nv_bfloat16* out, int ldo, cudaStream_t s);
+// LayerNorm with e4m3 output and per-row scales (out8 row stride ldo bytes).
+int ln_f32_q8(const float* x, int ldx, int M, int D, float eps, const float* shift, const float* scale,
+              const __nv_bfloat16* w, const __nv_bfloat16* b, uint8_t* out8, float* sa, int ldo, cudaStream_t s);
+int ln_bf16_q8(const __nv_bfloat16* x, int ldx, int M, int D, float eps, const float* shift, const float* scale,
+               const __nv_bfloat16* w, const __nv_bfloat16* b, uint8_t* out8, float* sa, int ldo, cudaStream_t s);
+// bf16 rows -> e4m3 rows + per-row scale absmax / 448.
+int quant_rows(const __nv_bfloat16* x, int ldx, int M, int K, uint8_t* q, int ldq, float* scale, cudaStream_t s);
 int rms_rope(const __nv_bfloat16* x, int ldx, int M, int D, float eps, const __nv_bfloat16* w, const float2* rope,
              int hd, __nv_bfloat16* out, int ldo, cudaStream_t s);
 // Two tensors of the same shape in one launch (x2 may be null).

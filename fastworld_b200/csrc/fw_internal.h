@@ -51,6 +51,10 @@ struct GemmEpi {
 struct GemmArgs {
   int M = 0, N = 0, K = 0;
   GemmEpi epi;
+  // e4m3 operands (A and B are bytes) when sa != null: sa[M] per-row activation scales,
+  // sw[N] per-column (output channel) weight scales; acc is multiplied by sa[row] * sw[col].
+  const float* sa = nullptr;
+  const float* sw = nullptr;
   int* status = nullptr;
 };
 

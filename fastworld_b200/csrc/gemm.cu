@@ -28,7 +28,7 @@ struct GemmCfg {
   static constexpr int STAGE = A_BYTES + B_BYTES;
   static constexpr int STAGES = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int SMEM = STAGES * STAGE + 256 + 8 * 4096 + 1024;   // stages, barriers, epilogue staging, align
+  static constexpr int SMEM = STAGES * STAGE + 1024 + 256;
 };
 
 __device__ __forceinline__ void add_bias(const GemmEpi& e, int frame, int col0, float (&v)[32]) {
@@ -60,67 +60,63 @@ __device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float (&
                        pack_bf16(v[8 * j + 4], v[8 * j + 5]), pack_bf16(v[8 * j + 6], v[8 * j + 7]));
 }
 
-// One 32 x 32 chunk of the output tile per warp (thread `lane` holds row row0 + lane, columns
-// col0 .. col0 + 31 in r).  Bias and activation are applied per thread; the chunk is then
-// staged through the warp's 4 KB shared-memory buffer (16-byte granules XOR-swizzled by row so
-// both phases are bank-conflict free) and written out row-contiguously: each warp instruction
-// covers 4 rows x 128 bytes, so the fp32 residual read-modify-write and the stores move whole
-// cache lines instead of 32 scattered 16-byte pieces.
-__device__ __forceinline__ void epilogue_chunk(const GemmEpi& e, int row0, int M, int col0, const uint32_t (&r)[32],
-                                               float4* stage, int lane) {
+__device__ __forceinline__ void epilogue_chunk(const GemmEpi& e, int row, int col0, const uint32_t (&r)[32],
+                                               const float* __restrict__ sa, const float* __restrict__ sw) {
   float v[32];
 #pragma unroll
   for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-  const int my_row = row0 + lane;
-  add_bias(e, (my_row < M ? my_row : 0) / e.rows_per_frame, col0, v);
-  if (e.mode == EPI_GELU_BF16) {
+  if (sa) {   // e4m3 operands: dequantise with the row's activation scale and each column's weight scale
+    const float ra = __ldg(sa + row);
+    const float4* w4 = reinterpret_cast<const float4*>(sw + col0);
 #pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
-  } else if (e.mode == EPI_GELU_ERF_BF16) {
-#pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = 0.5f * v[j] * (1.f + erff(v[j] * 0.7071067811865476f));
-  }
-  __syncwarp();
-#pragma unroll
-  for (int k = 0; k < 8; ++k)
-    stage[lane * 8 + (k ^ (lane & 7))] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
-  __syncwarp();
-  const int k = lane & 7;                    // this lane's 4 columns: col0 + 4k .. +3
-  const int col = col0 + 4 * k;
-#pragma unroll
-  for (int it = 0; it < 8; ++it) {
-    const int rr = it * 4 + (lane >> 3);     // row within the chunk
-    const int grow = row0 + rr;
-    if (grow >= M) continue;
-    float4 a = stage[rr * 8 + (k ^ (rr & 7))];
-    if (e.mode == EPI_RESID_F32) {
-      float4* rp = reinterpret_cast<float4*>(e.resid + (size_t)grow * e.ld_resid + col);
-      float4 x = *rp;
-      if (e.gate) {
-        const float4 g = __ldg(reinterpret_cast<const float4*>(e.gate + (size_t)(grow / e.rows_per_frame) * e.gate_stride + col));
-        x.x += g.x * a.x; x.y += g.y * a.y; x.z += g.z * a.z; x.w += g.w * a.w;
-      } else {
-        x.x += a.x; x.y += a.y; x.z += a.z; x.w += a.w;
-      }
-      *rp = x;
-      if (e.mirror)
-        *reinterpret_cast<uint2*>(e.mirror + (size_t)grow * e.ld_mirror + col) =
-            make_uint2(pack_bf16(x.x, x.y), pack_bf16(x.z, x.w));
-    } else if (e.mode == EPI_F32) {
-      *reinterpret_cast<float4*>(reinterpret_cast<float*>(e.out[0]) + (size_t)grow * e.ld_out + col) = a;
-    } else {
-      const int seg = col0 / e.seg_w;
-      __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(e.out[seg]) + (size_t)grow * e.ld_out + (col - seg * e.seg_w);
-      *reinterpret_cast<uint2*>(dst) = make_uint2(pack_bf16(a.x, a.y), pack_bf16(a.z, a.w));
+    for (int j = 0; j < 8; ++j) {
+      const float4 w = __ldg(w4 + j);
+      v[4 * j + 0] *= ra * w.x; v[4 * j + 1] *= ra * w.y; v[4 * j + 2] *= ra * w.z; v[4 * j + 3] *= ra * w.w;
     }
+  }
+  const int frame = row / e.rows_per_frame;
+  add_bias(e, frame, col0, v);
+  if (e.mode == EPI_BF16 || e.mode == EPI_GELU_BF16 || e.mode == EPI_GELU_ERF_BF16) {
+    if (e.mode == EPI_GELU_BF16) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
+    } else if (e.mode == EPI_GELU_ERF_BF16) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = 0.5f * v[j] * (1.f + erff(v[j] * 0.7071067811865476f));
+    }
+    const int seg = col0 / e.seg_w;
+    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(e.out[seg]) + (size_t)row * e.ld_out + (col0 - seg * e.seg_w);
+    store_bf16x32(dst, v);
+  } else if (e.mode == EPI_F32) {
+    float4* d4 = reinterpret_cast<float4*>(reinterpret_cast<float*>(e.out[0]) + (size_t)row * e.ld_out + col0);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) d4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+  } else {   // EPI_RESID_F32
+    float4* rp = reinterpret_cast<float4*>(e.resid + (size_t)row * e.ld_resid + col0);
+    const float4* gp = e.gate ? reinterpret_cast<const float4*>(e.gate + (size_t)frame * e.gate_stride + col0) : nullptr;
+    float4 x[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) x[j] = rp[j];   // all eight loads in flight before the math
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float4 g = gp ? __ldg(gp + j) : make_float4(1.f, 1.f, 1.f, 1.f);
+      x[j].x += g.x * v[4 * j + 0]; x[j].y += g.y * v[4 * j + 1]; x[j].z += g.z * v[4 * j + 2]; x[j].w += g.w * v[4 * j + 3];
+      rp[j] = x[j];
+      v[4 * j + 0] = x[j].x; v[4 * j + 1] = x[j].y; v[4 * j + 2] = x[j].z; v[4 * j + 3] = x[j].w;
+    }
+    if (e.mirror) store_bf16x32(e.mirror + (size_t)row * e.ld_mirror + col0, v);
   }
 }
 
-template <int BN>
+// F8 = false: bf16 operands, kind::f16, 64 elements (128 bytes) of K per stage.
+// F8 = true:  e4m3 operands, kind::f8f6f4, 128 elements (128 bytes) of K per stage; the same
+//             128-byte-swizzled smem tiles and descriptors, 32 bytes of K per MMA instruction.
+template <int BN, bool F8>
 __global__ void __launch_bounds__(320, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const GemmArgs args) {
   using C = GemmCfg<BN>;
+  constexpr int KE = F8 ? 128 : 64;   // K elements per stage
   extern __shared__ uint8_t smem_raw[];
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
   uint8_t* smem = smem_raw + pad;
@@ -134,11 +130,9 @@ __global__ void __launch_bounds__(320, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // per-epilogue-warp 4 KB staging buffers for coalesced output (after the 256-byte barrier area)
-  float4* stage = reinterpret_cast<float4*>(smem + C::STAGES * C::STAGE + 256) + (warp >= 2 ? (warp - 2) * 256 : 0);
   const int M = args.M, N = args.N, K = args.K;
   const int num_m = (M + 127) / 128, num_n = (N + BN - 1) / BN;
-  const int num_tiles = num_m * num_n, num_kb = (K + 63) / 64;
+  const int num_tiles = num_m * num_n, num_kb = (K + KE - 1) / KE;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
@@ -179,8 +173,8 @@ __global__ void __launch_bounds__(320, 1)
             break;
           }
           mbar_arrive_expect_tx(full + stage, C::STAGE);
-          tma_load_2d(sA + stage * C::A_BYTES, &tmA, full + stage, kb * 64, mb * 128);
-          tma_load_2d(sB + stage * C::B_BYTES, &tmB, full + stage, kb * 64, nb * BN);
+          tma_load_2d(sA + stage * C::A_BYTES, &tmA, full + stage, kb * KE, mb * 128);
+          tma_load_2d(sB + stage * C::B_BYTES, &tmB, full + stage, kb * KE, nb * BN);
           used |= 1u << stage;
           last_par = (last_par & ~(1u << stage)) | (phase << stage);
           if (++stage == C::STAGES) {
@@ -196,7 +190,7 @@ __global__ void __launch_bounds__(320, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16(128, BN, false, false);
+      constexpr uint32_t idesc = F8 ? idesc_e4m3(128, BN) : idesc_bf16(128, BN, false, false);
       int stage = 0, acc = 0;
       uint32_t phase = 0, acc_phase = 0;
       bool ok = true;
@@ -213,7 +207,11 @@ __global__ void __launch_bounds__(320, 1)
           const uint32_t a0 = smem_u32(sA + stage * C::A_BYTES), b0 = smem_u32(sB + stage * C::B_BYTES);
 #pragma unroll
           for (int k = 0; k < 4; ++k)
-            umma_bf16(d, sdesc_sw128(a0 + k * 32, 16, 1024), sdesc_sw128(b0 + k * 32, 16, 1024), idesc,
+            if constexpr (F8)
+              umma_f8(d, sdesc_sw128(a0 + k * 32, 16, 1024), sdesc_sw128(b0 + k * 32, 16, 1024), idesc,
+                      (kb | k) != 0);
+            else
+              umma_bf16(d, sdesc_sw128(a0 + k * 32, 16, 1024), sdesc_sw128(b0 + k * 32, 16, 1024), idesc,
                       (kb | k) != 0);
           umma_commit(empty + stage);
           if (++stage == C::STAGES) {
@@ -258,10 +256,12 @@ __global__ void __launch_bounds__(320, 1)
       tmem_ld_wait();
       tc_fence_before();
       mbar_arrive(tempty + acc);                 // the accumulator buffer is free again
+      if (row < M) {
 #pragma unroll
-      for (int c = 0; c < NC; ++c) {
-        const int col0 = colh + c * 32;
-        if (col0 < N) epilogue_chunk(args.epi, row - lane, M, col0, r[c], stage, lane);
+        for (int c = 0; c < NC; ++c) {
+          const int col0 = colh + c * 32;
+          if (col0 < N) epilogue_chunk(args.epi, row, col0, r[c], F8 ? args.sa : nullptr, args.sw);
+        }
       }
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
@@ -278,7 +278,8 @@ int gemm_check(const GemmArgs& a, int bn) {
   const GemmEpi& e = a.epi;
   if (a.M <= 0 || a.N <= 0 || a.K <= 0) return FW_EINVAL;
   if (bn != 64 && bn != 128 && bn != 256) return FW_EINVAL;
-  if (a.N % 32 || a.K % 8) return FW_ESHAPE;
+  if (a.N % 32 || a.K % (a.sa ? 16 : 8)) return FW_ESHAPE;
+  if (a.sa && (!a.sw || (reinterpret_cast<uintptr_t>(a.sw) & 15u))) return FW_EALIGN;
   auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
   if (e.bias && !al16(e.bias)) return FW_EALIGN;
   if (e.fbias && (!al16(e.fbias) || e.fbias_stride % 4)) return FW_EALIGN;
@@ -308,12 +309,13 @@ int gemm_check(const GemmArgs& a, int bn) {
   return 0;
 }
 
-template <int BN>
+template <int BN, bool F8>
 static int launch_bn(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmArgs& a, cudaStream_t s, int grid) {
   using C = GemmCfg<BN>;
-  cudaError_t err = cudaFuncSetAttribute(gemm_bf16_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+  cudaError_t err =
+      cudaFuncSetAttribute(gemm_bf16_kernel<BN, F8>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (err != cudaSuccess) return FW_ECUDA;
-  gemm_bf16_kernel<BN><<<grid, 320, C::SMEM, s>>>(tmA, tmB, a);
+  gemm_bf16_kernel<BN, F8><<<grid, 320, C::SMEM, s>>>(tmA, tmB, a);
   note_launch();
   return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
 }
@@ -326,9 +328,9 @@ int gemm_bf16_launch(const CUtensorMap& tmA, const CUtensorMap& tmB, int bn, con
   int grid = ctas > 0 ? ctas : num_sms();
   if (grid > tiles) grid = tiles;
   switch (bn) {
-    case 256: return launch_bn<256>(tmA, tmB, a, s, grid);
-    case 128: return launch_bn<128>(tmA, tmB, a, s, grid);
-    default: return launch_bn<64>(tmA, tmB, a, s, grid);
+    case 256: return a.sa ? launch_bn<256, true>(tmA, tmB, a, s, grid) : launch_bn<256, false>(tmA, tmB, a, s, grid);
+    case 128: return a.sa ? launch_bn<128, true>(tmA, tmB, a, s, grid) : launch_bn<128, false>(tmA, tmB, a, s, grid);
+    default: return a.sa ? launch_bn<64, true>(tmA, tmB, a, s, grid) : launch_bn<64, false>(tmA, tmB, a, s, grid);
   }
 }
 

@@ -3,6 +3,7 @@
 #include <cmath>
 
 #include "../../include/fastworld_b200.h"
+#include "fw_elem.h"
 #include "fw_internal.h"
 
 namespace fw {
@@ -78,6 +79,38 @@ int fw_gemm_bf16(const void* A, const void* B, const void* bias, void* out, int 
   a.epi.seg_w = 1 << 30;
   a.epi.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
   return gemm_bf16_launch(ta, tb, bn, a, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int fw_gemm_e4m3(const void* A8, const float* sa, const void* B8, const float* sw, const void* bias, void* out,
+                 int M, int N, int K, int epilogue, int tile_n, void* stream) {
+  using namespace fw;
+  if (!A8 || !sa || !B8 || !sw || !out) return FW_EINVAL;
+  if (epilogue != EPI_BF16 && epilogue != EPI_GELU_BF16 && epilogue != EPI_F32 && epilogue != EPI_GELU_ERF_BF16)
+    return FW_EINVAL;
+  const int bn = tile_n > 0 ? tile_n : (N >= 256 ? 256 : (N >= 128 ? 128 : 64));
+  if (bn != 64 && bn != 128 && bn != 256) return FW_EINVAL;
+  CUtensorMap ta, tb;
+  int rc = make_tmap_2d(&ta, A8, 1, M, K, K, 128, 128, true);
+  if (!rc) rc = make_tmap_2d(&tb, B8, 1, N, K, K, bn, 128, true);
+  if (rc) return rc;
+  GemmArgs a;
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.sa = sa;
+  a.sw = sw;
+  a.epi.mode = epilogue;
+  a.epi.out[0] = out;
+  a.epi.ld_out = N;
+  a.epi.seg_w = 1 << 30;
+  a.epi.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
+  return gemm_bf16_launch(ta, tb, bn, a, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int fw_quant_e4m3(const void* x, int M, int K, void* q, float* scale, void* stream) {
+  if (!x || !q || !scale || M <= 0 || K <= 0) return FW_EINVAL;
+  return fw::quant_rows(reinterpret_cast<const __nv_bfloat16*>(x), K, M, K, reinterpret_cast<uint8_t*>(q), K, scale,
+                        reinterpret_cast<cudaStream_t>(stream));
 }
 
 int fw_gemm_bf16_resid(const void* A, const void* B, const void* bias, float* resid, const float* gate,

@@ -33,6 +33,30 @@ def gemm(a: torch.Tensor, b: torch.Tensor, bias=None, epilogue: str = "none", ti
     return out
 
 
+def quant_e4m3(x: torch.Tensor):
+    """Per-row e4m3 quantisation: returns (q [M, K] uint8 e4m3 bits, scale [M] fp32)."""
+    _req(x, torch.bfloat16, "x")
+    M, K = x.shape
+    q = torch.empty(M, K, device=x.device, dtype=torch.uint8)
+    sc = torch.empty(M, device=x.device, dtype=torch.float32)
+    check(lib().fw_quant_e4m3(ptr(x), M, K, ptr(q), ptr(sc), stream_ptr()), "quant_e4m3")
+    return q, sc
+
+
+def gemm_e4m3(a8: torch.Tensor, sa: torch.Tensor, b8: torch.Tensor, sw: torch.Tensor, bias=None,
+              epilogue: str = "none", tile_n: int = 0) -> torch.Tensor:
+    """(a8 [M, K] e4m3 * sa[M]) @ (b8 [N, K] e4m3 * sw[N])^T (+ bias), fp32 accumulation."""
+    for n, t, d in (("a8", a8, torch.uint8), ("b8", b8, torch.uint8), ("sa", sa, torch.float32),
+                    ("sw", sw, torch.float32)):
+        _req(t, d, n)
+    M, K = a8.shape
+    N = b8.shape[0]
+    out = torch.empty(M, N, device=a8.device, dtype=torch.float32 if epilogue == "f32" else torch.bfloat16)
+    check(lib().fw_gemm_e4m3(ptr(a8), ptr(sa), ptr(b8), ptr(sw), ptr(bias), ptr(out), M, N, K, EPILOGUES[epilogue],
+                             tile_n, stream_ptr()), "gemm_e4m3")
+    return out
+
+
 def gemm_resid_(resid: torch.Tensor, a: torch.Tensor, b: torch.Tensor, bias=None, gate=None,
                 rows_per_frame: int = 1 << 30) -> torch.Tensor:
     """resid (fp32, in place) += gate[row // rows_per_frame] * (a @ b^T + bias)."""

@@ -50,6 +50,7 @@ extern "C" {
 #define FW_KIND_OUTPUT 3
 #define FW_KIND_WORKSPACE 4
 #define FW_KIND_STATUS 5
+#define FW_KIND_DERIVED 6   /* filled by fw_finalize from the weights (e4m3 copies, scales) */
 
 /* dtypes */
 #define FW_BF16 0
@@ -73,6 +74,7 @@ typedef struct fw_config {
   float eps;                                          /* block LayerNorm / RMSNorm eps */
   float eps_ln;                                       /* img_emb / mouse_mlp LayerNorm eps */
   float rope_theta;
+  int linear_fp8;                                     /* 1: block linears in e4m3 */
 } fw_config;
 
 typedef struct fw_tensor_info {
@@ -119,6 +121,12 @@ int fw_copy(void* dst, const void* src, size_t bytes, void* stream);
  * epilogue: 0 = store bf16, 1 = GELU(tanh) then bf16, 3 = store fp32 (out is float*). */
 int fw_gemm_bf16(const void* A, const void* B, const void* bias, void* out, int M, int N, int K, int epilogue,
                  int tile_n, void* stream);
+/* e4m3 operands (A8 [M,K], B8 [N,K] bytes, K % 16 == 0): C = (A8 B8^T) * sa[row] * sw[col] (+ bias),
+ * fp32 accumulate; epilogues as fw_gemm_bf16.  BASELINE configs[2]. */
+int fw_gemm_e4m3(const void* A8, const float* sa, const void* B8, const float* sw, const void* bias, void* out,
+                 int M, int N, int K, int epilogue, int tile_n, void* stream);
+/* Per-row e4m3 quantisation of bf16 x [M,K]: scale[row] = absmax / 448, q = e4m3(x / scale). */
+int fw_quant_e4m3(const void* x, int M, int K, void* q, float* scale, void* stream);
 /* resid[M,N] (fp32) += gate[row / rows_per_frame, N] * (A B^T + bias); gate may be NULL. */
 int fw_gemm_bf16_resid(const void* A, const void* B, const void* bias, float* resid, const float* gate,
                        int rows_per_frame, int M, int N, int K, void* stream);
