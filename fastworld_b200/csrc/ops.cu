@@ -1,6 +1,7 @@
 // Host utilities (TMA descriptors, device queries) and the op-level C ABI entry points.
 #include <atomic>
 #include <cmath>
+#include <cstring>
 
 #include "../../include/fastworld_b200.h"
 #include "fw_elem.h"
@@ -105,6 +106,40 @@ int fw_gemm_e4m3(const void* A8, const float* sa, const void* B8, const float* s
   a.epi.seg_w = 1 << 30;
   a.epi.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
   return gemm_bf16_launch(ta, tb, bn, a, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int fw_ipc_get_handle(const void* ptr, void* handle, size_t* offset) {
+  typedef CUresult (*PFN_range)(CUdeviceptr*, size_t*, CUdeviceptr);
+  static PFN_range range = nullptr;
+  if (!ptr || !handle || !offset) return FW_EINVAL;
+  if (!range) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return FW_ENODRIVER;
+    range = reinterpret_cast<PFN_range>(p);
+  }
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS) return FW_EINVAL;
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)) != cudaSuccess) return FW_ECUDA;
+  memcpy(handle, &h, sizeof(h));
+  *offset = (size_t)(reinterpret_cast<uintptr_t>(ptr) - (uintptr_t)base);
+  return 0;
+}
+
+int fw_ipc_open(const void* handle, void** ptr) {
+  if (!handle || !ptr) return FW_EINVAL;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  return cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess ? 0 : FW_ECUDA;
+}
+
+int fw_ipc_close(void* ptr) {
+  if (!ptr) return FW_EINVAL;
+  return cudaIpcCloseMemHandle(ptr) == cudaSuccess ? 0 : FW_ECUDA;
 }
 
 int fw_quant_e4m3(const void* x, int M, int K, void* q, float* scale, void* stream) {

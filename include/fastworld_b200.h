@@ -116,6 +116,15 @@ void fw_destroy(fw_handle* h);
  * peer GPU's memory when peer access is enabled. */
 int fw_copy(void* dst, const void* src, size_t bytes, void* stream);
 
+/* Export the cudaMalloc allocation that contains `ptr`: its 64-byte IPC handle and the byte
+ * offset of `ptr` inside it (for fw_ipc_open in another process). */
+int fw_ipc_get_handle(const void* ptr, void* handle, size_t* offset);
+/* Map another process's device allocation (a 64-byte cudaIpcMemHandle_t of its base) into the
+ * CURRENT device's address space with peer access enabled, so kernels on this GPU (fw_copy) can
+ * read it over NVLink; close it with fw_ipc_close once the copy has completed. */
+int fw_ipc_open(const void* handle, void** ptr);
+int fw_ipc_close(void* ptr);
+
 /* ---- individual kernels (used by the engine; exported for tests and reuse) ---- */
 /* C[M,N] = A[M,K] B[N,K]^T (+ bias[N]) with A, B, C bf16 row-major, fp32 accumulate.
  * epilogue: 0 = store bf16, 1 = GELU(tanh) then bf16, 3 = store fp32 (out is float*). */
