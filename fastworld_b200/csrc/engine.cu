@@ -695,6 +695,7 @@ const char* fw_strerror(int code) {
     case FW_ENODRIVER: return "cuTensorMapEncodeTiled unavailable (driver entry point)";
     case FW_ESTATE: return "call out of order (finalize first / already finalized)";
     case FW_ESIZE: return "bound buffer smaller than required";
+    case FW_ESCRATCH: return "problem exceeds the fixed scratch of fw_linear_e4m3_noalloc (M*K <= 32 MiB, M <= 16384)";
     default: return "unknown error";
   }
 }

@@ -42,6 +42,7 @@ extern "C" {
 #define FW_ENODRIVER (-6)   /* cuTensorMapEncodeTiled unavailable */
 #define FW_ESTATE (-7)      /* call out of order (e.g. launch before fw_finalize) */
 #define FW_ESIZE (-8)       /* bound buffer smaller than required */
+#define FW_ESCRATCH (-9)    /* problem larger than the fixed scratch of fw_linear_e4m3_noalloc */
 
 /* tensor kinds (fw_tensor_info.kind) */
 #define FW_KIND_WEIGHT 0
@@ -136,6 +137,17 @@ int fw_gemm_e4m3(const void* A8, const float* sa, const void* B8, const float* s
                  int M, int N, int K, int epilogue, int tile_n, void* stream);
 /* Per-row e4m3 quantisation of bf16 x [M,K]: scale[row] = absmax / 448, q = e4m3(x / scale). */
 int fw_quant_e4m3(const void* x, int M, int K, void* q, float* scale, void* stream);
+/* e4m3 linear layer for callers that cannot allocate device memory (no counterpart in the
+ * reference).  out[M,N] (bf16) = per-token-e4m3(x[M,K] bf16) * (w8[N,K] e4m3 * sw[N])^T + bias,
+ * the same computation as fw_quant_e4m3 into caller scratch followed by fw_gemm_e4m3, but the
+ * quantised copy of x lives in a fixed array inside the library (32 MiB of activations and
+ * 16384 row scales per GPU, held until the process exits): M * K must be <= 32 MiB and
+ * M <= 16384, else FW_ESCRATCH.  It calls no cudaMalloc / cudaFree.  The first call on a device
+ * looks up the array's device address (once per device, with that device current); make that
+ * first call before any stream capture.  All calls share the array and it keeps the last call's
+ * contents: calls whose executions overlap on the GPU (other streams, other threads) race. */
+int fw_linear_e4m3_noalloc(const void* x, const void* w8, const float* sw, const void* bias, void* out, int M, int N,
+                           int K, void* stream);
 /* resid[M,N] (fp32) += gate[row / rows_per_frame, N] * (A B^T + bias); gate may be NULL. */
 int fw_gemm_bf16_resid(const void* A, const void* B, const void* bias, float* resid, const float* gate,
                        int rows_per_frame, int M, int N, int K, void* stream);
