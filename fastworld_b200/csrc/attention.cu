@@ -7,16 +7,17 @@
 // so one captured graph serves chunk 0 (no history) and steady chunks, with no host cu_seqlens
 // and no concatenation.
 //
-// One CTA per (pair of 128-query tiles A and B, head); 320 threads:
+// One CTA per (pair of 128-query tiles A and B, head); 352 threads:
 //   warps 0-3  softmax of tile A, warps 4-7 softmax of tile B: thread = query row (TMEM lane).
 //              Loads its S row from TMEM, online softmax in the exp2 domain with a lazy O
 //              rescale (only when the running max grows by more than 2^8), writes P (bf16)
 //              into its tile's 128-byte-swizzled K-major smem buffer, final O / l and store.
 //   warp 8     TMA producer: both Q tiles once; then K_0, V_0, K_1, V_1, ... through a ring of
 //              three 32 KB slots (K_{j+1} lands while V_j is still in use).
-//   warp 9     MMA issuer, ping-pong between the tiles so the tensor core works on one tile
-//              while the other tile's softmax runs:
-//                S_A(j+1) = Q_A K_{j+1}^T,  O_A += P_A(j) V_j,  S_B(j+1),  O_B += P_B(j) V_j.
+//   warps 9-10 MMA issuers, one per tile, so the tensor core interleaves the tiles' work and
+//              a slow softmax on one tile never holds back the other:
+//                S_t(j+1) = Q_t K_{j+1}^T,  O_t += P_t(j) V_j;  K/V ring slots are released once
+//              both tiles committed their reads.
 // TMEM (512 columns): S_A [0,128), O_A [128,256), S_B [256,384), O_B [384,512).
 // SMEM: Q_A, Q_B (2 x 32 KB), K/V ring (3 x 32 KB), P_A, P_B (2 x 32 KB) = 224 KB.
 #include "../../include/fastworld_b200.h"
@@ -27,7 +28,7 @@ namespace fw {
 
 namespace attn {
 constexpr int BQ = 128, BKV = 128, HD = 128;
-constexpr int THREADS = 320;
+constexpr int THREADS = 352;
 constexpr int TILE = 128 * 64 * 2;          // one [128 rows x 64 cols] bf16 swizzled sub-tile (16 KB)
 constexpr int Q_OFF = 0;                    // tile t: 2 sub-tiles at Q_OFF + t * 2 * TILE
 constexpr int KV_OFF = Q_OFF + 4 * TILE;    // slot s: 2 sub-tiles at KV_OFF + s * 2 * TILE
@@ -44,6 +45,8 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
                      const __grid_constant__ CUtensorMap tmV0, const __grid_constant__ CUtensorMap tmK1,
                      const __grid_constant__ CUtensorMap tmV1, const AttnArgs args) {
   using namespace attn;
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ uint8_t smem_raw[];
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
   uint8_t* smem = smem_raw + pad;
@@ -55,7 +58,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
   uint64_t* s_free = bars + 9;      // [2]
   uint64_t* p_full = bars + 11;     // [2]
   uint64_t* o_done = bars + 13;     // [2]
-  uint64_t* drain = bars + 15;
+  uint64_t* drain = bars + 15;       // [tile 0]; tile 1 uses bars + 17
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -71,7 +74,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
     mbar_init(q_full, 1);
     for (int s = 0; s < 3; ++s) {
       mbar_init(kv_full + s, 1);
-      mbar_init(kv_free + s, 1);
+      mbar_init(kv_free + s, ntile);   // released once every tile's MMAs read the slot
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(s_full + t, 1);
@@ -80,6 +83,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
       mbar_init(o_done + t, 1);
     }
     mbar_init(drain, 1);
+    mbar_init(bars + 17, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -122,9 +126,10 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
       for (int s = 0; s < 3; ++s)
         if (used >> s & 1u) mbar_wait(kv_full + s, last_par >> s & 1u, &no_abort, args.status, DEV_TIMEOUT_DRAIN);
     }
-  } else if (warp == 9) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0 && nblk > 0) {
+  } else if (warp == 9 || warp == 10) {
+    // ------------------------------------------------------------ MMA issuers (one per tile)
+    const int tt = warp - 9;
+    if (lane == 0 && nblk > 0 && tt < ntile) {
       constexpr uint32_t idesc_s = idesc_bf16(128, 128, false, false);   // Q K^T: both K-major
       constexpr uint32_t idesc_o = idesc_bf16(128, 128, false, true);    // P V: V is MN-major
       bool ok = mbar_wait(q_full, 0, abort_flag, args.status, DEV_TIMEOUT_MMA);
@@ -144,7 +149,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
                     kk != 0);
         }
         umma_commit(s_full + t);
-        if (t == ntile - 1) umma_commit(kv_free + s);   // K_j no longer needed once the last tile read it
+        umma_commit(kv_free + s);   // this tile is done with K_j
         return true;
       };
       // O_t += P_t(j) V_j; needs P_t(j) written and V_j landed
@@ -164,19 +169,18 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
                     sdesc_sw128(sv + (uint32_t)(kk * 2048), TILE, 1024), idesc_o, (j | kk) != 0);
         }
         umma_commit(o_done + t);
-        if (t == ntile - 1) umma_commit(kv_free + s);   // V_j done
+        umma_commit(kv_free + s);   // this tile is done with V_j
         return true;
       };
-      for (int t = 0; ok && t < ntile; ++t) ok = issue_s(t, 0);
+      if (ok) ok = issue_s(tt, 0);
       for (int j = 0; ok && j < nblk; ++j) {
-        for (int t = 0; ok && t < ntile; ++t) {
-          if (j + 1 < nblk) ok = issue_s(t, j + 1);
-          if (ok) ok = issue_o(t, j);
-        }
+        if (j + 1 < nblk) ok = issue_s(tt, j + 1);
+        if (ok) ok = issue_o(tt, j);
       }
-      umma_commit(drain);
+      uint64_t* my_drain = tt == 0 ? drain : bars + 17;
+      umma_commit(my_drain);
       volatile int no_abort = 0;
-      mbar_wait(drain, 0, &no_abort, args.status, DEV_TIMEOUT_DRAIN);
+      mbar_wait(my_drain, 0, &no_abort, args.status, DEV_TIMEOUT_DRAIN);
     }
   } else if ((warp >> 2) < ntile) {
     // ------------------------------------------------------------ softmax / correction / epilogue
@@ -300,8 +304,7 @@ int attention_launch(const CUtensorMap& tmQ, const CUtensorMap& tmK0, const CUte
       cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, attn::SMEM);
   if (err != cudaSuccess) return FW_ECUDA;
   dim3 grid((a.Lq + 2 * attn::BQ - 1) / (2 * attn::BQ), a.heads);
-  attention_kernel<<<grid, attn::THREADS, attn::SMEM, s>>>(tmQ, tmK0, tmV0, tmK1, tmV1, a);
-  note_launch();
+  launch_k(attention_kernel, grid, attn::THREADS, attn::SMEM, s, tmQ, tmK0, tmV0, tmK1, tmV1, a);
   return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
 }
 

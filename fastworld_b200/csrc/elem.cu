@@ -63,6 +63,8 @@ __global__ void __launch_bounds__(256) ln_kernel(const Tin* __restrict__ x, int 
                                                  const __nv_bfloat16* __restrict__ w,
                                                  const __nv_bfloat16* __restrict__ b, __nv_bfloat16* __restrict__ out,
                                                  int ldo, uint8_t* __restrict__ out8, float* __restrict__ sa) {
+  pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (row >= M) return;
   constexpr int D = 128 * NG;
@@ -131,7 +133,7 @@ static int ln_dispatch(const Tin* x, int ldx, int M, int D, float eps, const flo
   const dim3 grid((M + 7) / 8), block(256);
   switch (D / 128) {
 #define FW_LN_CASE(n) \
-  case n: ln_kernel<Tin, n><<<grid, block, 0, s>>>(x, ldx, M, eps, shift, scale, w, b, out, ldo, out8, sa); note_launch(); break;
+  case n: launch_k(ln_kernel<Tin, n>, grid, block, 0, s, x, ldx, M, eps, shift, scale, w, b, out, ldo, out8, sa); break;
     FW_LN_CASE(1) FW_LN_CASE(2) FW_LN_CASE(3) FW_LN_CASE(4) FW_LN_CASE(5) FW_LN_CASE(6) FW_LN_CASE(7)
     FW_LN_CASE(8) FW_LN_CASE(9) FW_LN_CASE(10) FW_LN_CASE(11) FW_LN_CASE(12) FW_LN_CASE(16)
 #undef FW_LN_CASE
@@ -163,6 +165,8 @@ int ln_bf16_q8(const __nv_bfloat16* x, int ldx, int M, int D, float eps, const f
 // applied to a weight [N, K].  One warp per row, two passes (the second hits L1/L2).
 __global__ void __launch_bounds__(256) quant_rows_kernel(const __nv_bfloat16* __restrict__ x, int ldx, int M, int K,
                                                          uint8_t* __restrict__ q, int ldq, float* __restrict__ scale) {
+  pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (row >= M) return;
   const __nv_bfloat16* xr = x + (size_t)row * ldx;
@@ -189,8 +193,7 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const __nv_bfloat16* __
 }
 int quant_rows(const __nv_bfloat16* x, int ldx, int M, int K, uint8_t* q, int ldq, float* scale, cudaStream_t s) {
   if (K % 8 || ldx % 8 || ldq % 16) return FW_ESHAPE;
-  quant_rows_kernel<<<(M + 7) / 8, 256, 0, s>>>(x, ldx, M, K, q, ldq, scale);
-  note_launch();
+  launch_k(quant_rows_kernel, (M + 7) / 8, 256, 0, s, x, ldx, M, K, q, ldq, scale);
   return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
 }
 
@@ -206,6 +209,8 @@ struct RmsPair {
 template <int NG>
 __global__ void __launch_bounds__(256) rms_rope_kernel(RmsPair pr, int ldx, int M, float eps,
                                                        const float2* __restrict__ rope, int hd, int ldo) {
+  pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (row >= M) return;
   const __nv_bfloat16* __restrict__ x = pr.x[blockIdx.y];
@@ -251,7 +256,7 @@ int rms_rope2(const __nv_bfloat16* x, const __nv_bfloat16* w, __nv_bfloat16* out
   const dim3 grid((M + 7) / 8, x2 ? 2 : 1), block(256);
   switch (D / 128) {
 #define FW_RMS_CASE(n) \
-  case n: rms_rope_kernel<n><<<grid, block, 0, s>>>(pr, ldx, M, eps, rope, hd, ldo); note_launch(); break;
+  case n: launch_k(rms_rope_kernel<n>, grid, block, 0, s, pr, ldx, M, eps, rope, hd, ldo); break;
     FW_RMS_CASE(1) FW_RMS_CASE(2) FW_RMS_CASE(3) FW_RMS_CASE(4) FW_RMS_CASE(6) FW_RMS_CASE(8)
     FW_RMS_CASE(10) FW_RMS_CASE(12) FW_RMS_CASE(16)
 #undef FW_RMS_CASE
@@ -272,6 +277,8 @@ int rms_rope(const __nv_bfloat16* x, int ldx, int M, int D, float eps, const __n
 __global__ void rope_table_kernel(const int* __restrict__ chunk, int F, int th, int tw, int hd, double theta,
                                   float2* __restrict__ table, int act_hd, float* __restrict__ act_cos,
                                   float* __restrict__ act_sin) {
+  pdl_trigger();
+  pdl_wait();
   const int half = hd / 2;
   const int nt = half - 2 * (half / 3), nh = half / 3;
   const int s0 = __ldg(chunk + 1);   // first absolute latent frame of the chunk
@@ -303,8 +310,7 @@ int rope_tables(const int* chunk, int F, int th, int tw, int hd, double theta, f
                 float* act_cos, float* act_sin, cudaStream_t s) {
   const int n = F * th * tw * (hd / 2);
   const int m = n > F * act_hd ? n : F * act_hd;
-  rope_table_kernel<<<(m + 255) / 256, 256, 0, s>>>(chunk, F, th, tw, hd, theta, table, act_hd, act_cos, act_sin);
-  note_launch();
+  launch_k(rope_table_kernel, (m + 255) / 256, 256, 0, s, chunk, F, th, tw, hd, theta, table, act_hd, act_cos, act_sin);
   return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
 }
 
@@ -316,6 +322,8 @@ __global__ void __launch_bounds__(256) smallm_linear_kernel(const Tx* __restrict
                                                             const __nv_bfloat16* __restrict__ bias, int N, int K,
                                                             int act_in, int act_out, float* __restrict__ outf,
                                                             __nv_bfloat16* __restrict__ outb, int ldo) {
+  pdl_trigger();
+  pdl_wait();
   const int n = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (n >= N) return;
   const __nv_bfloat16* wr = W + (size_t)n * ldw;
@@ -340,14 +348,13 @@ __global__ void __launch_bounds__(256) smallm_linear_kernel(const Tx* __restrict
 
 int smallm_linear_f32(const float* x, int ldx, int M, const __nv_bfloat16* W, int ldw, const __nv_bfloat16* b, int N,
                       int K, int act_in, int act_out, float* outf, __nv_bfloat16* outb, int ldo, cudaStream_t s) {
-  smallm_linear_kernel<float><<<(N + 7) / 8, 256, 0, s>>>(x, ldx, M, W, ldw, b, N, K, act_in, act_out, outf, outb, ldo);
-  note_launch();
+  launch_k(smallm_linear_kernel<float>, (N + 7) / 8, 256, 0, s, x, ldx, M, W, ldw, b, N, K, act_in, act_out, outf, outb, ldo);
   return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
 }
 int smallm_linear_bf16(const __nv_bfloat16* x, int ldx, int M, const __nv_bfloat16* W, int ldw,
                        const __nv_bfloat16* b, int N, int K, int act_in, int act_out, float* outf,
                        __nv_bfloat16* outb, int ldo, cudaStream_t s) {
-  smallm_linear_kernel<__nv_bfloat16><<<(N + 7) / 8, 256, 0, s>>>(x, ldx, M, W, ldw, b, N, K, act_in, act_out, outf,
+  launch_k(smallm_linear_kernel<__nv_bfloat16>, (N + 7) / 8, 256, 0, s, x, ldx, M, W, ldw, b, N, K, act_in, act_out, outf,
                                                                    outb, ldo);
   return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
 }
@@ -355,6 +362,8 @@ int smallm_linear_bf16(const __nv_bfloat16* x, int ldx, int M, const __nv_bfloat
 // ------------------------------------------------------------------ time embedding helpers
 // Wan sinusoidal_embedding_1d of one timestep: [cos(t w_i), sin(t w_i)], w_i = 10000^(-i/half).
 __global__ void sinusoid_kernel(double t, int dim, float* out) {
+  pdl_trigger();
+  pdl_wait();
   const int half = dim / 2, i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < half) {
     const double a = t * pow(10000.0, -(double)i / (double)half);
@@ -365,8 +374,7 @@ __global__ void sinusoid_kernel(double t, int dim, float* out) {
   }
 }
 int sinusoid(double t, int dim, float* out, cudaStream_t s) {
-  sinusoid_kernel<<<(dim / 2 + 127) / 128, 128, 0, s>>>(t, dim, out);
-  note_launch();
+  launch_k(sinusoid_kernel, (dim / 2 + 127) / 128, 128, 0, s, t, dim, out);
   return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
 }
 
@@ -375,6 +383,8 @@ int sinusoid(double t, int dim, float* out, cudaStream_t s) {
 __global__ void modulation_kernel(const __nv_bfloat16* __restrict__ mods, const float* __restrict__ e0, int layers,
                                   int D, float* __restrict__ ee, const __nv_bfloat16* __restrict__ hmod,
                                   const float* __restrict__ e, float* __restrict__ head) {
+  pdl_trigger();
+  pdl_wait();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   const int n = layers * 6 * D;
   if (i < n) ee[i] = __bfloat162float(mods[i]) + e0[i % (6 * D)];
@@ -383,8 +393,7 @@ __global__ void modulation_kernel(const __nv_bfloat16* __restrict__ mods, const 
 int modulation(const __nv_bfloat16* mods, const float* e0, int layers, int D, float* ee, const __nv_bfloat16* hmod,
                const float* e, float* head, cudaStream_t s) {
   const int n = layers * 6 * D > 2 * D ? layers * 6 * D : 2 * D;
-  modulation_kernel<<<(n + 255) / 256, 256, 0, s>>>(mods, e0, layers, D, ee, hmod, e, head);
-  note_launch();
+  launch_k(modulation_kernel, (n + 255) / 256, 256, 0, s, mods, e0, layers, D, ee, hmod, e, head);
   return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
 }
 
@@ -392,6 +401,8 @@ int modulation(const __nv_bfloat16* mods, const float* e0, int layers, int D, fl
 // A[token, c * 4 + i * 2 + j] = cat(x, cc)[c, f, 2 h + i, 2 w + j]  (Conv3d weight order).
 __global__ void patchify_kernel(const __nv_bfloat16* __restrict__ x, int C1, const __nv_bfloat16* __restrict__ cc,
                                 int C2, int F, int H, int W, __nv_bfloat16* __restrict__ A) {
+  pdl_trigger();
+  pdl_wait();
   const int th = H / 2, tw = W / 2, C = C1 + C2, Kp = C * 4;
   const int L = F * th * tw;
   const int idx = blockIdx.x * blockDim.x + threadIdx.x;
@@ -405,8 +416,7 @@ __global__ void patchify_kernel(const __nv_bfloat16* __restrict__ x, int C1, con
 int patchify(const __nv_bfloat16* x, int C1, const __nv_bfloat16* cc, int C2, int F, int H, int W, __nv_bfloat16* A,
              cudaStream_t s) {
   const int n = F * (H / 2) * (W / 2) * (C1 + C2) * 4;
-  patchify_kernel<<<(n + 255) / 256, 256, 0, s>>>(x, C1, cc, C2, F, H, W, A);
-  note_launch();
+  launch_k(patchify_kernel, (n + 255) / 256, 256, 0, s, x, C1, cc, C2, F, H, W, A);
   return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
 }
 
@@ -418,6 +428,8 @@ __global__ void scheduler_kernel(const float* __restrict__ head, const __nv_bflo
                                  __nv_bfloat16* __restrict__ den, __nv_bfloat16* __restrict__ out_copy,
                                  const __nv_bfloat16* __restrict__ noise, float sigma_n,
                                  __nv_bfloat16* __restrict__ xnext, int C, int F, int H, int W) {
+  pdl_trigger();
+  pdl_wait();
   const int idx = blockIdx.x * blockDim.x + threadIdx.x;
   const int n = C * F * H * W;
   if (idx >= n) return;
@@ -438,8 +450,7 @@ int scheduler(const float* head, const __nv_bfloat16* x, float sigma, __nv_bfloa
               const __nv_bfloat16* noise, float sigma_n, __nv_bfloat16* xnext, int C, int F, int H, int W,
               cudaStream_t s) {
   const int n = C * F * H * W;
-  scheduler_kernel<<<(n + 255) / 256, 256, 0, s>>>(head, x, sigma, den, out_copy, noise, sigma_n, xnext, C, F, H, W);
-  note_launch();
+  launch_k(scheduler_kernel, (n + 255) / 256, 256, 0, s, head, x, sigma, den, out_copy, noise, sigma_n, xnext, C, F, H, W);
   return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
 }
 
@@ -468,6 +479,8 @@ __global__ void __launch_bounds__(256) mouse_attn_kernel(const __nv_bfloat16* __
                                                          const float* __restrict__ asin_, __nv_bfloat16* mk,
                                                          __nv_bfloat16* mv, int first, int write,
                                                          __nv_bfloat16* __restrict__ out, int S, int AH, float eps) {
+  pdl_trigger();
+  pdl_wait();
   const int wid = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (wid >= S * AH) return;
   const int s = wid / AH, h = wid % AH, A = AH * 64, d = 2 * lane;
@@ -519,8 +532,7 @@ int mouse_attn(const __nv_bfloat16* qkv, const __nv_bfloat16* wq, const __nv_bfl
                const float* asin_, __nv_bfloat16* mk, __nv_bfloat16* mv, int first, int write, __nv_bfloat16* out,
                int S, int F, int AH, float eps, cudaStream_t s) {
   if (F != 3) return FW_ESHAPE;
-  mouse_attn_kernel<3><<<(S * AH + 7) / 8, 256, 0, s>>>(qkv, wq, wk, acos_, asin_, mk, mv, first, write, out, S, AH, eps);
-  note_launch();
+  launch_k(mouse_attn_kernel<3>, (S * AH + 7) / 8, 256, 0, s, qkv, wq, wk, acos_, asin_, mk, mv, first, write, out, S, AH, eps);
   return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
 }
 
@@ -529,6 +541,8 @@ __global__ void kb_kv_kernel(const float* __restrict__ kv, const __nv_bfloat16* 
                              const float* __restrict__ acos_, const float* __restrict__ asin_,
                              __nv_bfloat16* __restrict__ kout, __nv_bfloat16* __restrict__ vout, int F, int AH,
                              float eps) {
+  pdl_trigger();
+  pdl_wait();
   const int wid = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (wid >= F * AH) return;
   const int f = wid / AH, h = wid % AH, A = AH * 64, d = 2 * lane;
@@ -540,8 +554,7 @@ __global__ void kb_kv_kernel(const float* __restrict__ kv, const __nv_bfloat16* 
 }
 int kb_kv(const float* kv, const __nv_bfloat16* wk, const float* acos_, const float* asin_, __nv_bfloat16* kout,
           __nv_bfloat16* vout, int F, int AH, float eps, cudaStream_t s) {
-  kb_kv_kernel<<<(F * AH + 3) / 4, 128, 0, s>>>(kv, wk, acos_, asin_, kout, vout, F, AH, eps);
-  note_launch();
+  launch_k(kb_kv_kernel, (F * AH + 3) / 4, 128, 0, s, kv, wk, acos_, asin_, kout, vout, F, AH, eps);
   return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
 }
 
@@ -557,6 +570,8 @@ __global__ void __launch_bounds__(256) kb_attn_kernel(const __nv_bfloat16* __res
                                                       const __nv_bfloat16* __restrict__ kc,
                                                       const __nv_bfloat16* __restrict__ vc, int first,
                                                       __nv_bfloat16* __restrict__ out, int L, int S, int AH, float eps) {
+  pdl_trigger();
+  pdl_wait();
   const int wid = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (wid >= L * AH) return;
   const int row = wid / AH, h = wid % AH, f = row / S, A = AH * 64, d = 2 * lane;
@@ -587,8 +602,7 @@ int kb_attn(const __nv_bfloat16* mq, const __nv_bfloat16* wq, const float* acos_
             const __nv_bfloat16* kh, const __nv_bfloat16* vh, const __nv_bfloat16* kc, const __nv_bfloat16* vc,
             int first, __nv_bfloat16* out, int L, int S, int F, int AH, float eps, cudaStream_t s) {
   if (F != 3) return FW_ESHAPE;
-  kb_attn_kernel<3><<<(L * AH + 7) / 8, 256, 0, s>>>(mq, wq, acos_, asin_, kh, vh, kc, vc, first, out, L, S, AH, eps);
-  note_launch();
+  launch_k(kb_attn_kernel<3>, (L * AH + 7) / 8, 256, 0, s, mq, wq, acos_, asin_, kh, vh, kc, vc, first, out, L, S, AH, eps);
   return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
 }
 
@@ -597,6 +611,8 @@ int kb_attn(const __nv_bfloat16* mq, const __nv_bfloat16* wq, const float* acos_
 __global__ void __launch_bounds__(256) copy_kernel(uint4* __restrict__ dst, const uint4* __restrict__ src, size_t n16,
                                                    uint8_t* __restrict__ dtail, const uint8_t* __restrict__ stail,
                                                    int ntail) {
+  pdl_trigger();
+  pdl_wait();
   const size_t stride = (size_t)gridDim.x * blockDim.x;
   size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   for (; i + 3 * stride < n16; i += 4 * stride) {
@@ -620,7 +636,7 @@ int copy_bytes(void* dst, const void* src, size_t bytes, cudaStream_t s) {
   size_t want = (n16 + 255) / 256;
   const size_t cap = (size_t)num_sms() * 8;
   const int grid = (int)(want < 1 ? 1 : (want > cap ? cap : want));
-  copy_kernel<<<grid, 256, 0, s>>>(reinterpret_cast<uint4*>(dst), reinterpret_cast<const uint4*>(src), n16,
+  launch_k(copy_kernel, grid, 256, 0, s, reinterpret_cast<uint4*>(dst), reinterpret_cast<const uint4*>(src), n16,
                                    reinterpret_cast<uint8_t*>(dst) + n16 * 16,
                                    reinterpret_cast<const uint8_t*>(src) + n16 * 16, ntail);
   return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;

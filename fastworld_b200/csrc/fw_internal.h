@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 namespace fw {
 
 // ---------------------------------------------------------------- host utilities
@@ -21,6 +23,29 @@ int make_tmap_2d(CUtensorMap* out, const void* base, int elem_bytes, int64_t row
 int num_sms();
 // Counts kernel launches enqueued by this library (all threads); read with fw_launch_count().
 void note_launch();
+// Programmatic dependent launch (on unless FW_PDL=0 in the environment): every kernel of the
+// library signals griddepcontrol.launch_dependents on entry and waits (griddepcontrol.wait)
+// before touching data produced upstream, so the next kernel's launch and prologue overlap the
+// tail of the current one, in streams and in captured graphs alike.
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                            Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+  note_launch();
+  return e;
+}
 
 // ---------------------------------------------------------------- GEMM
 enum EpiMode : int {

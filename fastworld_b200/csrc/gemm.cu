@@ -117,6 +117,7 @@ __global__ void __launch_bounds__(320, 1)
                      const GemmArgs args) {
   using C = GemmCfg<BN>;
   constexpr int KE = F8 ? 128 : 64;   // K elements per stage
+  pdl_trigger();
   extern __shared__ uint8_t smem_raw[];
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
   uint8_t* smem = smem_raw + pad;
@@ -159,6 +160,7 @@ __global__ void __launch_bounds__(320, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();   // everything below reads or writes data of earlier kernels
 
   if (warp == 0) {
     if (lane == 0) {
@@ -315,8 +317,7 @@ static int launch_bn(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmA
   cudaError_t err =
       cudaFuncSetAttribute(gemm_bf16_kernel<BN, F8>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (err != cudaSuccess) return FW_ECUDA;
-  gemm_bf16_kernel<BN, F8><<<grid, 320, C::SMEM, s>>>(tmA, tmB, a);
-  note_launch();
+  launch_k(gemm_bf16_kernel<BN, F8>, grid, 320, C::SMEM, s, tmA, tmB, a);
   return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
 }
 

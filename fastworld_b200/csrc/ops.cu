@@ -1,5 +1,6 @@
 // Host utilities (TMA descriptors, device queries) and the op-level C ABI entry points.
 #include <atomic>
+#include <cstdlib>
 #include <cmath>
 #include <cstring>
 
@@ -23,6 +24,14 @@ PFN_encodeTiled get_encode_fn() {
 
 static std::atomic<unsigned long long> g_launches{0};
 void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("FW_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
 
 int num_sms() {
   int dev = 0, n = 0;
