@@ -40,24 +40,14 @@ import torch
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
+from fastworld_b200.config import chunk_flops  # noqa: E402
+
 METRIC = "MG2-shape DiT chunk ms & FPS at 1 GPU; session FPS at 1/2/4/8 B200"
 FRAMES_PER_CHUNK = 12
 
 
 def dist_env():
     return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
-
-
-def chunk_flops(cfg, steady=True):
-    """Algorithmic flops of one chunk: GEMMs (2 M N K) + attention (4 Lq Lk D), all forwards."""
-    L, D, F, A, Mh = cfg.tokens, cfg.dim, cfg.ffn, cfg.act_dim, cfg.mouse_hidden
-    blk = 2 * L * D * (3 * D + D + D + D + 2 * F)
-    lk = 2 * L if steady else L
-    attn = 4 * L * lk * D + 4 * L * cfg.ctx_tokens * D
-    act = 2 * L * (D * Mh + Mh * Mh + Mh * 3 * A + A * D + D * A + A * D)
-    per_fwd = cfg.layers * (blk + attn) + len(cfg.action_blocks) * act + 2 * L * (cfg.patch_k * D + D * cfg.out_dim)
-    per_chunk_ctx = cfg.layers * 2 * cfg.ctx_tokens * D * 2 * D
-    return cfg.n_fwd * per_fwd + per_chunk_ctx, cfg.n_fwd * cfg.layers * (blk + attn)
 
 
 def peaks():

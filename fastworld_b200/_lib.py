@@ -32,6 +32,7 @@ class FwConfig(ctypes.Structure):
         ("n_steps", ctypes.c_int), ("steps", ctypes.c_float * FW_MAX_STEPS),
         ("eps", ctypes.c_float), ("eps_ln", ctypes.c_float), ("rope_theta", ctypes.c_float),
         ("linear_fp8", ctypes.c_int),
+        ("hist_chunks", ctypes.c_int), ("tp_size", ctypes.c_int), ("tp_rank", ctypes.c_int),
     ]
 
 
@@ -70,6 +71,10 @@ _SIGS = {
     "fw_gemm_bf16_resid": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                           ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                           ctypes.c_void_p]),
+    "fw_tp_unique_id": (ctypes.c_int, [ctypes.c_char_p]),
+    "fw_tp_init": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_char_p]),
+    "fw_tp_allreduce": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int,
+                                       ctypes.c_void_p]),
     "fw_attention": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
                                     ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p,
                                     ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),
@@ -101,8 +106,9 @@ def check(rc: int, what: str = "call") -> None:
         raise RuntimeError(f"fastworld_b200 {what} failed: {strerror(rc)} (code {rc})")
 
 
-def make_config(cfg) -> FwConfig:
-    """fw_config from a :class:`fastworld_b200.config.DiTConfig`."""
+def make_config(cfg, tp_size: int = 1, tp_rank: int = 0) -> FwConfig:
+    """fw_config from a :class:`fastworld_b200.config.DiTConfig` (and this rank's tensor-parallel
+    position)."""
     c = FwConfig()
     for f in ("dim", "heads", "head_dim", "ffn", "layers", "freq_dim", "lat_ch", "cond_ch", "frames", "lat_h",
               "lat_w", "ctx_tokens", "ctx_dim", "act_heads", "act_head_dim", "mouse_hidden", "keyboard_hidden",
@@ -120,6 +126,8 @@ def make_config(cfg) -> FwConfig:
     if cfg.linear not in ("bf16", "fp8"):
         raise ValueError(f"linear dtype {cfg.linear!r}")
     c.linear_fp8 = int(cfg.linear == "fp8")
+    c.hist_chunks = int(cfg.hist_chunks)
+    c.tp_size, c.tp_rank = int(tp_size), int(tp_rank)
     return c
 
 

@@ -64,6 +64,10 @@ class DiTConfig:
     # block linears: "bf16", or "fp8" = e4m3 with per-output-channel weight scales (absmax/448)
     # and per-token activation scales; attention and norms stay bf16
     linear: str = "bf16"
+    # KV history window in chunks: 1 = the previous chunk (MG2, static.py:47-48); BASELINE
+    # configs[4] keeps 2.  Chunk k's context forward writes ring slot k % hist_chunks and a
+    # steady chunk attends to the min(k, hist_chunks) filled slots, then its own tokens.
+    hist_chunks: int = 1
 
     # ---- derived
     @property
@@ -123,6 +127,21 @@ class DiTConfig:
         assert all(0 <= b < self.layers for b in self.action_blocks)
         assert self.lat_h % self.patch[1] == 0 and self.lat_w % self.patch[2] == 0
         assert self.patch[0] == 1
+        assert self.hist_chunks >= 1
+
+
+def chunk_flops(cfg: DiTConfig, steady: bool = True):
+    """Algorithmic flops of one chunk: (all, block GEMMs + attention only).  GEMMs count
+    2 M N K, attention 4 Lq Lk head_dim per head (Q K^T and P V); a steady chunk attends to the
+    full history window plus its own tokens, chunk 0 to its own tokens."""
+    L, D, F, A, Mh = cfg.tokens, cfg.dim, cfg.ffn, cfg.act_dim, cfg.mouse_hidden
+    blk = 2 * L * D * (3 * D + D + D + D + 2 * F)
+    lk = (cfg.hist_chunks + 1) * L if steady else L
+    attn = 4 * L * lk * D + 4 * L * cfg.ctx_tokens * D
+    act = 2 * L * (D * Mh + Mh * Mh + Mh * 3 * A + A * D + D * A + A * D)
+    per_fwd = cfg.layers * (blk + attn) + len(cfg.action_blocks) * act + 2 * L * (cfg.patch_k * D + D * cfg.out_dim)
+    per_chunk_ctx = cfg.layers * 2 * cfg.ctx_tokens * D * 2 * D
+    return cfg.n_fwd * per_fwd + per_chunk_ctx, cfg.n_fwd * cfg.layers * (blk + attn)
 
 
 # BASELINE configs[0]: one Wan-1.3B block (parity case, no action module).
@@ -131,7 +150,7 @@ BLOCK = DiTConfig(name="block", layers=1, action_blocks=())
 MG2 = DiTConfig()
 # Wan-14B shape (40 x 128 heads, 5120 wide, 1560 tokens per frame).
 WAN14B = DiTConfig(name="wan14b", dim=5120, heads=40, head_dim=128, ffn=13824, layers=40,
-                   lat_h=60, lat_w=104, action_blocks=())
+                   lat_h=60, lat_w=104, action_blocks=(), hist_chunks=2)
 # Small shapes for CPU tests: same code paths, tiny widths, the reference's chunk geometry.
 TINY = DiTConfig(name="tiny", dim=128, heads=2, head_dim=64, ffn=256, layers=2, ctx_dim=64,
                  action_blocks=(0,), act_heads=2, mouse_hidden=128, keyboard_hidden=32)
@@ -139,7 +158,12 @@ TINY = DiTConfig(name="tiny", dim=128, heads=2, head_dim=64, ffn=256, layers=2, 
 SMALL = DiTConfig(name="small", dim=256, heads=2, head_dim=128, ffn=512, layers=2, ctx_dim=256,
                   action_blocks=(1,), act_heads=4, mouse_hidden=256, keyboard_hidden=64)
 
+# configs[4]'s structure (2-chunk history, no action module) at test size, for tensor-parallel
+# parity on 2 GPUs: 4 heads, FFN 1024, two blocks.
+SMALL_TP = DiTConfig(name="small_tp", dim=512, heads=4, head_dim=128, ffn=1024, layers=2, ctx_dim=256,
+                     action_blocks=(), hist_chunks=2)
+
 # config[1] with e4m3 block linears.
 MG2_FP8 = MG2.replace(name="mg2_fp8", linear="fp8")
 
-PRESETS = {c.name: c for c in (BLOCK, MG2, MG2_FP8, WAN14B, TINY, SMALL)}
+PRESETS = {c.name: c for c in (BLOCK, MG2, MG2_FP8, WAN14B, TINY, SMALL, SMALL_TP)}

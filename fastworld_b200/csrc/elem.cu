@@ -135,7 +135,7 @@ static int ln_dispatch(const Tin* x, int ldx, int M, int D, float eps, const flo
 #define FW_LN_CASE(n) \
   case n: launch_k(ln_kernel<Tin, n>, grid, block, 0, s, x, ldx, M, eps, shift, scale, w, b, out, ldo, out8, sa); break;
     FW_LN_CASE(1) FW_LN_CASE(2) FW_LN_CASE(3) FW_LN_CASE(4) FW_LN_CASE(5) FW_LN_CASE(6) FW_LN_CASE(7)
-    FW_LN_CASE(8) FW_LN_CASE(9) FW_LN_CASE(10) FW_LN_CASE(11) FW_LN_CASE(12) FW_LN_CASE(16)
+    FW_LN_CASE(8) FW_LN_CASE(9) FW_LN_CASE(10) FW_LN_CASE(11) FW_LN_CASE(12) FW_LN_CASE(16) FW_LN_CASE(40)
 #undef FW_LN_CASE
     default: return FW_ESHAPE;
   }
@@ -199,11 +199,15 @@ int quant_rows(const __nv_bfloat16* x, int ldx, int M, int K, uint8_t* q, int ld
 
 // ------------------------------------------------------------------ RMSNorm (+ RoPE)
 // out = RMSNorm(x) * w over D = 128 * NG, then (optionally) each (even, odd) pair of every
-// head is rotated by rope[row, pair % (hd / 2)] = (cos, sin).
+// head is rotated by rope[row, pair % (hd / 2)] = (cos, sin).  With tensor parallelism the
+// row is a shard of the normalised width: `ss` then holds the all-reduced sum of squares of
+// the full row (ss[row * 2 + tensor]) and inv_d is 1 / full width.
 struct RmsPair {
   const __nv_bfloat16* x[2];
   const __nv_bfloat16* w[2];
   __nv_bfloat16* out[2];
+  const float* ss = nullptr;
+  float inv_d = 0.f;
 };
 
 template <int NG>
@@ -225,7 +229,8 @@ __global__ void __launch_bounds__(256) rms_rope_kernel(RmsPair pr, int ldx, int 
 #pragma unroll
     for (int i = 0; i < 4; ++i) q += v[g][i] * v[g][i];
   }
-  const float r = rsqrtf(warp_sum(q) * (1.f / D) + eps);
+  const float tot = pr.ss ? __ldg(pr.ss + (size_t)row * 2 + blockIdx.y) : warp_sum(q);
+  const float r = rsqrtf(tot * (pr.ss ? pr.inv_d : 1.f / D) + eps);
   const int half = hd >> 1;
 #pragma unroll
   for (int g = 0; g < NG; ++g) {
@@ -248,20 +253,167 @@ __global__ void __launch_bounds__(256) rms_rope_kernel(RmsPair pr, int ldx, int 
   }
 }
 
-int rms_rope2(const __nv_bfloat16* x, const __nv_bfloat16* w, __nv_bfloat16* out, const __nv_bfloat16* x2,
-              const __nv_bfloat16* w2, __nv_bfloat16* out2, int ldx, int M, int D, float eps, const float2* rope, int hd,
-              int ldo, cudaStream_t s) {
+static int rms_rope_launch(const RmsPair& pr, bool two, int ldx, int M, int D, float eps, const float2* rope, int hd,
+                           int ldo, cudaStream_t s) {
   if (D % 128 || ldx % 4 || ldo % 4 || (rope && (hd % 4 || D % hd))) return FW_ESHAPE;
-  RmsPair pr{{x, x2}, {w, w2}, {out, out2}};
-  const dim3 grid((M + 7) / 8, x2 ? 2 : 1), block(256);
+  const dim3 grid((M + 7) / 8, two ? 2 : 1), block(256);
   switch (D / 128) {
 #define FW_RMS_CASE(n) \
   case n: launch_k(rms_rope_kernel<n>, grid, block, 0, s, pr, ldx, M, eps, rope, hd, ldo); break;
-    FW_RMS_CASE(1) FW_RMS_CASE(2) FW_RMS_CASE(3) FW_RMS_CASE(4) FW_RMS_CASE(6) FW_RMS_CASE(8)
-    FW_RMS_CASE(10) FW_RMS_CASE(12) FW_RMS_CASE(16)
+    FW_RMS_CASE(1) FW_RMS_CASE(2) FW_RMS_CASE(3) FW_RMS_CASE(4) FW_RMS_CASE(5) FW_RMS_CASE(6) FW_RMS_CASE(8)
+    FW_RMS_CASE(10) FW_RMS_CASE(12) FW_RMS_CASE(16) FW_RMS_CASE(20) FW_RMS_CASE(40)
 #undef FW_RMS_CASE
     default: return FW_ESHAPE;
   }
+  return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
+}
+
+int rms_rope2(const __nv_bfloat16* x, const __nv_bfloat16* w, __nv_bfloat16* out, const __nv_bfloat16* x2,
+              const __nv_bfloat16* w2, __nv_bfloat16* out2, int ldx, int M, int D, float eps, const float2* rope, int hd,
+              int ldo, cudaStream_t s) {
+  RmsPair pr{{x, x2}, {w, w2}, {out, out2}};
+  return rms_rope_launch(pr, x2 != nullptr, ldx, M, D, eps, rope, hd, ldo, s);
+}
+
+int rms_rope2_ss(const __nv_bfloat16* x, const __nv_bfloat16* w, __nv_bfloat16* out, const __nv_bfloat16* x2,
+                 const __nv_bfloat16* w2, __nv_bfloat16* out2, int ldx, int M, int D, const float* ss, int d_full,
+                 float eps, const float2* rope, int hd, int ldo, cudaStream_t s) {
+  if (!ss || d_full <= 0) return FW_EINVAL;
+  RmsPair pr{{x, x2}, {w, w2}, {out, out2}, ss, 1.f / (float)d_full};
+  return rms_rope_launch(pr, x2 != nullptr, ldx, M, D, eps, rope, hd, ldo, s);
+}
+
+// Per-row partial sums of squares of one or two bf16 tensors [M, D]: ss[row * 2 + t].  One
+// warp per row.
+__global__ void __launch_bounds__(256) sumsq_kernel(const __nv_bfloat16* __restrict__ x0,
+                                                    const __nv_bfloat16* __restrict__ x1, int ld, int M, int D,
+                                                    float* __restrict__ ss) {
+  pdl_trigger();
+  pdl_wait();
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (row >= M) return;
+  const __nv_bfloat16* __restrict__ x = blockIdx.y ? x1 : x0;
+  float q = 0.f;
+  for (int c = lane * 8; c < D; c += 256) {
+    const uint4 u = *reinterpret_cast<const uint4*>(x + (size_t)row * ld + c);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = unpack_bf16(w[i]);
+      q += f.x * f.x + f.y * f.y;
+    }
+  }
+  q = warp_sum(q);
+  if (lane == 0) ss[(size_t)row * 2 + blockIdx.y] = q;
+}
+int sumsq_rows(const __nv_bfloat16* x0, const __nv_bfloat16* x1, int ld, int M, int D, float* ss, cudaStream_t s) {
+  if (D % 8 || ld % 8) return FW_ESHAPE;
+  launch_k(sumsq_kernel, dim3((M + 7) / 8, x1 ? 2 : 1), 256, 0, s, x0, x1, ld, M, D, ss);
+  return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
+}
+
+// xs[row, :] += gate[(row / rows_per_frame) * gate_stride + :] * (p[row, :] + bias) after the
+// all-reduce of a row-parallel linear (gate and bias optional; gate_stride 0 = one gate row for
+// all frames); mirror (optional) = bf16 copy of the new xs.  One warp per row, 8 columns per
+// lane per step.
+__global__ void __launch_bounds__(256) resid_add_kernel(float* __restrict__ xs, int ldx,
+                                                        const __nv_bfloat16* __restrict__ p, int ldp,
+                                                        const __nv_bfloat16* __restrict__ bias,
+                                                        const float* __restrict__ gate, int gate_stride,
+                                                        int rows_per_frame, __nv_bfloat16* __restrict__ mirror,
+                                                        int M, int D) {
+  pdl_trigger();
+  pdl_wait();
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (row >= M) return;
+  const float* g = gate ? gate + (size_t)(row / rows_per_frame) * gate_stride : nullptr;
+  for (int c = lane * 8; c < D; c += 256) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p + (size_t)row * ldp + c);
+    const uint32_t pw[4] = {u.x, u.y, u.z, u.w};
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = unpack_bf16(pw[i]);
+      v[2 * i] = f.x;
+      v[2 * i + 1] = f.y;
+    }
+    if (bias) {
+      const uint4 b = *reinterpret_cast<const uint4*>(bias + c);
+      const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = unpack_bf16(bw[i]);
+        v[2 * i] += f.x;
+        v[2 * i + 1] += f.y;
+      }
+    }
+    float4* xr = reinterpret_cast<float4*>(xs + (size_t)row * ldx + c);
+    float4 a = xr[0], b = xr[1];
+    if (g) {
+      const float4 g0 = *reinterpret_cast<const float4*>(g + c), g1 = *reinterpret_cast<const float4*>(g + c + 4);
+      a.x += g0.x * v[0]; a.y += g0.y * v[1]; a.z += g0.z * v[2]; a.w += g0.w * v[3];
+      b.x += g1.x * v[4]; b.y += g1.y * v[5]; b.z += g1.z * v[6]; b.w += g1.w * v[7];
+    } else {
+      a.x += v[0]; a.y += v[1]; a.z += v[2]; a.w += v[3];
+      b.x += v[4]; b.y += v[5]; b.z += v[6]; b.w += v[7];
+    }
+    xr[0] = a;
+    xr[1] = b;
+    if (mirror)
+      *reinterpret_cast<uint4*>(mirror + (size_t)row * D + c) =
+          make_uint4(pack_bf16(a.x, a.y), pack_bf16(a.z, a.w), pack_bf16(b.x, b.y), pack_bf16(b.z, b.w));
+  }
+}
+int resid_add(float* xs, int ldx, const __nv_bfloat16* p, int ldp, const __nv_bfloat16* bias, const float* gate,
+              int gate_stride, int rows_per_frame, __nv_bfloat16* mirror, int M, int D, cudaStream_t s) {
+  if (D % 8 || ldx % 4 || ldp % 8 || gate_stride % 4 || rows_per_frame <= 0) return FW_ESHAPE;
+  launch_k(resid_add_kernel, (M + 7) / 8, 256, 0, s, xs, ldx, p, ldp, bias, gate, gate_stride, rows_per_frame, mirror,
+           M, D);
+  return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
+}
+
+// ------------------------------------------------------------------ multi-chunk history window
+// meta = {min(k, window) * L, L} for steady chunk k = chunk[0] (keys: filled history slots,
+// then the current chunk).
+__global__ void hist_meta_kernel(const int* __restrict__ chunk, int window, int L, int* __restrict__ meta) {
+  pdl_trigger();
+  pdl_wait();
+  if (threadIdx.x == 0) {
+    const int k = max(chunk[0], 0);
+    meta[0] = min(k, window) * L;
+    meta[1] = L;
+  }
+}
+int hist_meta(const int* chunk, int window, int L, int* meta, cudaStream_t s) {
+  if (!chunk || !meta || window < 1) return FW_EINVAL;
+  launch_k(hist_meta_kernel, 1, 32, 0, s, chunk, window, L, meta);
+  return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
+}
+
+// dst_base + (chunk[0] % window) * slot_bytes <- src (n16 16-byte words): the context forward
+// of chunk k writes its K or V into slot k % window of the history ring.
+__global__ void __launch_bounds__(256) slot_copy_kernel(uint8_t* __restrict__ dst_base, size_t slot_bytes,
+                                                        const int* __restrict__ chunk, int window,
+                                                        const uint4* __restrict__ src, size_t n16) {
+  pdl_trigger();
+  pdl_wait();
+  const int slot = max(chunk[0], 0) % window;
+  uint4* __restrict__ dst = reinterpret_cast<uint4*>(dst_base + (size_t)slot * slot_bytes);
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += stride) __stcs(dst + i, __ldcs(src + i));
+}
+int slot_copy(void* dst_base, size_t slot_bytes, const int* chunk, int window, const void* src, size_t bytes,
+              cudaStream_t s) {
+  if (!dst_base || !src || !chunk || window < 1) return FW_EINVAL;
+  if (((reinterpret_cast<uintptr_t>(dst_base) | reinterpret_cast<uintptr_t>(src)) & 15u) || bytes % 16 ||
+      slot_bytes % 16 || bytes > slot_bytes)
+    return FW_EALIGN;
+  const size_t n16 = bytes / 16;
+  size_t want = (n16 + 255) / 256;
+  const size_t cap = (size_t)num_sms() * 8;
+  const int grid = (int)(want < 1 ? 1 : (want > cap ? cap : want));
+  launch_k(slot_copy_kernel, grid, 256, 0, s, reinterpret_cast<uint8_t*>(dst_base), slot_bytes, chunk, window,
+           reinterpret_cast<const uint4*>(src), n16);
   return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
 }
 

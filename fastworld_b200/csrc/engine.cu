@@ -18,6 +18,7 @@
 #include "../../include/fastworld_b200.h"
 #include "fw_elem.h"
 #include "fw_internal.h"
+#include "fw_tp.h"
 
 namespace fw {
 
@@ -56,8 +57,13 @@ struct fw_handle {
   std::vector<fw::Tensor> tensors;
   std::unordered_map<std::string, int> index;
   bool finalized = false;
-  // dims
+  // dims (Hl, Dl, FFl: this rank's heads, attention width and FFN width; = H, D, FF at tp 1)
   int L, S, F, D, H, HD, FF, A, AH, Mh, Kh, nA, th, tw, Ctx, Cd, Kp, OUT, KC, PAD;
+  int Hl, Dl, FFl;
+  int tp = 1, tpr = 0, hc = 1;   // tensor-parallel size / rank, history window in chunks
+  void* comm = nullptr;           // NCCL communicator (tp > 1)
+  __nv_bfloat16* part = nullptr;  // [L, D] partial output of a row-parallel linear (tp > 1)
+  float* ss = nullptr;            // [max(L, Ctx), 2] sums of squares for the sharded RMSNorms
   size_t lat_elems;
   // workspace layout (offsets into "workspace")
   std::vector<std::pair<std::string, size_t>> ws_off;
@@ -113,7 +119,7 @@ static size_t ws_add(fw_handle* h, const char* name, size_t bytes) {
 
 static int register_tensors(fw_handle* h) {
   const fw_config& c = h->cfg;
-  const int D = h->D, FF = h->FF, A = h->A;
+  const int D = h->D, A = h->A, Dl = h->Dl, FFl = h->FFl;
   auto wt = [&](const std::string& n, std::vector<int64_t> s) { add_tensor(h, n, FW_KIND_WEIGHT, FW_BF16, s); };
   wt("patch.w", {D, h->Kp});
   wt("patch.b", {D});
@@ -137,25 +143,27 @@ static int register_tensors(fw_handle* h) {
   wt("mods", {c.layers, 6, D});
   for (int i = 0; i < c.layers; ++i) {
     const std::string p = "b" + std::to_string(i) + ".";
-    wt(p + "sa.qkv.w", {3 * D, D});
-    wt(p + "sa.qkv.b", {3 * D});
-    wt(p + "sa.o.w", {D, D});
+    // with tp > 1: q/k/v, ca.q/k/v and ffn.0 are this rank's rows (column-parallel), sa.o,
+    // ca.o and ffn.2 this rank's input columns (row-parallel; their biases are whole)
+    wt(p + "sa.qkv.w", {3 * Dl, D});
+    wt(p + "sa.qkv.b", {3 * Dl});
+    wt(p + "sa.o.w", {D, Dl});
     wt(p + "sa.o.b", {D});
-    wt(p + "sa.nq.w", {D});
-    wt(p + "sa.nk.w", {D});
+    wt(p + "sa.nq.w", {Dl});
+    wt(p + "sa.nk.w", {Dl});
     wt(p + "n3.w", {D});
     wt(p + "n3.b", {D});
-    wt(p + "ca.q.w", {D, D});
-    wt(p + "ca.q.b", {D});
-    wt(p + "ca.kv.w", {2 * D, D});
-    wt(p + "ca.kv.b", {2 * D});
-    wt(p + "ca.o.w", {D, D});
+    wt(p + "ca.q.w", {Dl, D});
+    wt(p + "ca.q.b", {Dl});
+    wt(p + "ca.kv.w", {2 * Dl, D});
+    wt(p + "ca.kv.b", {2 * Dl});
+    wt(p + "ca.o.w", {D, Dl});
     wt(p + "ca.o.b", {D});
-    wt(p + "ca.nq.w", {D});
-    wt(p + "ca.nk.w", {D});
-    wt(p + "ffn.0.w", {FF, D});
-    wt(p + "ffn.0.b", {FF});
-    wt(p + "ffn.2.w", {D, FF});
+    wt(p + "ca.nq.w", {Dl});
+    wt(p + "ca.nk.w", {Dl});
+    wt(p + "ffn.0.w", {FFl, D});
+    wt(p + "ffn.0.b", {FFl});
+    wt(p + "ffn.2.w", {D, FFl});
     wt(p + "ffn.2.b", {D});
     if (h->layers[i].act >= 0) {
       const std::string a = p + "am.";
@@ -192,12 +200,12 @@ static int register_tensors(fw_handle* h) {
     };
     for (int i = 0; i < c.layers; ++i) {
       const std::string p = "b" + std::to_string(i) + ".";
-      der(p + "sa.qkv", 3 * D, D);
-      der(p + "sa.o", D, D);
-      der(p + "ca.q", D, D);
-      der(p + "ca.o", D, D);
-      der(p + "ffn.0", FF, D);
-      der(p + "ffn.2", D, FF);
+      der(p + "sa.qkv", 3 * Dl, D);
+      der(p + "sa.o", D, Dl);
+      der(p + "ca.q", Dl, D);
+      der(p + "ca.o", D, Dl);
+      der(p + "ffn.0", FFl, D);
+      der(p + "ffn.2", D, FFl);
       if (h->layers[i].act >= 0) {
         const std::string a = p + "am.";
         der(a + "mlp1", h->Mh, D);
@@ -210,8 +218,11 @@ static int register_tensors(fw_handle* h) {
     }
   }
   // session state (static.py:47-54, 280-281)
-  for (int i = 0; i < c.layers; ++i) add_tensor(h, "hk." + std::to_string(i), FW_KIND_STATE, FW_BF16, {1, h->L, h->H, h->HD});
-  for (int i = 0; i < c.layers; ++i) add_tensor(h, "hv." + std::to_string(i), FW_KIND_STATE, FW_BF16, {1, h->L, h->H, h->HD});
+  // (history window of hc chunks: hc slots of L rows; this rank's heads)
+  for (int i = 0; i < c.layers; ++i)
+    add_tensor(h, "hk." + std::to_string(i), FW_KIND_STATE, FW_BF16, {1, (int64_t)h->hc * h->L, h->Hl, h->HD});
+  for (int i = 0; i < c.layers; ++i)
+    add_tensor(h, "hv." + std::to_string(i), FW_KIND_STATE, FW_BF16, {1, (int64_t)h->hc * h->L, h->Hl, h->HD});
   const char* an[4] = {"mk.", "mv.", "kk.", "kv."};
   for (int t = 0; t < 4; ++t)
     for (int i = 0; i < c.layers; ++i)
@@ -238,11 +249,11 @@ static int register_tensors(fw_handle* h) {
   ws_add(h, "xs", (size_t)L * D * f4);
   ws_add(h, "y", (size_t)L * mx({D, h->Mh}) * bf);
   ws_add(h, "xbf", (size_t)L * D * bf);
-  ws_add(h, "q", (size_t)L * D * bf);
-  ws_add(h, "kcur", (size_t)L * D * bf);
-  ws_add(h, "vcur", (size_t)L * D * bf);
-  ws_add(h, "ao", (size_t)L * mx({D, A}) * bf);
-  ws_add(h, "hb", (size_t)L * mx({FF, 3 * A, h->Mh}) * bf);
+  ws_add(h, "q", (size_t)L * Dl * bf);
+  ws_add(h, "kcur", (size_t)L * Dl * bf);
+  ws_add(h, "vcur", (size_t)L * Dl * bf);
+  ws_add(h, "ao", (size_t)L * mx({Dl, A}) * bf);
+  ws_add(h, "hb", (size_t)L * mx({FFl, 3 * A, h->Mh}) * bf);
   ws_add(h, "hb2", (size_t)L * mx({h->Mh, A}) * bf);
   ws_add(h, "patchA", (size_t)L * h->Kp * bf);
   ws_add(h, "headout", (size_t)L * h->OUT * f4);
@@ -254,7 +265,7 @@ static int register_tensors(fw_handle* h) {
   ws_add(h, "ctx_h", (size_t)h->Ctx * h->Cd * bf);
   ws_add(h, "ctx_o", (size_t)h->Ctx * D * bf);
   ws_add(h, "ctx", (size_t)h->Ctx * D * bf);
-  ws_add(h, "ckv", (size_t)c.layers * 2 * h->Ctx * D * bf);
+  ws_add(h, "ckv", (size_t)c.layers * 2 * h->Ctx * Dl * bf);
   ws_add(h, "ke1", (size_t)h->KC * h->Kh * f4);
   ws_add(h, "ke", (size_t)h->KC * h->Kh * f4);
   ws_add(h, "kbkv", (size_t)h->F * 2 * A * f4);
@@ -272,8 +283,12 @@ static int register_tensors(fw_handle* h) {
   ws_add(h, "hmod", (size_t)2 * D * f4);
   ws_add(h, "consts", 64 * sizeof(int));
   if (h->fp8) {
-    ws_add(h, "a8", (size_t)L * mx({D, FF, h->Mh, A}));
+    ws_add(h, "a8", (size_t)L * mx({D, FFl, h->Mh, A}));
     ws_add(h, "sa", (size_t)L * f4);
+  }
+  if (h->tp > 1) {
+    ws_add(h, "part", (size_t)L * D * bf);
+    ws_add(h, "ss", (size_t)mx({L, h->Ctx}) * 2 * f4);
   }
   h->ws_bytes = (h->ws_bytes + 1023) & ~(size_t)1023;
   add_tensor(h, "workspace", FW_KIND_WORKSPACE, FW_U8, {(int64_t)h->ws_bytes});
@@ -291,6 +306,10 @@ static int config_check(const fw_config& c) {
     return FW_ESHAPE;
   for (int i = 0; i < c.n_action; ++i)
     if (c.action_blocks[i] < 0 || c.action_blocks[i] >= c.layers) return FW_EINVAL;
+  if (c.hist_chunks < 1 || c.tp_size < 1 || c.tp_rank < 0 || c.tp_rank >= c.tp_size) return FW_EINVAL;
+  if (c.tp_size > 1) {   // whole heads and 32-column FFN shards per rank; no action module
+    if (c.heads % c.tp_size || c.ffn % (32 * c.tp_size) || c.n_action) return FW_ESHAPE;
+  }
   return 0;
 }
 
@@ -400,6 +419,29 @@ static int ln_op(fw_handle* h, int M, int D, float eps, const float* shift, cons
   return ln_f32(h->xs, D, M, D, eps, shift, scale, w, b, h->y, D, s);
 }
 
+// q/k RMSNorm over the full hidden width (+ RoPE when `rope`) of x0 (and x1), in place; rows
+// of this rank's width Dl.  With tp > 1 the per-row sums of squares of the shards are
+// all-reduced first (static.py:208-209, 189-190 normalise over all heads).
+static int rms_norm_op(fw_handle* h, __nv_bfloat16* x0, __nv_bfloat16* x1, const __nv_bfloat16* w0,
+                       const __nv_bfloat16* w1, int M, const float2* rope, cudaStream_t s) {
+  const float eps = h->cfg.eps;
+  const int Dl = h->Dl;
+  if (h->tp == 1) return rms_rope2(x0, w0, x0, x1, w1, x1, Dl, M, Dl, eps, rope, h->HD, Dl, s);
+  FW_TRY(sumsq_rows(x0, x1, Dl, M, Dl, h->ss, s));
+  FW_TRY(tp_allreduce(h->comm, h->ss, (size_t)M * 2, FW_F32, s));
+  return rms_rope2_ss(x0, w0, x0, x1, w1, x1, Dl, M, Dl, h->ss, h->D, eps, rope, h->HD, Dl, s);
+}
+
+// After a row-parallel linear with tp > 1: all-reduce the partial outputs, then
+// xs += gate[frame] * (sum + bias) (the epilogue the GEMM applies itself at tp 1).
+static int tp_reduce(fw_handle* h, const std::string& bias, const float* gate, __nv_bfloat16* mirror,
+                     cudaStream_t s) {
+  if (h->tp == 1) return 0;
+  FW_TRY(tp_allreduce(h->comm, h->part, (size_t)h->L * h->D, FW_BF16, s));
+  // the adaLN gate is one row for every frame (e0 is per timestep; static.py:204, 220, 225)
+  return resid_add(h->xs, h->D, h->part, h->D, W(h, bias), gate, 0, h->S, mirror, h->L, h->D, s);
+}
+
 static int finalize(fw_handle* h) {
   for (auto& t : h->tensors)
     if (!t.ptr) return FW_ENOTBOUND;
@@ -448,11 +490,16 @@ static int finalize(fw_handle* h) {
   h->consts = (int*)WS("consts");
   h->a8 = (uint8_t*)WS("a8");
   h->sa = (float*)WS("sa");
+  h->part = (__nv_bfloat16*)WS("part");
+  h->ss = (float*)WS("ss");
   h->status = P<int>(h, "status");
-  // constant device tables: attention segment lengths {first, steady, cross}
-  int consts[8] = {0, h->L, h->L, h->L, h->Ctx, 0, 0, 0};
+  // device tables: attention segment lengths {first, steady, cross, steady with a history
+  // window of several chunks (rewritten per chunk by hist_meta)}
+  int consts[8] = {0, h->L, h->L, h->L, h->Ctx, 0, 0, h->L};
   if (cudaMemcpy(h->consts, consts, sizeof(consts), cudaMemcpyHostToDevice) != cudaSuccess) return FW_ECUDA;
-  const int L = h->L, D = h->D, Ctx = h->Ctx;
+  const int L = h->L, D = h->D, Ctx = h->Ctx, Dl = h->Dl, Hl = h->Hl;
+  const bool tp = h->tp > 1;
+  const int bnl = Dl % 256 ? 128 : 256;   // column tile that divides this rank's head width
   int* st = h->status;
   // patch embedding and head
   FW_TRY(make_gemm(h->patch, h->patchA, L, h->Kp, h->Kp, W(h, "patch.w"), D, h->Kp, pick_bn(D),
@@ -469,35 +516,41 @@ static int finalize(fw_handle* h) {
     const std::string p = "b" + std::to_string(i) + ".";
     const float* ee = h->ee + (size_t)i * 6 * D;
     {
-      GemmEpi e = epi_bf16(h->q, D, W(h, p + "sa.qkv.b"));
+      GemmEpi e = epi_bf16(h->q, Dl, W(h, p + "sa.qkv.b"));
       e.out[1] = h->kcur;
       e.out[2] = h->vcur;
-      e.seg_w = D;
-      FW_TRY(make_lin(h, ly.qkv, p + "sa.qkv", h->y, D, L, D, 3 * D, D, 256, e));
+      e.seg_w = Dl;
+      FW_TRY(make_lin(h, ly.qkv, p + "sa.qkv", h->y, D, L, D, 3 * Dl, D, bnl, e));
     }
-    FW_TRY(make_lin(h, ly.o, p + "sa.o", h->ao, D, L, D, D, D, 256,
-                    epi_resid(h->xs, D, W(h, p + "sa.o.b"), ee + 2 * D, nullptr)));
-    FW_TRY(make_lin(h, ly.caq, p + "ca.q", h->y, D, L, D, D, D, 256, epi_bf16(h->q, D, W(h, p + "ca.q.b"))));
+    // row-parallel linears: with tp > 1 the GEMM writes this rank's partial sum (no bias);
+    // the all-reduce and resid_add apply the bias and the gated residual once
+    auto row_par = [&](const char* name, const float* gate, __nv_bfloat16* mirror) {
+      return tp ? epi_bf16(h->part, D, nullptr) : epi_resid(h->xs, D, W(h, p + name + ".b"), gate, mirror);
+    };
+    FW_TRY(make_lin(h, ly.o, p + "sa.o", h->ao, Dl, L, Dl, D, Dl, 256, row_par("sa.o", ee + 2 * D, nullptr)));
+    FW_TRY(make_lin(h, ly.caq, p + "ca.q", h->y, D, L, D, Dl, D, bnl, epi_bf16(h->q, Dl, W(h, p + "ca.q.b"))));
     {
-      __nv_bfloat16* ck = h->ckv + (size_t)i * 2 * Ctx * D;
-      GemmEpi e = epi_bf16(ck, D, W(h, p + "ca.kv.b"));
-      e.out[1] = ck + (size_t)Ctx * D;
-      e.seg_w = D;
-      FW_TRY(make_gemm(ly.cakv, h->ctx, Ctx, D, D, W(h, p + "ca.kv.w"), 2 * D, D, 256, e, st));
+      __nv_bfloat16* ck = h->ckv + (size_t)i * 2 * Ctx * Dl;
+      GemmEpi e = epi_bf16(ck, Dl, W(h, p + "ca.kv.b"));
+      e.out[1] = ck + (size_t)Ctx * Dl;
+      e.seg_w = Dl;
+      FW_TRY(make_gemm(ly.cakv, h->ctx, Ctx, D, D, W(h, p + "ca.kv.w"), 2 * Dl, D, bnl, e, st));
     }
-    FW_TRY(make_lin(h, ly.cao, p + "ca.o", h->ao, D, L, D, D, D, 256,
-                    epi_resid(h->xs, D, W(h, p + "ca.o.b"), nullptr, ly.act >= 0 ? h->xbf : nullptr)));
-    FW_TRY(make_lin(h, ly.ff0, p + "ffn.0", h->y, D, L, D, h->FF, D, 256,
-                    epi_bf16(h->hb, h->FF, W(h, p + "ffn.0.b"), EPI_GELU_BF16)));
-    FW_TRY(make_lin(h, ly.ff2, p + "ffn.2", h->hb, h->FF, L, h->FF, D, h->FF, 256,
-                    epi_resid(h->xs, D, W(h, p + "ffn.2.b"), ee + 5 * D, nullptr)));
+    FW_TRY(make_lin(h, ly.cao, p + "ca.o", h->ao, Dl, L, Dl, D, Dl, 256,
+                    row_par("ca.o", nullptr, ly.act >= 0 ? h->xbf : nullptr)));
+    FW_TRY(make_lin(h, ly.ff0, p + "ffn.0", h->y, D, L, D, h->FFl, D, 256,
+                    epi_bf16(h->hb, h->FFl, W(h, p + "ffn.0.b"), EPI_GELU_BF16)));
+    FW_TRY(make_lin(h, ly.ff2, p + "ffn.2", h->hb, h->FFl, L, h->FFl, D, h->FFl, 256,
+                    row_par("ffn.2", ee + 5 * D, nullptr)));
     const void* hk = ptr_of(h, "hk." + std::to_string(i));
     const void* hv = ptr_of(h, "hv." + std::to_string(i));
-    FW_TRY(make_attn(ly.self_first, h->q, L, h->H, hk, hv, L, h->kcur, h->vcur, L, h->consts + 0, h->ao, st));
-    FW_TRY(make_attn(ly.self_steady, h->q, L, h->H, hk, hv, L, h->kcur, h->vcur, L, h->consts + 2, h->ao, st));
+    const int cap = h->hc * L;
+    FW_TRY(make_attn(ly.self_first, h->q, L, Hl, hk, hv, cap, h->kcur, h->vcur, L, h->consts + 0, h->ao, st));
+    FW_TRY(make_attn(ly.self_steady, h->q, L, Hl, hk, hv, cap, h->kcur, h->vcur, L,
+                     h->consts + (h->hc > 1 ? 6 : 2), h->ao, st));
     {
-      const __nv_bfloat16* ck = h->ckv + (size_t)i * 2 * Ctx * D;
-      FW_TRY(make_attn(ly.cross, h->q, L, h->H, ck, ck + (size_t)Ctx * D, Ctx, ck, ck + (size_t)Ctx * D, Ctx,
+      const __nv_bfloat16* ck = h->ckv + (size_t)i * 2 * Ctx * Dl;
+      FW_TRY(make_attn(ly.cross, h->q, L, Hl, ck, ck + (size_t)Ctx * Dl, Ctx, ck, ck + (size_t)Ctx * Dl, Ctx,
                        h->consts + 4, h->ao, st));
     }
     if (ly.act >= 0) {
@@ -549,11 +602,13 @@ static int prologue(fw_handle* h, cudaStream_t s) {
   FW_TRY(run(h->fc1, s));
   FW_TRY(run(h->fc2, s));
   FW_TRY(ln_bf16(h->ctx_o, D, Ctx, D, c.eps_ln, nullptr, nullptr, W(h, "img.ln1.w"), W(h, "img.ln1.b"), h->ctx, D, s));
+  const int Dl = h->Dl;
+  if (h->hc > 1) FW_TRY(hist_meta(P<int>(h, "chunk"), h->hc, h->L, h->consts + 6, s));
   for (int i = 0; i < c.layers; ++i) {
     const std::string p = "b" + std::to_string(i) + ".";
-    __nv_bfloat16* ck = h->ckv + (size_t)i * 2 * Ctx * D;
+    __nv_bfloat16* ck = h->ckv + (size_t)i * 2 * Ctx * Dl;
     FW_TRY(run(h->layers[i].cakv, s));
-    FW_TRY(rms_rope(ck, D, Ctx, D, c.eps, W(h, p + "ca.nk.w"), nullptr, 128, ck, D, s));
+    FW_TRY(rms_norm_op(h, ck, nullptr, W(h, p + "ca.nk.w"), nullptr, Ctx, nullptr, s));
   }
   for (int i = 0; i < c.layers; ++i) {
     const Layer& ly = h->layers[i];
@@ -633,25 +688,36 @@ static int forward(fw_handle* h, int step, int first, int write, const __nv_bflo
     const Layer& ly = h->layers[i];
     const std::string p = "b" + std::to_string(i) + ".";
     const float* ee = h->ee + (size_t)i * 6 * D;
+    const int Dl = h->Dl;
     FW_TRY(ln_op(h, L, D, c.eps, ee + 0 * D, ee + 1 * D, nullptr, nullptr, s));
     FW_TRY(run(ly.qkv, s));
-    FW_TRY(rms_rope2(h->q, W(h, p + "sa.nq.w"), h->q, h->kcur, W(h, p + "sa.nk.w"), h->kcur, D, L, D, c.eps, rope,
-                     h->HD, D, s));
+    FW_TRY(rms_norm_op(h, h->q, h->kcur, W(h, p + "sa.nq.w"), W(h, p + "sa.nk.w"), L, rope, s));
     FW_TRY(run(first ? ly.self_first : ly.self_steady, s));
     if (write) {   // the history is written after the attention read it (static.py:217-218)
-      FW_TRY(copy_bytes(ptr_of(h, "hk." + std::to_string(i)), h->kcur, (size_t)L * D * 2, s));
-      FW_TRY(copy_bytes(ptr_of(h, "hv." + std::to_string(i)), h->vcur, (size_t)L * D * 2, s));
+      const size_t bytes = (size_t)L * Dl * 2;
+      void* hk = ptr_of(h, "hk." + std::to_string(i));
+      void* hv = ptr_of(h, "hv." + std::to_string(i));
+      if (h->hc == 1) {
+        FW_TRY(copy_bytes(hk, h->kcur, bytes, s));
+        FW_TRY(copy_bytes(hv, h->vcur, bytes, s));
+      } else {   // slot k % window of the history ring
+        FW_TRY(slot_copy(hk, bytes, P<int>(h, "chunk"), h->hc, h->kcur, bytes, s));
+        FW_TRY(slot_copy(hv, bytes, P<int>(h, "chunk"), h->hc, h->vcur, bytes, s));
+      }
     }
-    FW_TRY(run_from(h, ly.o, h->ao, D, s));
+    FW_TRY(run_from(h, ly.o, h->ao, Dl, s));
+    FW_TRY(tp_reduce(h, p + "sa.o.b", ee + 2 * D, nullptr, s));
     FW_TRY(ln_op(h, L, D, c.eps, nullptr, nullptr, W(h, p + "n3.w"), W(h, p + "n3.b"), s));
     FW_TRY(run(ly.caq, s));
-    FW_TRY(rms_rope(h->q, D, L, D, c.eps, W(h, p + "ca.nq.w"), nullptr, h->HD, h->q, D, s));
+    FW_TRY(rms_norm_op(h, h->q, nullptr, W(h, p + "ca.nq.w"), nullptr, L, nullptr, s));
     FW_TRY(run(ly.cross, s));
-    FW_TRY(run_from(h, ly.cao, h->ao, D, s));
+    FW_TRY(run_from(h, ly.cao, h->ao, Dl, s));
+    FW_TRY(tp_reduce(h, p + "ca.o.b", nullptr, nullptr, s));
     if (ly.act >= 0) FW_TRY(action(h, i, first, write, s));
     FW_TRY(ln_op(h, L, D, c.eps, ee + 3 * D, ee + 4 * D, nullptr, nullptr, s));
     FW_TRY(run(ly.ff0, s));
-    FW_TRY(run_from(h, ly.ff2, h->hb, h->FF, s));
+    FW_TRY(run_from(h, ly.ff2, h->hb, h->FFl, s));
+    FW_TRY(tp_reduce(h, p + "ffn.2.b", ee + 5 * D, nullptr, s));
   }
   FW_TRY(ln_f32(h->xs, D, L, D, c.eps, h->hmod, h->hmod + D, nullptr, nullptr, h->y, D, s));
   FW_TRY(run(h->head, s));
@@ -696,6 +762,7 @@ const char* fw_strerror(int code) {
     case FW_ESTATE: return "call out of order (finalize first / already finalized)";
     case FW_ESIZE: return "bound buffer smaller than required";
     case FW_ESCRATCH: return "problem exceeds the fixed scratch of fw_linear_e4m3_noalloc (M*K <= 32 MiB, M <= 16384)";
+    case FW_ENCCL: return "NCCL unavailable (libnccl.so.2) or an NCCL call failed";
     default: return "unknown error";
   }
 }
@@ -729,6 +796,12 @@ int fw_create(const fw_config* cfg, fw_handle** out) {
   h->KC = c.frames * c.time_ratio + h->PAD - 3;
   h->lat_elems = (size_t)c.lat_ch * c.frames * c.lat_h * c.lat_w;
   h->fp8 = c.linear_fp8 != 0;
+  h->tp = c.tp_size;
+  h->tpr = c.tp_rank;
+  h->hc = c.hist_chunks;
+  h->Hl = c.heads / c.tp_size;
+  h->Dl = h->Hl * c.head_dim;
+  h->FFl = c.ffn / c.tp_size;
   h->layers.resize(c.layers);
   for (int j = 0; j < c.n_action; ++j) h->layers[c.action_blocks[j]].act = j;
   fw::register_tensors(h);
@@ -770,13 +843,13 @@ int fw_finalize(fw_handle* h) {
 
 int fw_chunk(fw_handle* h, int first, void* stream) {
   if (!h) return FW_EINVAL;
-  if (!h->finalized) return FW_ESTATE;
+  if (!h->finalized || (h->tp > 1 && !h->comm)) return FW_ESTATE;
   return fw::chunk(h, first, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int fw_prefill(fw_handle* h, int first, void* stream) {
   if (!h) return FW_EINVAL;
-  if (!h->finalized) return FW_ESTATE;
+  if (!h->finalized || (h->tp > 1 && !h->comm)) return FW_ESTATE;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   int rc = fw::prologue(h, s);
   if (rc) return rc;
@@ -786,7 +859,7 @@ int fw_prefill(fw_handle* h, int first, void* stream) {
 
 int fw_forward(fw_handle* h, int step, int first, int write, void* stream) {
   if (!h) return FW_EINVAL;
-  if (!h->finalized) return FW_ESTATE;
+  if (!h->finalized || (h->tp > 1 && !h->comm)) return FW_ESTATE;
   if (step < 0 || step > h->cfg.n_steps) return FW_EINVAL;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   int rc = fw::prologue(h, s);
@@ -796,7 +869,25 @@ int fw_forward(fw_handle* h, int step, int first, int write, void* stream) {
   return fw::forward(h, step, first, write, x, h->den, fw::P<__nv_bfloat16>(h, "out"), nullptr, 0.f, nullptr, s);
 }
 
-void fw_destroy(fw_handle* h) { delete h; }
+void fw_destroy(fw_handle* h) {
+  if (!h) return;
+  fw::tp_comm_destroy(h->comm);
+  delete h;
+}
+
+int fw_tp_unique_id(void* id128) { return fw::tp_unique_id(id128); }
+
+int fw_tp_init(fw_handle* h, const void* id128) {
+  if (!h || !id128) return FW_EINVAL;
+  if (h->tp == 1 || h->comm) return FW_ESTATE;
+  return fw::tp_comm_init(&h->comm, id128, h->tpr, h->tp);
+}
+
+int fw_tp_allreduce(fw_handle* h, void* buf, size_t count, int dtype, void* stream) {
+  if (!h) return FW_EINVAL;
+  if (!h->comm) return FW_ESTATE;
+  return fw::tp_allreduce(h->comm, buf, count, dtype, reinterpret_cast<cudaStream_t>(stream));
+}
 
 int fw_copy(void* dst, const void* src, size_t bytes, void* stream) {
   return fw::copy_bytes(dst, src, bytes, reinterpret_cast<cudaStream_t>(stream));

@@ -23,6 +23,21 @@ int rms_rope(const __nv_bfloat16* x, int ldx, int M, int D, float eps, const __n
 int rms_rope2(const __nv_bfloat16* x, const __nv_bfloat16* w, __nv_bfloat16* out, const __nv_bfloat16* x2,
               const __nv_bfloat16* w2, __nv_bfloat16* out2, int ldx, int M, int D, float eps, const float2* rope, int hd,
               int ldo, cudaStream_t s);
+// rms_rope2 with the sum of squares of each full row given (ss[row * 2 + t], all-reduced over
+// the tensor-parallel group) and d_full the full normalised width.
+int rms_rope2_ss(const __nv_bfloat16* x, const __nv_bfloat16* w, __nv_bfloat16* out, const __nv_bfloat16* x2,
+                 const __nv_bfloat16* w2, __nv_bfloat16* out2, int ldx, int M, int D, const float* ss, int d_full,
+                 float eps, const float2* rope, int hd, int ldo, cudaStream_t s);
+// ss[row * 2 + t] = sum of squares of row `row` of x0 (t = 0) and x1 (t = 1, optional).
+int sumsq_rows(const __nv_bfloat16* x0, const __nv_bfloat16* x1, int ld, int M, int D, float* ss, cudaStream_t s);
+// xs += gate[frame * gate_stride] * (p + bias) (gate, bias, mirror optional), for all-reduced
+// row-parallel outputs.
+int resid_add(float* xs, int ldx, const __nv_bfloat16* p, int ldp, const __nv_bfloat16* bias, const float* gate,
+              int gate_stride, int rows_per_frame, __nv_bfloat16* mirror, int M, int D, cudaStream_t s);
+// History window of several chunks: meta = {min(k, window) * L, L}; slot_copy writes slot k % window.
+int hist_meta(const int* chunk, int window, int L, int* meta, cudaStream_t s);
+int slot_copy(void* dst_base, size_t slot_bytes, const int* chunk, int window, const void* src, size_t bytes,
+              cudaStream_t s);
 int rope_tables(const int* chunk, int F, int th, int tw, int hd, double theta, float2* table, int act_hd,
                 float* act_cos, float* act_sin, cudaStream_t s);
 int smallm_linear_f32(const float* x, int ldx, int M, const __nv_bfloat16* W, int ldw, const __nv_bfloat16* b, int N,

@@ -60,21 +60,38 @@ class SessionState(list):
 
 
 class B200StaticMG:
+    """Session runtime.  ``tp_group`` (a ``torch.distributed`` process group, or ``True`` for
+    the default group) shards the model over the group's ranks, one GPU each (BASELINE
+    configs[4]): every rank constructs its object at the same time with the same arguments;
+    ``weights`` is then either the full state dict (sharded here) or already this rank's part
+    (``weights.shard_state_dict``).  Inputs, outputs and the call sequence are the same on
+    every rank; the output latent is identical on all ranks."""
+
     def __init__(self, cfg: DiTConfig = MG2, weights: Optional[Dict[str, torch.Tensor]] = None, device="cuda",
-                 seed: int = 0):
+                 seed: int = 0, tp_group=None):
         cfg.validate()
         self.cfg = cfg
         self.dev = torch.device(device)
         if self.dev.type != "cuda":
             raise RuntimeError("B200StaticMG runs on a CUDA device (sm_100a) only")
+        self.tp_size, self.tp_rank = 1, 0
+        if tp_group is not None:
+            import torch.distributed as dist
+            grp = None if tp_group is True else tp_group
+            self.tp_size, self.tp_rank = dist.get_world_size(grp), dist.get_rank(grp)
+        from .weights import shard_state_dict, synthetic_state_dict
         if weights is None:
-            from .weights import synthetic_state_dict
-            weights = synthetic_state_dict(cfg, seed, device=self.dev)
+            weights = synthetic_state_dict(cfg, seed, device=self.dev,
+                                           shard=(self.tp_rank, self.tp_size) if self.tp_size > 1 else None)
+        elif self.tp_size > 1 and weights[f"b0.sa.q.w"].shape[0] == cfg.dim:
+            weights = shard_state_dict(cfg, weights, self.tp_rank, self.tp_size)
         packed = pack_weights(cfg, weights)
-        self._ccfg = _lib.make_config(cfg)
+        self._ccfg = _lib.make_config(cfg, self.tp_size, self.tp_rank)
         h = ctypes.c_void_p()
         check(lib().fw_create(ctypes.byref(self._ccfg), ctypes.byref(h)), "fw_create")
         self._h = h
+        if self.tp_size > 1:
+            self._tp_connect(tp_group)
         self.buffers: Dict[str, torch.Tensor] = {}
         infos = []
         for i in range(lib().fw_tensor_count(h)):
@@ -119,6 +136,21 @@ class B200StaticMG:
         self.steps = [int(t) for t in cfg.steps]
         self.images: Dict[str, Dict[str, torch.Tensor]] = {}
         self.graphs, self.cur_img = {}, None
+
+    def _tp_connect(self, tp_group) -> None:
+        """Create the engine's NCCL communicator: the group's first rank draws the id, the
+        host process group broadcasts it, every rank joins (blocking, collective)."""
+        import torch.distributed as dist
+        grp = None if tp_group is True else tp_group
+        idbuf = ctypes.create_string_buffer(128)
+        if self.tp_rank == 0:
+            check(lib().fw_tp_unique_id(idbuf), "fw_tp_unique_id")
+        obj = [idbuf.raw if self.tp_rank == 0 else None]
+        src = dist.get_global_rank(grp, 0) if grp is not None else 0
+        dist.broadcast_object_list(obj, src=src, group=grp, device=torch.device("cpu") if
+                                   dist.get_backend(grp) == "gloo" else self.dev)
+        with torch.cuda.device(self.dev):
+            check(lib().fw_tp_init(self._h, obj[0]), "fw_tp_init")
 
     def __del__(self):
         h = getattr(self, "_h", None)

@@ -112,9 +112,46 @@ def _tensor_seed(seed: int, name: str) -> int:
     return int.from_bytes(h[:8], "little") & ((1 << 63) - 1)
 
 
-def synthetic_state_dict(cfg: DiTConfig, seed: int = 0, device="cpu",
-                         dtype=torch.bfloat16) -> Dict[str, torch.Tensor]:
-    """Seeded weights, one generator per tensor. Values depend on the device's RNG."""
+_COL_PARALLEL = (".sa.q.", ".sa.k.", ".sa.v.", ".ca.q.", ".ca.k.", ".ca.v.", ".sa.nq.", ".sa.nk.",
+                 ".ca.nq.", ".ca.nk.")
+_ROW_PARALLEL = (".sa.o.w", ".ca.o.w")
+
+
+def shard_tensor(cfg: DiTConfig, name: str, t: torch.Tensor, rank: int, world: int) -> torch.Tensor:
+    """This rank's part of one flat-named tensor under tensor parallelism over `world` ranks.
+
+    Attention is split by heads: the q/k/v (self and cross) rows and q/k RMSNorm weights of
+    heads [rank * heads / world, ...) and the matching input columns of the output
+    projections.  The FFN is split by hidden columns: rows of ffn.0, input columns of ffn.2.
+    Output-projection biases, norms outside attention, embeddings, the head and the adaLN
+    tables stay whole (replicated)."""
+    if world == 1 or not name.startswith("b"):
+        return t
+    dl, fl = cfg.dim // world, cfg.ffn // world
+    if any(k in name for k in _COL_PARALLEL):
+        return t[rank * dl:(rank + 1) * dl]
+    if name.endswith(_ROW_PARALLEL):
+        return t[:, rank * dl:(rank + 1) * dl]
+    if ".ffn.0." in name:
+        return t[rank * fl:(rank + 1) * fl]
+    if name.endswith(".ffn.2.w"):
+        return t[:, rank * fl:(rank + 1) * fl]
+    return t
+
+
+def shard_state_dict(cfg: DiTConfig, sd: Dict[str, torch.Tensor], rank: int, world: int) -> Dict[str, torch.Tensor]:
+    """:func:`shard_tensor` over a whole state dict (contiguous copies of the local parts)."""
+    if cfg.heads % world or cfg.ffn % world:
+        raise ValueError(f"{world} ranks do not divide {cfg.heads} heads / ffn {cfg.ffn}")
+    return {k: shard_tensor(cfg, k, v, rank, world).contiguous() for k, v in sd.items()}
+
+
+def synthetic_state_dict(cfg: DiTConfig, seed: int = 0, device="cpu", dtype=torch.bfloat16,
+                         shard=None) -> Dict[str, torch.Tensor]:
+    """Seeded weights, one generator per tensor. Values depend on the device's RNG.
+
+    ``shard=(rank, world)`` keeps only this rank's tensor-parallel part of each tensor as it is
+    drawn (same values as sharding the full dict; the full model is never resident)."""
     cfg.validate()
     out: Dict[str, torch.Tensor] = {}
     for name, shape, kind, fi, fo in param_specs(cfg):
@@ -132,7 +169,10 @@ def synthetic_state_dict(cfg: DiTConfig, seed: int = 0, device="cpu",
             t = torch.randn(shape, generator=g, device=device) / cfg.dim ** 0.5
         else:  # pragma: no cover
             raise ValueError(kind)
-        out[name] = t.to(dtype)
+        t = t.to(dtype)
+        if shard is not None:
+            t = shard_tensor(cfg, name, t, *shard).contiguous()
+        out[name] = t
     return out
 
 

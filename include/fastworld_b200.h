@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define FW_ABI_VERSION 1
+#define FW_ABI_VERSION 2
 
 /* error codes */
 #define FW_OK 0
@@ -43,6 +43,7 @@ extern "C" {
 #define FW_ESTATE (-7)      /* call out of order (e.g. launch before fw_finalize) */
 #define FW_ESIZE (-8)       /* bound buffer smaller than required */
 #define FW_ESCRATCH (-9)    /* problem larger than the fixed scratch of fw_linear_e4m3_noalloc */
+#define FW_ENCCL (-10)      /* NCCL unavailable or an NCCL call failed */
 
 /* tensor kinds (fw_tensor_info.kind) */
 #define FW_KIND_WEIGHT 0
@@ -76,6 +77,14 @@ typedef struct fw_config {
   float eps_ln;                                       /* img_emb / mouse_mlp LayerNorm eps */
   float rope_theta;
   int linear_fp8;                                     /* 1: block linears in e4m3 */
+  /* KV history window in chunks (1 = MG2: the previous chunk only).  With W > 1 the history
+   * buffer holds W chunk slots; chunk k's context forward writes slot k % W and a steady
+   * chunk attends to the min(k, W) filled slots and the current chunk. */
+  int hist_chunks;
+  /* Tensor parallelism: this handle computes heads
+   * [tp_rank * heads / tp_size, ...) and the same share of the FFN columns; tensors are
+   * registered with the local widths.  tp_size 1 = the whole model on one GPU. */
+  int tp_size, tp_rank;
 } fw_config;
 
 typedef struct fw_tensor_info {
@@ -110,7 +119,22 @@ int fw_prefill(fw_handle* h, int first, void* stream);
 /* One forward (static.py:194-230) at timestep index `step` (n_steps = the context forward
  * at t = 0) from latent x_cur into den; write != 0 updates the history. */
 int fw_forward(fw_handle* h, int step, int first, int write, void* stream);
+/* Destroys the handle and, with tp_size > 1, its NCCL communicator (release every CUDA graph
+ * that captured this handle's launches first). */
 void fw_destroy(fw_handle* h);
+
+/* ---- tensor parallelism (no counterpart in the reference, whose runtimes are single-GPU;
+ * BASELINE configs[4]) ----
+ * NCCL is loaded at run time (libnccl.so.2: the copy already in the process if any).
+ * fw_tp_unique_id: on one rank, 128 bytes to broadcast to every rank of the group.
+ * fw_tp_init: on every rank (collective, blocking), after fw_create and before the first
+ * launch; the engine then all-reduces (sum) the row-parallel partial outputs of sa.o,
+ * ca.o and ffn.2 and the per-token sums of squares of the q/k RMSNorms over the group,
+ * enqueued on the launch stream (capturable). */
+int fw_tp_unique_id(void* id128);
+int fw_tp_init(fw_handle* h, const void* id128);
+/* In-place sum all-reduce over the handle's group (dtype FW_BF16 or FW_F32); for tests. */
+int fw_tp_allreduce(fw_handle* h, void* buf, size_t count, int dtype, void* stream);
 
 /* ---- checkpoint copies (state save / restore / migrate; static.py:273-278) ----
  * Vectorised device copy of `bytes` (16-byte aligned pointers; any size).  `src` may be a

@@ -173,7 +173,8 @@ class Oracle:
     def new_state(self) -> Dict[str, object]:
         c = self.cfg
         L, H, D = c.tokens, c.heads, c.head_dim
-        st = {"hk": torch.zeros(c.layers, L, H, D), "hv": torch.zeros(c.layers, L, H, D),
+        W = c.hist_chunks   # history window: W slots of one chunk's keys
+        st = {"hk": torch.zeros(c.layers, W * L, H, D), "hv": torch.zeros(c.layers, W * L, H, D),
               "mk": {}, "mv": {}, "kk": {}, "kv": {}}
         for i in c.action_blocks:
             st["mk"][i] = torch.zeros(c.tok_per_frame, c.frames, c.act_heads, c.act_head_dim)
@@ -294,12 +295,17 @@ class Oracle:
         v = self.lin(y_in, f"{p}.sa.v").view(-1, c.heads, c.head_dim)
         rq, rk = self.r(apply_rope(q, fi)), self.i(apply_rope(k, fi))
         v = self.i(v)
+        L, Wn, k_idx = c.tokens, c.hist_chunks, s // c.frames
+        # keys: the filled history slots (one chunk for MG2, static.py:213-216), then the
+        # current chunk; with a window of Wn > 1 chunks, chunk k has min(k, Wn) filled slots
+        n0 = L if Wn == 1 else min(k_idx, Wn) * L
         if first:
             y = attention(rq, rk, v)
         else:
-            y = attention(rq, torch.cat([st["hk"][i], rk], 0), torch.cat([st["hv"][i], v], 0))
-        if write:
-            st["hk"][i], st["hv"][i] = rk, v
+            y = attention(rq, torch.cat([st["hk"][i][:n0], rk], 0), torch.cat([st["hv"][i][:n0], v], 0))
+        if write:   # ring slot k % Wn (static.py:217-218 for Wn = 1)
+            sl = slice((k_idx % Wn) * L, (k_idx % Wn + 1) * L)
+            st["hk"][i][sl], st["hv"][i][sl] = rk, v
         y = self.lin(self.r(y).reshape(-1, c.dim), f"{p}.sa.o")
         xs = xs + per_frame(y, lambda t: t * ee[2][:, None])
         xs = xs + self.cross(i, self.r(layer_norm(xs, W[f"{p}.n3.w"], W[f"{p}.n3.b"], c.eps)), ctx_kv)

@@ -33,7 +33,7 @@ def test_exports_every_declared_symbol(L):
 
 def test_abi_version_and_strerror(L):
     from fastworld_b200 import _lib
-    assert L.fw_abi_version() == 1
+    assert L.fw_abi_version() == 2
     assert _lib.strerror(0) == "ok"
     assert "not bound" in _lib.strerror(-5)
     assert _lib.strerror(-999) == "unknown error"
