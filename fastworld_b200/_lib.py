@@ -73,6 +73,8 @@ _SIGS = {
                                           ctypes.c_void_p]),
     "fw_tp_unique_id": (ctypes.c_int, [ctypes.c_char_p]),
     "fw_tp_init": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_char_p]),
+    "fw_tp_peers": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p), ctypes.c_int]),
+    "fw_tp_reduce_once": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
     "fw_tp_allreduce": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int,
                                        ctypes.c_void_p]),
     "fw_attention": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,

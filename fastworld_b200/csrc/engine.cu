@@ -62,6 +62,8 @@ struct fw_handle {
   int Hl, Dl, FFl;
   int tp = 1, tpr = 0, hc = 1;   // tensor-parallel size / rank, history window in chunks
   void* comm = nullptr;           // NCCL communicator (tp > 1)
+  fw::TpPeers peers;              // the other ranks' workspaces (tp > 1, after fw_tp_peers)
+  bool use_peers = false;         // reductions over peer memory instead of NCCL
   __nv_bfloat16* part = nullptr;  // [L, D] partial output of a row-parallel linear (tp > 1)
   float* ss = nullptr;            // [max(L, Ctx), 2] sums of squares for the sharded RMSNorms
   size_t lat_elems;
@@ -289,6 +291,12 @@ static int register_tensors(fw_handle* h) {
   if (h->tp > 1) {
     ws_add(h, "part", (size_t)L * D * bf);
     ws_add(h, "ss", (size_t)mx({L, h->Ctx}) * 2 * f4);
+    // peer-memory reductions (tp_reduce.cu): reduced sums, flags, gathered sums of squares,
+    // per-CTA call counters; other ranks address these at the same offsets of their mapping
+    ws_add(h, "tp.red", (size_t)L * D * bf);
+    ws_add(h, "tp.flags", (size_t)3 * TP_MAX_RANKS * TP_MAX_CTAS * sizeof(unsigned));
+    ws_add(h, "tp.gat", (size_t)2 * TP_MAX_RANKS * mx({L, h->Ctx}) * 2 * f4);
+    ws_add(h, "tp.epoch", (size_t)2 * TP_MAX_CTAS * sizeof(unsigned));
   }
   h->ws_bytes = (h->ws_bytes + 1023) & ~(size_t)1023;
   add_tensor(h, "workspace", FW_KIND_WORKSPACE, FW_U8, {(int64_t)h->ws_bytes});
@@ -428,15 +436,20 @@ static int rms_norm_op(fw_handle* h, __nv_bfloat16* x0, __nv_bfloat16* x1, const
   const int Dl = h->Dl;
   if (h->tp == 1) return rms_rope2(x0, w0, x0, x1, w1, x1, Dl, M, Dl, eps, rope, h->HD, Dl, s);
   FW_TRY(sumsq_rows(x0, x1, Dl, M, Dl, h->ss, s));
-  FW_TRY(tp_allreduce(h->comm, h->ss, (size_t)M * 2, FW_F32, s));
+  if (h->use_peers)
+    FW_TRY(tp_sumsq(h->peers, h->ss, M, h->status, s));
+  else
+    FW_TRY(tp_allreduce(h->comm, h->ss, (size_t)M * 2, FW_F32, s));
   return rms_rope2_ss(x0, w0, x0, x1, w1, x1, Dl, M, Dl, h->ss, h->D, eps, rope, h->HD, Dl, s);
 }
 
 // After a row-parallel linear with tp > 1: all-reduce the partial outputs, then
-// xs += gate[frame] * (sum + bias) (the epilogue the GEMM applies itself at tp 1).
-static int tp_reduce(fw_handle* h, const std::string& bias, const float* gate, __nv_bfloat16* mirror,
-                     cudaStream_t s) {
+// xs += gate[frame] * (sum + bias) (the epilogue the GEMM applies itself at tp 1).  With the
+// peers mapped this is one fused kernel over NVLink; otherwise NCCL + resid_add.
+static int row_parallel_done(fw_handle* h, const std::string& bias, const float* gate, __nv_bfloat16* mirror,
+                             cudaStream_t s) {
   if (h->tp == 1) return 0;
+  if (h->use_peers) return tp_reduce(h->peers, h->L, h->D, W(h, bias), gate, h->xs, mirror, h->status, s);
   FW_TRY(tp_allreduce(h->comm, h->part, (size_t)h->L * h->D, FW_BF16, s));
   // the adaLN gate is one row for every frame (e0 is per timestep; static.py:204, 220, 225)
   return resid_add(h->xs, h->D, h->part, h->D, W(h, bias), gate, 0, h->S, mirror, h->L, h->D, s);
@@ -706,18 +719,18 @@ static int forward(fw_handle* h, int step, int first, int write, const __nv_bflo
       }
     }
     FW_TRY(run_from(h, ly.o, h->ao, Dl, s));
-    FW_TRY(tp_reduce(h, p + "sa.o.b", ee + 2 * D, nullptr, s));
+    FW_TRY(row_parallel_done(h, p + "sa.o.b", ee + 2 * D, nullptr, s));
     FW_TRY(ln_op(h, L, D, c.eps, nullptr, nullptr, W(h, p + "n3.w"), W(h, p + "n3.b"), s));
     FW_TRY(run(ly.caq, s));
     FW_TRY(rms_norm_op(h, h->q, nullptr, W(h, p + "ca.nq.w"), nullptr, L, nullptr, s));
     FW_TRY(run(ly.cross, s));
     FW_TRY(run_from(h, ly.cao, h->ao, Dl, s));
-    FW_TRY(tp_reduce(h, p + "ca.o.b", nullptr, nullptr, s));
+    FW_TRY(row_parallel_done(h, p + "ca.o.b", nullptr, nullptr, s));
     if (ly.act >= 0) FW_TRY(action(h, i, first, write, s));
     FW_TRY(ln_op(h, L, D, c.eps, ee + 3 * D, ee + 4 * D, nullptr, nullptr, s));
     FW_TRY(run(ly.ff0, s));
     FW_TRY(run_from(h, ly.ff2, h->hb, h->FFl, s));
-    FW_TRY(tp_reduce(h, p + "ffn.2.b", ee + 5 * D, nullptr, s));
+    FW_TRY(row_parallel_done(h, p + "ffn.2.b", ee + 5 * D, nullptr, s));
   }
   FW_TRY(ln_f32(h->xs, D, L, D, c.eps, h->hmod, h->hmod + D, nullptr, nullptr, h->y, D, s));
   FW_TRY(run(h->head, s));
@@ -843,13 +856,13 @@ int fw_finalize(fw_handle* h) {
 
 int fw_chunk(fw_handle* h, int first, void* stream) {
   if (!h) return FW_EINVAL;
-  if (!h->finalized || (h->tp > 1 && !h->comm)) return FW_ESTATE;
+  if (!h->finalized || (h->tp > 1 && !h->comm && !h->use_peers)) return FW_ESTATE;
   return fw::chunk(h, first, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int fw_prefill(fw_handle* h, int first, void* stream) {
   if (!h) return FW_EINVAL;
-  if (!h->finalized || (h->tp > 1 && !h->comm)) return FW_ESTATE;
+  if (!h->finalized || (h->tp > 1 && !h->comm && !h->use_peers)) return FW_ESTATE;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   int rc = fw::prologue(h, s);
   if (rc) return rc;
@@ -859,7 +872,7 @@ int fw_prefill(fw_handle* h, int first, void* stream) {
 
 int fw_forward(fw_handle* h, int step, int first, int write, void* stream) {
   if (!h) return FW_EINVAL;
-  if (!h->finalized || (h->tp > 1 && !h->comm)) return FW_ESTATE;
+  if (!h->finalized || (h->tp > 1 && !h->comm && !h->use_peers)) return FW_ESTATE;
   if (step < 0 || step > h->cfg.n_steps) return FW_EINVAL;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   int rc = fw::prologue(h, s);
@@ -881,6 +894,40 @@ int fw_tp_init(fw_handle* h, const void* id128) {
   if (!h || !id128) return FW_EINVAL;
   if (h->tp == 1 || h->comm) return FW_ESTATE;
   return fw::tp_comm_init(&h->comm, id128, h->tpr, h->tp);
+}
+
+int fw_tp_peers(fw_handle* h, void* const* ws_bases, int n) {
+  if (!h || !ws_bases) return FW_EINVAL;
+  if (h->tp == 1 || !h->finalized) return FW_ESTATE;
+  if (n != h->tp || n > fw::TP_MAX_RANKS) return FW_EINVAL;
+  const uint8_t* own = fw::P<uint8_t>(h, "workspace");
+  if (ws_bases[h->tpr] != own) return FW_EINVAL;
+  auto off = [&](const char* name) -> size_t {
+    for (auto& p : h->ws_off)
+      if (p.first == name) return p.second;
+    return (size_t)-1;
+  };
+  fw::TpPeers& P = h->peers;
+  P.tp = h->tp;
+  P.rank = h->tpr;
+  P.gat_rows = h->L > h->Ctx ? h->L : h->Ctx;
+  for (int j = 0; j < n; ++j) {
+    uint8_t* b = reinterpret_cast<uint8_t*>(ws_bases[j]);
+    if (!b || (reinterpret_cast<uintptr_t>(b) & 255u)) return FW_EALIGN;
+    P.part[j] = reinterpret_cast<const __nv_bfloat16*>(b + off("part"));
+    P.red[j] = reinterpret_cast<__nv_bfloat16*>(b + off("tp.red"));
+    P.flags[j] = reinterpret_cast<unsigned*>(b + off("tp.flags"));
+    P.gat[j] = reinterpret_cast<float*>(b + off("tp.gat"));
+  }
+  P.epoch = reinterpret_cast<unsigned*>(const_cast<uint8_t*>(own) + off("tp.epoch"));
+  h->use_peers = true;
+  return 0;
+}
+
+int fw_tp_reduce_once(fw_handle* h, void* stream) {
+  if (!h) return FW_EINVAL;
+  if (h->tp == 1 || !h->finalized || !(h->use_peers || h->comm)) return FW_ESTATE;
+  return fw::row_parallel_done(h, "b0.sa.o.b", nullptr, nullptr, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int fw_tp_allreduce(fw_handle* h, void* buf, size_t count, int dtype, void* stream) {

@@ -1,5 +1,7 @@
-// NCCL wrappers for tensor parallelism (tp.cu).  All return 0 or a negative FW_E* code.
+// Tensor parallelism: NCCL wrappers (tp.cu) and the peer-memory reductions (tp_reduce.cu).
+// All functions return 0 or a negative FW_E* code.
 #pragma once
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 
@@ -10,5 +12,27 @@ int tp_comm_init(void** comm, const void* id128, int rank, int world);
 // In-place sum over the communicator's ranks; dtype FW_BF16 or FW_F32.
 int tp_allreduce(void* comm, void* buf, size_t count, int dtype, cudaStream_t s);
 void tp_comm_destroy(void* comm);
+
+constexpr int TP_MAX_RANKS = 8;
+constexpr int TP_MAX_CTAS = 160;   // >= SMs per GPU; CTA c of every rank pairs with CTA c of the others
+
+// Every rank's buffers as seen from this rank (index = rank; own rank = local pointers, the
+// others mapped peer memory).
+struct TpPeers {
+  int tp = 0, rank = 0;
+  int gat_rows = 0;                              // rows per gather slot (>= every M of tp_sumsq)
+  const __nv_bfloat16* part[TP_MAX_RANKS] = {};  // [L, D] bf16 partial sums of a row-parallel linear
+  __nv_bfloat16* red[TP_MAX_RANKS] = {};         // [L, D] bf16 reduced sums (+ bias)
+  unsigned* flags[TP_MAX_RANKS] = {};            // [3][TP_MAX_RANKS][TP_MAX_CTAS] epochs
+  float* gat[TP_MAX_RANKS] = {};                 // [2][TP_MAX_RANKS][gat_rows][2] gathered sums of squares
+  unsigned* epoch = nullptr;                     // this rank's [2][TP_MAX_CTAS] call counters
+};
+
+// xs[L, D] += gate * (sum over ranks of part + bias) on every rank (two-shot over NVLink);
+// mirror (optional) = bf16 copy of the new xs.  gate: one [D] row for all tokens, or null.
+int tp_reduce(const TpPeers& p, int L, int D, const __nv_bfloat16* bias, const float* gate, float* xs,
+              __nv_bfloat16* mirror, int* status, cudaStream_t s);
+// ss[M, 2] (fp32, in place) = sum over ranks of ss.
+int tp_sumsq(const TpPeers& p, float* ss, int M, int* status, cudaStream_t s);
 
 }  // namespace fw

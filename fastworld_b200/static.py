@@ -68,7 +68,7 @@ class B200StaticMG:
     every rank; the output latent is identical on all ranks."""
 
     def __init__(self, cfg: DiTConfig = MG2, weights: Optional[Dict[str, torch.Tensor]] = None, device="cuda",
-                 seed: int = 0, tp_group=None):
+                 seed: int = 0, tp_group=None, tp_peers: bool = True):
         cfg.validate()
         self.cfg = cfg
         self.dev = torch.device(device)
@@ -123,6 +123,9 @@ class B200StaticMG:
             check(lib().fw_bind(h, name.encode(), ptr(t), t.numel() * t.element_size()), f"fw_bind({name})")
         check(lib().fw_finalize(h), "fw_finalize")
         torch.cuda.synchronize(self.dev)
+        self._peer_maps = []
+        if self.tp_size > 1 and tp_peers:
+            self._tp_map_peers(tp_group)
         B = self.buffers
         self.hk = [B[f"hk.{i}"] for i in range(cfg.layers)]
         self.hv = [B[f"hv.{i}"] for i in range(cfg.layers)]
@@ -152,7 +155,34 @@ class B200StaticMG:
         with torch.cuda.device(self.dev):
             check(lib().fw_tp_init(self._h, obj[0]), "fw_tp_init")
 
+    def _tp_map_peers(self, tp_group) -> None:
+        """Map every other rank's engine workspace into this process (CUDA IPC, peer access) and
+        hand the bases to the engine, which then reduces over NVLink with its own kernels
+        instead of NCCL (``fw_tp_peers``)."""
+        import torch.distributed as dist
+        from . import migrate
+        grp = None if tp_group is True else tp_group
+        ws = self.buffers["workspace"]
+        descs = [None] * self.tp_size
+        dist.all_gather_object(descs, migrate.export_blob(ws), group=grp)
+        bases = (ctypes.c_void_p * self.tp_size)()
+        for j, d in enumerate(descs):
+            if j == self.tp_rank:
+                bases[j] = ws.data_ptr()
+                continue
+            pb = migrate.PeerBuffer(d, self.dev).__enter__()
+            self._peer_maps.append(pb)
+            bases[j] = pb.ptr
+        check(lib().fw_tp_peers(self._h, bases, self.tp_size), "fw_tp_peers")
+        dist.barrier(group=grp)   # every rank mapped before anyone launches
+
     def __del__(self):
+        for pb in getattr(self, "_peer_maps", []):
+            try:
+                pb.__exit__(None, None, None)
+            except Exception:
+                pass
+        self._peer_maps = []
         h = getattr(self, "_h", None)
         if h is not None and h.value:
             lib().fw_destroy(h)

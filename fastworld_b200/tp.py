@@ -11,8 +11,9 @@ history window; the timed chunks are steady (keys = 2 history chunks + the curre
 
 Reports (rank 0, one JSON line): steady chunk latency (CUDA events, max over ranks), frames per
 second (12 pixel frames per chunk), algorithmic TFLOP/s per GPU and as a fraction of the
-measured bf16 peak, and the time of one standalone all-reduce of a [tokens, dim] bf16 partial
-(the collective of a row-parallel linear) on the same communicator.
+measured bf16 peak, and the time of one standalone NCCL all-reduce of a [tokens, dim] bf16 partial
+(the collective of a row-parallel linear) for comparison.  ``--nccl`` runs the engine's
+collectives on NCCL instead of its own peer-memory kernels.
 """
 from __future__ import annotations
 
@@ -30,6 +31,7 @@ def main():
     ap.add_argument("--chunks", type=int, default=3, help="timed steady chunks")
     ap.add_argument("--warmup", type=int, default=1, help="untimed steady chunks after chunks 0 and 1")
     ap.add_argument("--graph", action="store_true", help="replay captured CUDA graphs instead of eager launches")
+    ap.add_argument("--nccl", action="store_true", help="NCCL collectives instead of the peer-memory kernels")
     a = ap.parse_args()
     rank, world, local = (int(os.environ.get(k, d)) for k, d in (("RANK", 0), ("WORLD_SIZE", 1), ("LOCAL_RANK", 0)))
     torch.cuda.set_device(local)
@@ -40,7 +42,7 @@ def main():
     from .static import B200StaticMG
     cfg = PRESETS[a.config]
     dev = torch.device(f"cuda:{local}")
-    S = B200StaticMG(cfg, device=dev, seed=0, tp_group=True if world > 1 else None)
+    S = B200StaticMG(cfg, device=dev, seed=0, tp_group=True if world > 1 else None, tp_peers=not a.nccl)
     n = 2 + a.warmup + a.chunks
     S.add_image("img0", seed=7, max_chunks=n + 1)
     path = [("img0", ("w", "u"))] * (n + 1)
@@ -65,7 +67,7 @@ def main():
         ms.append(e0.elapsed_time(e1))
     status = S.device_status()
     # one all-reduce of a row-parallel partial on the engine's communicator
-    ar_ms = None
+    ar_ms = rp_ms = None
     if world > 1:
         buf = torch.zeros(cfg.tokens, cfg.dim, dtype=torch.bfloat16, device=dev)
         st = torch.cuda.current_stream()
@@ -80,7 +82,16 @@ def main():
         e1.record()
         torch.cuda.synchronize()
         ar_ms = e0.elapsed_time(e1) / 10
-    res = {"ms": ms, "status": status, "ar_ms": ar_ms}
+        # one row-parallel reduction step exactly as the engine runs it (sum + bias + residual)
+        for _ in range(3):
+            _lib.check(_lib.lib().fw_tp_reduce_once(S._h, _lib.stream_ptr(st)), "fw_tp_reduce_once")
+        e0.record()
+        for _ in range(10):
+            _lib.check(_lib.lib().fw_tp_reduce_once(S._h, _lib.stream_ptr(st)), "fw_tp_reduce_once")
+        e1.record()
+        torch.cuda.synchronize()
+        rp_ms = e0.elapsed_time(e1) / 10
+    res = {"ms": ms, "status": status, "ar_ms": ar_ms, "rp_ms": rp_ms if world > 1 else None}
     allres = [res]
     if world > 1:
         allres = [None] * world
@@ -95,9 +106,11 @@ def main():
         ar = allres[0]["ar_ms"]
         line = {"workload": "wan14b tensor-parallel chunk (BASELINE configs[4])", "config": cfg.name, "tp": world,
                 "tokens": cfg.tokens, "history_tokens": cfg.hist_chunks * cfg.tokens, "graph": a.graph,
+                "collectives": ("nccl" if a.nccl else "peer-memory kernels") if world > 1 else None,
                 "chunk_ms_median": med, "chunk_ms_max": chunk_ms, "fps": 12 / (med / 1e3),
                 "chunk_tflop": flops / 1e12, "tflops_per_gpu": per_gpu, "frac_of_measured_bf16_peak": per_gpu / peak,
-                "allreduce_ms": ar, "allreduces_per_chunk": 3 * cfg.layers * cfg.n_fwd if world > 1 else 0,
+                "allreduce_ms": ar, "row_parallel_step_ms": max(r["rp_ms"] for r in allres) if ar else None,
+                "allreduces_per_chunk": 3 * cfg.layers * cfg.n_fwd if world > 1 else 0,
                 "allreduce_busbw_gbs": (2 * (world - 1) / world * cfg.tokens * cfg.dim * 2 / (ar / 1e3) / 1e9)
                 if ar else None,
                 "status_ok": all(r["status"][0] == 0 for r in allres)}

@@ -133,6 +133,18 @@ void fw_destroy(fw_handle* h);
  * enqueued on the launch stream (capturable). */
 int fw_tp_unique_id(void* id128);
 int fw_tp_init(fw_handle* h, const void* id128);
+/* Peer-memory reductions (replace NCCL for the engine's collectives): after fw_finalize on every
+ * rank, pass the tp workspace base addresses as seen from this process (index = rank; this
+ * rank's own binding at its index, the others mapped with fw_ipc_open).  The engine then sums
+ * the row-parallel partials with one kernel per linear that reads and writes the other GPUs'
+ * workspaces over NVLink and applies bias + gated residual in the same pass (two-shot), and
+ * gathers the RMSNorm sums of squares the same way.  Every rank must call it, before its first
+ * launch. */
+int fw_tp_peers(fw_handle* h, void* const* ws_bases, int n);
+/* One row-parallel reduction step of the engine (sum of every rank's partial output buffer,
+ * block 0's O-projection bias, residual update of the handle's workspace), on the path the
+ * handle uses (peer kernels or NCCL); for timing and tests.  Collective: every rank calls it. */
+int fw_tp_reduce_once(fw_handle* h, void* stream);
 /* In-place sum all-reduce over the handle's group (dtype FW_BF16 or FW_F32); for tests. */
 int fw_tp_allreduce(fw_handle* h, void* buf, size_t count, int dtype, void* stream);
 

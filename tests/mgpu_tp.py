@@ -4,7 +4,9 @@ Both ranks build the same tensor-parallel session (SMALL_TP: 4 heads and FFN 102
 a 2-chunk history window) and play chunks 0-3, which covers no history, one filled slot, two
 slots and the ring wrap-around.  Rank 0 checks the latents and its heads' history against the
 CPU oracle and against the same session on one GPU; both ranks must produce identical latents.
-Then chunk 4 is replayed from a snapshot through CUDA graphs that captured the NCCL calls."""
+The collectives run on the engine's peer-memory kernels (workspaces mapped over NVLink); the
+same session with NCCL collectives must agree.  Then chunk 4 is replayed from a snapshot
+through captured CUDA graphs."""
 import datetime
 import json
 import os
@@ -52,8 +54,14 @@ def main():
     S.capture(warmup=1)
     out4g = S.gen_chunk(PATH, 4)
     torch.cuda.synchronize()
-    res = {"rank": rank, "status": status, "graph_vs_eager": rel(out4g, out4),
-           "outs": [o.cpu() for o in outs], "hk": hist}
+    # the same model with the collectives on NCCL instead of the peer-memory kernels
+    S2 = B200StaticMG(cfg, sd, device=f"cuda:{local}", tp_group=True, tp_peers=False)
+    S2.add_image("img0", img)
+    e_nccl = [rel(S2.gen_chunk(PATH, k, graph=False), outs[k]) for k in range(4)]
+    status2 = S2.device_status()
+    del S2
+    res = {"rank": rank, "status": status, "graph_vs_eager": rel(out4g, out4), "nccl_rel": e_nccl,
+           "status_nccl": status2, "outs": [o.cpu() for o in outs], "hk": hist}
     allres = [None] * world
     torch.distributed.all_gather_object(allres, res)
     if rank == 0:
@@ -80,7 +88,9 @@ def main():
         S1.add_image("img0", img)
         e_tp1 = [rel(outs[k], S1.gen_chunk(PATH, k, graph=False)) for k in range(4)]
         line = {"ranks_identical": same, "oracle_rel": e_orc, "hist_rel": e_hist, "tp1_rel": e_tp1,
-                "graph_vs_eager": max(r["graph_vs_eager"] for r in allres), "status": [r["status"] for r in allres]}
+                "graph_vs_eager": max(r["graph_vs_eager"] for r in allres),
+                "nccl_rel": max(max(r["nccl_rel"]) for r in allres),
+                "status": [r["status"] for r in allres] + [r["status_nccl"] for r in allres]}
         print("TP_RESULT " + json.dumps(line), flush=True)
     S.graphs = {}
     del S

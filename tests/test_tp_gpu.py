@@ -41,3 +41,4 @@ def test_tensor_parallel_two_gpus():
     assert max(res["oracle_rel"]) < TOL and res["hist_rel"] < TOL
     assert max(res["tp1_rel"]) < 1e-2
     assert res["graph_vs_eager"] < 1e-2
+    assert res["nccl_rel"] < 1e-2
