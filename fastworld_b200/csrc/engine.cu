@@ -32,6 +32,8 @@ struct Tensor {
 
 struct GemmOp {
   CUtensorMap a, b;
+  CUtensorMap c;          // fp32 residual, for EPI_RESID_TMA
+  bool has_c = false;
   int bn = 256;
   GemmArgs args;
   bool valid = false;
@@ -321,6 +323,17 @@ static int config_check(const fw_config& c) {
   return 0;
 }
 
+// A residual epilogue with no bf16 mirror becomes a TMA reduce-add into the residual.
+static int resid_to_tma(GemmOp& op) {
+  GemmEpi& e = op.args.epi;
+  if (e.mode != EPI_RESID_F32 || e.mirror || !resid_tma_enabled()) return 0;
+  int rc = make_tmap_2d(&op.c, e.resid, 4, op.args.M, op.args.N, e.ld_resid, 32, 32, true);
+  if (rc) return rc;
+  e.mode = EPI_RESID_TMA;
+  op.has_c = true;
+  return 0;
+}
+
 // ---------------------------------------------------------------- op construction
 static int make_gemm(GemmOp& op, const void* A, int M, int K, int lda, const void* B, int N, int ldb, int bn,
                      const GemmEpi& epi, int* status) {
@@ -335,9 +348,13 @@ static int make_gemm(GemmOp& op, const void* A, int M, int K, int lda, const voi
   op.args.epi = epi;
   op.args.status = status;
   op.valid = true;
+  rc = resid_to_tma(op);
+  if (rc) return rc;
   return gemm_check(op.args, bn);
 }
-static int run(const GemmOp& op, cudaStream_t s) { return gemm_bf16_launch(op.a, op.b, op.bn, op.args, s); }
+static int run(const GemmOp& op, cudaStream_t s) {
+  return gemm_bf16_launch(op.a, op.b, op.bn, op.args, s, 0, op.has_c ? &op.c : nullptr);
+}
 static int pick_bn(int N) { return N >= 256 ? 256 : (N >= 128 ? 128 : 64); }
 
 // A block linear `wname` (weight `wname.w` [N, ldb]) whose bf16 operand is A [M, lda].  With
@@ -410,6 +427,7 @@ static int make_lin(fw_handle* h, GemmOp& op, const std::string& wname, const vo
   op.args.sw = P<float>(h, wname + ".sw");
   op.args.status = h->status;
   op.valid = true;
+  FW_TRY(resid_to_tma(op));
   return gemm_check(op.args, bn);
 }
 

@@ -28,6 +28,9 @@ void note_launch();
 // before touching data produced upstream, so the next kernel's launch and prologue overlap the
 // tail of the current one, in streams and in captured graphs alike.
 bool pdl_enabled();
+// Residual GEMM epilogues without a bf16 mirror add into the fp32 residual by TMA reduce-add
+// (EPI_RESID_TMA) unless FW_RESID_TMA=0 in the environment (then EPI_RESID_F32).
+bool resid_tma_enabled();
 
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
@@ -54,6 +57,7 @@ enum EpiMode : int {
   EPI_RESID_F32 = 2,   // resid_f32 += gate[frame] * (acc + bias); optional bf16 mirror of resid
   EPI_F32 = 3,         // out_f32 = acc + bias
   EPI_GELU_ERF_BF16 = 4,   // out_bf16 = gelu_erf(acc + bias)
+  EPI_RESID_TMA = 5,   // resid_f32 += gate[frame] * (acc + bias) by TMA reduce-add (no mirror; needs tmC)
 };
 
 struct GemmEpi {
@@ -85,8 +89,10 @@ struct GemmArgs {
 
 // C[M,N] = A[M,K] * B[N,K]^T.  tmA: box [128 rows, 64 cols]; tmB: box [bn rows, 64 cols];
 // bn in {64, 128, 256}.  `ctas` = 0 uses one CTA per SM (persistent).
+// tmC: the fp32 residual [M, ld_resid] with box [32 rows, 32 cols], 128-byte swizzle, for
+// EPI_RESID_TMA (ignored otherwise).
 int gemm_bf16_launch(const CUtensorMap& tmA, const CUtensorMap& tmB, int bn, const GemmArgs& a, cudaStream_t s,
-                     int ctas = 0);
+                     int ctas = 0, const CUtensorMap* tmC = nullptr);
 int gemm_check(const GemmArgs& a, int bn);
 
 // ---------------------------------------------------------------- attention

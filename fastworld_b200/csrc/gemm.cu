@@ -28,7 +28,11 @@ struct GemmCfg {
   static constexpr int STAGE = A_BYTES + B_BYTES;
   static constexpr int STAGES = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int SMEM = STAGES * STAGE + 1024 + 256;
+  // staging for EPI_RESID_TMA: one [32 rows x 32 fp32] 128-byte-swizzled box per epilogue warp,
+  // 1024-aligned after the barrier block
+  static constexpr int EPI_OFF = STAGES * STAGE + 1024;
+  static constexpr int EPI_BOX = 32 * 32 * 4;
+  static constexpr int SMEM = EPI_OFF + 8 * EPI_BOX + 1024;
 };
 
 __device__ __forceinline__ void add_bias(const GemmEpi& e, int frame, int col0, float (&v)[32]) {
@@ -108,13 +112,57 @@ __device__ __forceinline__ void epilogue_chunk(const GemmEpi& e, int row, int co
   }
 }
 
+// EPI_RESID_TMA: the warp's 32 rows x 32 columns of gate * (acc + bias) go through a
+// 128-byte-swizzled staging box (16-byte chunk c of row l at chunk position c ^ (l % 8), the
+// layout TMA expects, 4-way bank spread) and lane 0 adds the box into the fp32 residual with
+// one TMA reduce-add; rows past M are dropped by TMA.  No residual read leaves the SM.  `row`
+// is clamped to a valid row for the scale / bias / gate reads (its values are discarded).
+__device__ __forceinline__ void epilogue_chunk_tma(const GemmEpi& e, const CUtensorMap* tmC, int row, int row0,
+                                                   int col0, const uint32_t (&r)[32], const float* __restrict__ sa,
+                                                   const float* __restrict__ sw, uint8_t* box, int lane) {
+  float v[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+  if (sa) {
+    const float ra = __ldg(sa + row);
+    const float4* w4 = reinterpret_cast<const float4*>(sw + col0);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float4 w = __ldg(w4 + j);
+      v[4 * j + 0] *= ra * w.x; v[4 * j + 1] *= ra * w.y; v[4 * j + 2] *= ra * w.z; v[4 * j + 3] *= ra * w.w;
+    }
+  }
+  const int frame = row / e.rows_per_frame;
+  add_bias(e, frame, col0, v);
+  if (e.gate) {
+    const float4* gp = reinterpret_cast<const float4*>(e.gate + (size_t)frame * e.gate_stride + col0);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float4 g = __ldg(gp + j);
+      v[4 * j + 0] *= g.x; v[4 * j + 1] *= g.y; v[4 * j + 2] *= g.z; v[4 * j + 3] *= g.w;
+    }
+  }
+  uint8_t* myrow = box + lane * 128;
+#pragma unroll
+  for (int c = 0; c < 8; ++c)
+    *reinterpret_cast<float4*>(myrow + ((c ^ (lane & 7)) << 4)) = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    tma_reduce_add_2d(tmC, box, col0, row0);
+    bulk_commit();
+    bulk_wait_read0();   // the box may be rewritten once TMA has read it
+  }
+  __syncwarp();
+}
+
 // F8 = false: bf16 operands, kind::f16, 64 elements (128 bytes) of K per stage.
 // F8 = true:  e4m3 operands, kind::f8f6f4, 128 elements (128 bytes) of K per stage; the same
 //             128-byte-swizzled smem tiles and descriptors, 32 bytes of K per MMA instruction.
 template <int BN, bool F8>
 __global__ void __launch_bounds__(320, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                     const GemmArgs args) {
+                     const __grid_constant__ CUtensorMap tmC, const GemmArgs args) {
   using C = GemmCfg<BN>;
   constexpr int KE = F8 ? 128 : 64;   // K elements per stage
   pdl_trigger();
@@ -258,7 +306,16 @@ __global__ void __launch_bounds__(320, 1)
       tmem_ld_wait();
       tc_fence_before();
       mbar_arrive(tempty + acc);                 // the accumulator buffer is free again
-      if (row < M) {
+      if (args.epi.mode == EPI_RESID_TMA) {      // warp-collective: every lane takes part
+        uint8_t* box = smem + C::EPI_OFF + (warp - 2) * C::EPI_BOX;
+#pragma unroll
+        for (int c = 0; c < NC; ++c) {
+          const int col0 = colh + c * 32;
+          if (col0 < N)
+            epilogue_chunk_tma(args.epi, &tmC, min(row, M - 1), mb * 128 + q * 32, col0, r[c],
+                               F8 ? args.sa : nullptr, args.sw, box, lane);
+        }
+      } else if (row < M) {
 #pragma unroll
         for (int c = 0; c < NC; ++c) {
           const int col0 = colh + c * 32;
@@ -268,6 +325,7 @@ __global__ void __launch_bounds__(320, 1)
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
+    if (args.epi.mode == EPI_RESID_TMA && lane == 0) bulk_wait0();   // residual adds performed before exit
   }
   __syncthreads();
   if (warp == 1) {
@@ -300,6 +358,11 @@ int gemm_check(const GemmArgs& a, int bn) {
     case EPI_F32:
       if (!e.out[0] || !al16(e.out[0]) || e.ld_out % 4) return FW_EALIGN;
       break;
+    case EPI_RESID_TMA:
+      if (e.mirror) return FW_EINVAL;   // the mirror needs the updated residual in registers
+      if (!e.resid || !al16(e.resid) || e.ld_resid % 4) return FW_EALIGN;
+      if (e.gate && (!al16(e.gate) || e.gate_stride % 4)) return FW_EALIGN;
+      break;
     case EPI_RESID_F32:
       if (!e.resid || !al16(e.resid) || e.ld_resid % 4) return FW_EALIGN;
       if (e.gate && (!al16(e.gate) || e.gate_stride % 4)) return FW_EALIGN;
@@ -312,26 +375,29 @@ int gemm_check(const GemmArgs& a, int bn) {
 }
 
 template <int BN, bool F8>
-static int launch_bn(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmArgs& a, cudaStream_t s, int grid) {
+static int launch_bn(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmC, const GemmArgs& a,
+                     cudaStream_t s, int grid) {
   using C = GemmCfg<BN>;
   cudaError_t err =
       cudaFuncSetAttribute(gemm_bf16_kernel<BN, F8>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (err != cudaSuccess) return FW_ECUDA;
-  launch_k(gemm_bf16_kernel<BN, F8>, grid, 320, C::SMEM, s, tmA, tmB, a);
+  launch_k(gemm_bf16_kernel<BN, F8>, grid, 320, C::SMEM, s, tmA, tmB, tmC, a);
   return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
 }
 
 int gemm_bf16_launch(const CUtensorMap& tmA, const CUtensorMap& tmB, int bn, const GemmArgs& a, cudaStream_t s,
-                     int ctas) {
+                     int ctas, const CUtensorMap* tmC) {
   int rc = gemm_check(a, bn);
   if (rc) return rc;
+  if (a.epi.mode == EPI_RESID_TMA && !tmC) return FW_EINVAL;
+  const CUtensorMap& mc = tmC ? *tmC : tmA;   // unused unless EPI_RESID_TMA
   const int tiles = ((a.M + 127) / 128) * ((a.N + bn - 1) / bn);
   int grid = ctas > 0 ? ctas : num_sms();
   if (grid > tiles) grid = tiles;
   switch (bn) {
-    case 256: return a.sa ? launch_bn<256, true>(tmA, tmB, a, s, grid) : launch_bn<256, false>(tmA, tmB, a, s, grid);
-    case 128: return a.sa ? launch_bn<128, true>(tmA, tmB, a, s, grid) : launch_bn<128, false>(tmA, tmB, a, s, grid);
-    default: return a.sa ? launch_bn<64, true>(tmA, tmB, a, s, grid) : launch_bn<64, false>(tmA, tmB, a, s, grid);
+    case 256: return a.sa ? launch_bn<256, true>(tmA, tmB, mc, a, s, grid) : launch_bn<256, false>(tmA, tmB, mc, a, s, grid);
+    case 128: return a.sa ? launch_bn<128, true>(tmA, tmB, mc, a, s, grid) : launch_bn<128, false>(tmA, tmB, mc, a, s, grid);
+    default: return a.sa ? launch_bn<64, true>(tmA, tmB, mc, a, s, grid) : launch_bn<64, false>(tmA, tmB, mc, a, s, grid);
   }
 }
 

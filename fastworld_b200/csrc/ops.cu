@@ -25,6 +25,14 @@ PFN_encodeTiled get_encode_fn() {
 static std::atomic<unsigned long long> g_launches{0};
 void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
+bool resid_tma_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("FW_RESID_TMA");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 bool pdl_enabled() {
   static const bool on = [] {
     const char* v = getenv("FW_PDL");
@@ -177,7 +185,13 @@ int fw_gemm_bf16_resid(const void* A, const void* B, const void* bias, float* re
   a.epi.gate = gate;
   a.epi.gate_stride = N;
   a.epi.rows_per_frame = rows_per_frame;
-  return gemm_bf16_launch(ta, tb, bn, a, reinterpret_cast<cudaStream_t>(stream));
+  if (!resid_tma_enabled()) return gemm_bf16_launch(ta, tb, bn, a, reinterpret_cast<cudaStream_t>(stream));
+  // the residual is added by TMA reduce-add (EPI_RESID_TMA)
+  CUtensorMap tc;
+  rc = make_tmap_2d(&tc, resid, 4, M, N, N, 32, 32, true);
+  if (rc) return rc;
+  a.epi.mode = EPI_RESID_TMA;
+  return gemm_bf16_launch(ta, tb, bn, a, reinterpret_cast<cudaStream_t>(stream), 0, &tc);
 }
 
 int fw_attention(const void* q, int Lq, int heads, const void* k0, const void* v0, int max_keys0, const void* k1,
