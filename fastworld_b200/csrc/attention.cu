@@ -20,8 +20,6 @@
 //              both tiles committed their reads.
 // TMEM (512 columns): S_A [0,128), O_A [128,256), S_B [256,384), O_B [384,512).
 // SMEM: Q_A, Q_B (2 x 32 KB), K/V ring (3 x 32 KB), P_A, P_B (2 x 32 KB) = 224 KB.
-#include <cstdlib>
-
 #include "../../include/fastworld_b200.h"
 #include "fw_internal.h"
 #include "fw_ptx.cuh"
@@ -38,14 +36,10 @@ constexpr int P_OFF = KV_OFF + 6 * TILE;    // tile t: 2 sub-tiles at P_OFF + t 
 constexpr int BAR_OFF = P_OFF + 4 * TILE;
 constexpr int SMEM = BAR_OFF + 256 + 1024;
 constexpr uint32_t TMEM_COLS = 512;
-constexpr int EMU_DEFAULT = 0;   // exponentials per polynomial one (0: all on MUFU); FW_ATTN_EMU overrides
 __host__ __device__ constexpr uint32_t s_col(int t) { return (uint32_t)(t * 256); }
 __host__ __device__ constexpr uint32_t o_col(int t) { return (uint32_t)(t * 256 + 128); }
 }  // namespace attn
 
-// EMU > 0: every EMU-th exponential of the softmax is evaluated by ex2_poly on the FMA pipe
-// instead of the MUFU unit, balancing the two pipes.
-template <int EMU>
 __global__ void __launch_bounds__(attn::THREADS, 1)
     attention_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK0,
                      const __grid_constant__ CUtensorMap tmV0, const __grid_constant__ CUtensorMap tmK1,
@@ -235,8 +229,7 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
       for (int a = 0; a < 8; ++a) rs8[a] = 0.f;
 #pragma unroll
       for (int i = 0; i < 128; ++i) {
-        const float xv = fmaf(sv[i], sl2, -m);
-        sv[i] = (EMU > 0 && i % (EMU > 0 ? EMU : 1) == (EMU > 0 ? EMU : 1) - 1) ? ex2_poly(xv) : ex2(xv);
+        sv[i] = ex2(fmaf(sv[i], sl2, -m));
         rs8[i & 7] += sv[i];
       }
       l = l * alpha + (((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7])));
@@ -307,10 +300,6 @@ int attention_launch(const CUtensorMap& tmQ, const CUtensorMap& tmK0, const CUte
                      const CUtensorMap& tmK1, const CUtensorMap& tmV1, const AttnArgs& a, cudaStream_t s) {
   if (a.Lq <= 0 || a.heads <= 0 || !a.meta || !a.out) return FW_EINVAL;
   if (a.ld_out % 8 || (reinterpret_cast<uintptr_t>(a.out) & 15u)) return FW_EALIGN;
-  static const int emu = [] {
-    const char* e = getenv("FW_ATTN_EMU");
-    return e ? atoi(e) : attn::EMU_DEFAULT;
-  }();
   dim3 grid((a.Lq + 2 * attn::BQ - 1) / (2 * attn::BQ), a.heads);
   auto go = [&](auto kern) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, attn::SMEM) != cudaSuccess)
@@ -318,13 +307,7 @@ int attention_launch(const CUtensorMap& tmQ, const CUtensorMap& tmK0, const CUte
     launch_k(kern, grid, attn::THREADS, attn::SMEM, s, tmQ, tmK0, tmV0, tmK1, tmV1, a);
     return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
   };
-  switch (emu) {
-    case 2: return go(attention_kernel<2>);
-    case 3: return go(attention_kernel<3>);
-    case 4: return go(attention_kernel<4>);
-    case 8: return go(attention_kernel<8>);
-    default: return go(attention_kernel<0>);
-  }
+  return go(attention_kernel);
 }
 
 }  // namespace fw

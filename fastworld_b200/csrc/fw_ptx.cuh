@@ -227,23 +227,6 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-// 2^x on the FMA/ALU pipes, for x <= 8 (softmax exponents): x = n + f with n = round(x) taken
-// from the low mantissa bits of x + 1.5 * 2^23, 2^f on [-1/2, 1/2] by a cubic fitted here to
-// 2^f (weighted least squares toward minimax on Chebyshev nodes; max relative error 1.0e-4,
-// far below the bf16 rounding of P), and 2^n added to the exponent field.  x is clamped at
-// -127 (2^-127 ~ 0), so -inf (masked keys) gives ~0.  Lets part of the exponentials bypass
-// the MUFU pipe.
-__device__ __forceinline__ float ex2_poly(float x) {
-  x = fmaxf(x, -127.f);
-  const float magic = 12582912.f;   // 1.5 * 2^23
-  const float t = x + magic;
-  const float f = x - (t - magic);
-  float p = fmaf(0.05500893f, f, 0.24221097f);
-  p = fmaf(p, f, 0.69328293f);
-  p = fmaf(p, f, 1.f);
-  const int n = __float_as_int(t) - __float_as_int(magic);
-  return __int_as_float(__float_as_int(p) + (n << 23));
-}
 __device__ __forceinline__ float tanh_approx(float x) {
   float y;
   asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));

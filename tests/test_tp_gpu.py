@@ -25,11 +25,15 @@ def test_history_window_two_chunks_one_gpu():
         assert all(v < TOL for v in e.values()), e
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_tensor_parallel_two_gpus():
+@pytest.mark.parametrize("world", [2, 4])
+def test_tensor_parallel(world):
+    """world 2: the one-shot peer reduction; world 4: the two-shot one (1 head per rank)."""
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     cmd = ["timeout", "-k", "30", "400", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
-           "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=29533", os.path.join(HERE, "mgpu_tp.py")]
+           f"--nproc-per-node={world}", "--master-addr=127.0.0.1", f"--master-port={29533 + world}",
+           os.path.join(HERE, "mgpu_tp.py")]
     r = subprocess.run(cmd, capture_output=True, text=True, env=env)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     line = [x for x in r.stdout.splitlines() if x.startswith("TP_RESULT ")]
