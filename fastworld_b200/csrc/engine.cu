@@ -34,6 +34,7 @@ struct GemmOp {
   CUtensorMap a, b;
   CUtensorMap c;          // fp32 residual, for EPI_RESID_TMA
   bool has_c = false;
+  bool pair = false;      // 256 x 256 CTA-pair tiles (gemm2.cu)
   int bn = 256;
   GemmArgs args;
   bool valid = false;
@@ -323,6 +324,10 @@ static int config_check(const fw_config& c) {
   return 0;
 }
 
+// CTA-pair tiles (opt-in, FW_GEMM_PAIR=1) for bf16 linears with large M and N: the 14B QKV and
+// FFN-up at tensor-parallel size 1-2 (4680 x 15360 x 5120: 511 us vs 586 us in isolation); the
+// MG2 shapes and N = 5120 outputs keep one-CTA tiles (fewer wave-quantisation losses).
+static bool use_pair(int M, int N) { return gemm_pair_enabled() && M >= 4096 && N >= 6144; }
 // A residual epilogue with no bf16 mirror becomes a TMA reduce-add into the residual.
 static int resid_to_tma(GemmOp& op) {
   GemmEpi& e = op.args.epi;
@@ -337,10 +342,12 @@ static int resid_to_tma(GemmOp& op) {
 // ---------------------------------------------------------------- op construction
 static int make_gemm(GemmOp& op, const void* A, int M, int K, int lda, const void* B, int N, int ldb, int bn,
                      const GemmEpi& epi, int* status) {
+  op.pair = use_pair(M, N);
+  if (op.pair) bn = 256;
   op.bn = bn;
   int rc = make_tmap_2d(&op.a, A, 2, M, K, lda, 128, 64, true);
   if (rc) return rc;
-  rc = make_tmap_2d(&op.b, B, 2, N, K, ldb, bn, 64, true);
+  rc = make_tmap_2d(&op.b, B, 2, N, K, ldb, op.pair ? 128 : bn, 64, true);
   if (rc) return rc;
   op.args.M = M;
   op.args.N = N;
@@ -353,6 +360,7 @@ static int make_gemm(GemmOp& op, const void* A, int M, int K, int lda, const voi
   return gemm_check(op.args, bn);
 }
 static int run(const GemmOp& op, cudaStream_t s) {
+  if (op.pair) return gemm_pair_launch(op.a, op.b, op.args, s, op.has_c ? &op.c : nullptr);
   return gemm_bf16_launch(op.a, op.b, op.bn, op.args, s, 0, op.has_c ? &op.c : nullptr);
 }
 static int pick_bn(int N) { return N >= 256 ? 256 : (N >= 128 ? 128 : 64); }

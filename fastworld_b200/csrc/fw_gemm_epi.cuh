@@ -1,0 +1,131 @@
+// GEMM epilogue helpers shared by the one-CTA (gemm.cu) and CTA-pair (gemm2.cu) kernels: a
+// thread holds 32 consecutive fp32 accumulator columns of one output row (one tcgen05.ld
+// 32x32b.x32) and applies the fused epilogue of GemmEpi to them.
+#pragma once
+#include "fw_internal.h"
+#include "fw_ptx.cuh"
+
+namespace fw {
+
+__device__ __forceinline__ void add_bias(const GemmEpi& e, int frame, int col0, float (&v)[32]) {
+  if (e.bias) {
+    const uint4* bp = reinterpret_cast<const uint4*>(e.bias + col0);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint4 u = __ldg(bp + j);
+      float2 f0 = unpack_bf16(u.x), f1 = unpack_bf16(u.y), f2 = unpack_bf16(u.z), f3 = unpack_bf16(u.w);
+      v[8 * j + 0] += f0.x; v[8 * j + 1] += f0.y; v[8 * j + 2] += f1.x; v[8 * j + 3] += f1.y;
+      v[8 * j + 4] += f2.x; v[8 * j + 5] += f2.y; v[8 * j + 6] += f3.x; v[8 * j + 7] += f3.y;
+    }
+  }
+  if (e.fbias) {
+    const float4* fp = reinterpret_cast<const float4*>(e.fbias + (size_t)frame * e.fbias_stride + col0);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float4 b = __ldg(fp + j);
+      v[4 * j + 0] += b.x; v[4 * j + 1] += b.y; v[4 * j + 2] += b.z; v[4 * j + 3] += b.w;
+    }
+  }
+}
+
+__device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float (&v)[32]) {
+  uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    d4[j] = make_uint4(pack_bf16(v[8 * j + 0], v[8 * j + 1]), pack_bf16(v[8 * j + 2], v[8 * j + 3]),
+                       pack_bf16(v[8 * j + 4], v[8 * j + 5]), pack_bf16(v[8 * j + 6], v[8 * j + 7]));
+}
+
+__device__ __forceinline__ void epilogue_chunk(const GemmEpi& e, int row, int col0, const uint32_t (&r)[32],
+                                               const float* __restrict__ sa, const float* __restrict__ sw) {
+  float v[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+  if (sa) {   // e4m3 operands: dequantise with the row's activation scale and each column's weight scale
+    const float ra = __ldg(sa + row);
+    const float4* w4 = reinterpret_cast<const float4*>(sw + col0);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float4 w = __ldg(w4 + j);
+      v[4 * j + 0] *= ra * w.x; v[4 * j + 1] *= ra * w.y; v[4 * j + 2] *= ra * w.z; v[4 * j + 3] *= ra * w.w;
+    }
+  }
+  const int frame = row / e.rows_per_frame;
+  add_bias(e, frame, col0, v);
+  if (e.mode == EPI_BF16 || e.mode == EPI_GELU_BF16 || e.mode == EPI_GELU_ERF_BF16) {
+    if (e.mode == EPI_GELU_BF16) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
+    } else if (e.mode == EPI_GELU_ERF_BF16) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = 0.5f * v[j] * (1.f + erff(v[j] * 0.7071067811865476f));
+    }
+    const int seg = col0 / e.seg_w;
+    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(e.out[seg]) + (size_t)row * e.ld_out + (col0 - seg * e.seg_w);
+    store_bf16x32(dst, v);
+  } else if (e.mode == EPI_F32) {
+    float4* d4 = reinterpret_cast<float4*>(reinterpret_cast<float*>(e.out[0]) + (size_t)row * e.ld_out + col0);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) d4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+  } else {   // EPI_RESID_F32
+    float4* rp = reinterpret_cast<float4*>(e.resid + (size_t)row * e.ld_resid + col0);
+    const float4* gp = e.gate ? reinterpret_cast<const float4*>(e.gate + (size_t)frame * e.gate_stride + col0) : nullptr;
+    float4 x[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) x[j] = rp[j];   // all eight loads in flight before the math
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float4 g = gp ? __ldg(gp + j) : make_float4(1.f, 1.f, 1.f, 1.f);
+      x[j].x += g.x * v[4 * j + 0]; x[j].y += g.y * v[4 * j + 1]; x[j].z += g.z * v[4 * j + 2]; x[j].w += g.w * v[4 * j + 3];
+      rp[j] = x[j];
+      v[4 * j + 0] = x[j].x; v[4 * j + 1] = x[j].y; v[4 * j + 2] = x[j].z; v[4 * j + 3] = x[j].w;
+    }
+    if (e.mirror) store_bf16x32(e.mirror + (size_t)row * e.ld_mirror + col0, v);
+  }
+}
+
+// EPI_RESID_TMA: the warp's 32 rows x 32 columns of gate * (acc + bias) go through a
+// 128-byte-swizzled staging box (16-byte chunk c of row l at chunk position c ^ (l % 8), the
+// layout TMA expects, 4-way bank spread) and lane 0 adds the box into the fp32 residual with
+// one TMA reduce-add; rows past M are dropped by TMA.  No residual read leaves the SM.  `row`
+// is clamped to a valid row for the scale / bias / gate reads (its values are discarded).
+__device__ __forceinline__ void epilogue_chunk_tma(const GemmEpi& e, const CUtensorMap* tmC, int row, int row0,
+                                                   int col0, const uint32_t (&r)[32], const float* __restrict__ sa,
+                                                   const float* __restrict__ sw, uint8_t* box, int lane) {
+  float v[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+  if (sa) {
+    const float ra = __ldg(sa + row);
+    const float4* w4 = reinterpret_cast<const float4*>(sw + col0);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float4 w = __ldg(w4 + j);
+      v[4 * j + 0] *= ra * w.x; v[4 * j + 1] *= ra * w.y; v[4 * j + 2] *= ra * w.z; v[4 * j + 3] *= ra * w.w;
+    }
+  }
+  const int frame = row / e.rows_per_frame;
+  add_bias(e, frame, col0, v);
+  if (e.gate) {
+    const float4* gp = reinterpret_cast<const float4*>(e.gate + (size_t)frame * e.gate_stride + col0);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float4 g = __ldg(gp + j);
+      v[4 * j + 0] *= g.x; v[4 * j + 1] *= g.y; v[4 * j + 2] *= g.z; v[4 * j + 3] *= g.w;
+    }
+  }
+  uint8_t* myrow = box + lane * 128;
+#pragma unroll
+  for (int c = 0; c < 8; ++c)
+    *reinterpret_cast<float4*>(myrow + ((c ^ (lane & 7)) << 4)) = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    tma_reduce_add_2d(tmC, box, col0, row0);
+    bulk_commit();
+    bulk_wait_read0();   // the box may be rewritten once TMA has read it
+  }
+  __syncwarp();
+}
+
+}  // namespace fw

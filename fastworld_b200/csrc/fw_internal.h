@@ -94,6 +94,14 @@ struct GemmArgs {
 int gemm_bf16_launch(const CUtensorMap& tmA, const CUtensorMap& tmB, int bn, const GemmArgs& a, cudaStream_t s,
                      int ctas = 0, const CUtensorMap* tmC = nullptr);
 int gemm_check(const GemmArgs& a, int bn);
+// CTA-pair variant (gemm2.cu): 256 x 256 tiles; tmA box [128 rows, 64 cols] as above, tmB box
+// [128 rows, 64 cols] (half a tile of output columns per CTA).
+int gemm_pair_launch(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmArgs& a, cudaStream_t s,
+                     const CUtensorMap* tmC = nullptr);
+// Pair tiles for the engine's large linears only with FW_GEMM_PAIR=1 in the environment: in
+// isolation they beat one-CTA tiles on the 14B shapes by up to 13 %, but a whole 14B chunk
+// (weights streamed from HBM) measured the same either way (837.9 vs 834.5 ms).
+bool gemm_pair_enabled();
 
 // ---------------------------------------------------------------- attention
 struct AttnArgs {

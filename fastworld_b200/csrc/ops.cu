@@ -25,6 +25,14 @@ PFN_encodeTiled get_encode_fn() {
 static std::atomic<unsigned long long> g_launches{0};
 void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
+bool gemm_pair_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("FW_GEMM_PAIR");
+    return e && e[0] == '1';
+  }();
+  return on;
+}
+
 bool resid_tma_enabled() {
   static const bool on = [] {
     const char* e = getenv("FW_RESID_TMA");
@@ -82,10 +90,10 @@ int fw_gemm_bf16(const void* A, const void* B, const void* bias, void* out, int 
   if (epilogue != EPI_BF16 && epilogue != EPI_GELU_BF16 && epilogue != EPI_F32 && epilogue != EPI_GELU_ERF_BF16)
     return FW_EINVAL;
   const int bn = tile_n > 0 ? tile_n : (N >= 256 ? 256 : (N >= 128 ? 128 : 64));
-  if (bn != 64 && bn != 128 && bn != 256) return FW_EINVAL;
+  if (bn != 64 && bn != 128 && bn != 256 && bn != 512) return FW_EINVAL;
   CUtensorMap ta, tb;
   int rc = make_tmap_2d(&ta, A, 2, M, K, K, 128, 64, true);
-  if (!rc) rc = make_tmap_2d(&tb, B, 2, N, K, K, bn, 64, true);
+  if (!rc) rc = make_tmap_2d(&tb, B, 2, N, K, K, bn == 512 ? 128 : bn, 64, true);
   if (rc) return rc;
   GemmArgs a;
   a.M = M;
@@ -96,6 +104,7 @@ int fw_gemm_bf16(const void* A, const void* B, const void* bias, void* out, int 
   a.epi.ld_out = N;
   a.epi.seg_w = 1 << 30;
   a.epi.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
+  if (bn == 512) return gemm_pair_launch(ta, tb, a, reinterpret_cast<cudaStream_t>(stream));
   return gemm_bf16_launch(ta, tb, bn, a, reinterpret_cast<cudaStream_t>(stream));
 }
 
@@ -106,10 +115,10 @@ int fw_gemm_e4m3(const void* A8, const float* sa, const void* B8, const float* s
   if (epilogue != EPI_BF16 && epilogue != EPI_GELU_BF16 && epilogue != EPI_F32 && epilogue != EPI_GELU_ERF_BF16)
     return FW_EINVAL;
   const int bn = tile_n > 0 ? tile_n : (N >= 256 ? 256 : (N >= 128 ? 128 : 64));
-  if (bn != 64 && bn != 128 && bn != 256) return FW_EINVAL;
+  if (bn != 64 && bn != 128 && bn != 256 && bn != 512) return FW_EINVAL;
   CUtensorMap ta, tb;
   int rc = make_tmap_2d(&ta, A8, 1, M, K, K, 128, 128, true);
-  if (!rc) rc = make_tmap_2d(&tb, B8, 1, N, K, K, bn, 128, true);
+  if (!rc) rc = make_tmap_2d(&tb, B8, 1, N, K, K, bn == 512 ? 128 : bn, 128, true);
   if (rc) return rc;
   GemmArgs a;
   a.M = M;
@@ -122,6 +131,7 @@ int fw_gemm_e4m3(const void* A8, const float* sa, const void* B8, const float* s
   a.epi.ld_out = N;
   a.epi.seg_w = 1 << 30;
   a.epi.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
+  if (bn == 512) return gemm_pair_launch(ta, tb, a, reinterpret_cast<cudaStream_t>(stream));
   return gemm_bf16_launch(ta, tb, bn, a, reinterpret_cast<cudaStream_t>(stream));
 }
 

@@ -1,6 +1,6 @@
 """Small, self-terminating workloads for ncu captures (run them plain first, then under ncu).
 
-    python -m fastworld_b200.profile chunk [--chunks 2]   eager MG2 chunks (chunk 0, then steady)
+    python -m fastworld_b200.profile chunk [--chunks 2] [--config mg2|mg2_fp8]   eager chunks (chunk 0, then steady)
     python -m fastworld_b200.profile gemm  [--reps 3]     FFN-up GEMM, MG2 shape, GELU epilogue
     python -m fastworld_b200.profile gemm_resid           O-projection GEMM (N = K = 1536) with the gated residual
     python -m fastworld_b200.profile attn  [--reps 3]     steady self-attention, 12 heads, 2640 + 2640 keys
@@ -12,11 +12,11 @@ import argparse
 import torch
 
 
-def chunk(n: int) -> None:
+def chunk(n: int, config: str = "mg2") -> None:
     from fastworld_b200 import _lib
-    from fastworld_b200.config import MG2
+    from fastworld_b200.config import PRESETS
     from fastworld_b200.static import B200StaticMG
-    S = B200StaticMG(MG2, seed=0)
+    S = B200StaticMG(PRESETS[config], seed=0)
     S.add_image("img0", seed=3, max_chunks=n + 1)
     path = [("img0", ("w", "u"))] * (n + 1)
     for k in range(n):
@@ -70,6 +70,7 @@ if __name__ == "__main__":
     ap.add_argument("what", choices=["chunk", "gemm", "gemm_resid", "attn"])
     ap.add_argument("--chunks", type=int, default=2)
     ap.add_argument("--reps", type=int, default=3)
+    ap.add_argument("--config", default="mg2")
     a = ap.parse_args()
-    {"chunk": lambda: chunk(a.chunks), "gemm": lambda: gemm(a.reps), "gemm_resid": lambda: gemm_resid(a.reps),
+    {"chunk": lambda: chunk(a.chunks, a.config), "gemm": lambda: gemm(a.reps), "gemm_resid": lambda: gemm_resid(a.reps),
      "attn": lambda: attn(a.reps)}[a.what]()

@@ -1,6 +1,6 @@
 """tcgen05 GEMM parity against an fp32 PyTorch reference of the same op (bf16 inputs).
 
-Covers the tile widths (64/128/256), M/N/K tails (TMA zero fill + masked epilogue), every
+Covers the tile widths (64/128/256 and the 256 x 256 CTA-pair tile, tile_n 512), M/N/K tails (TMA zero fill + masked epilogue), every
 epilogue (bias, GELU-tanh, GELU-erf, fp32 store, gated fp32 residual) and the MG2 shapes.
 Tolerance: rel-L2 <= 6e-3 and max-abs <= 3e-2 * max|ref| (bf16 output rounding is 2^-9).
 """
@@ -26,7 +26,9 @@ def _data(M, N, K, seed=0):
 
 SHAPES = [(128, 256, 64, 256), (300, 512, 200, 256), (2640, 1536, 1536, 256), (257, 1280, 1280, 128),
           (2640, 64, 1536, 64), (200, 384, 136, 128), (2640, 4608, 1536, 256), (2640, 1536, 8960, 256),
-          (96, 96, 72, 64)]
+          (96, 96, 72, 64),
+          # CTA pair (cta_group::2): tails in M, N and K, one and several tiles per pair
+          (256, 256, 64, 512), (300, 544, 200, 512), (2640, 1536, 1536, 512), (4680, 7680, 512, 512)]
 
 
 @pytest.mark.parametrize("M,N,K,tile", SHAPES)
@@ -72,3 +74,26 @@ def test_gemm_deterministic():
     x = ops.gemm(a, b, bias)
     y = ops.gemm(a, b, bias)
     assert torch.equal(x, y)
+
+
+@pytest.mark.parametrize("epi", ["gelu_tanh", "f32"])
+def test_gemm_pair_epilogues(epi):
+    """The CTA-pair kernel's epilogues agree bitwise with the one-CTA kernel's (same fp32
+    accumulation order per output element: K blocks in order)."""
+    from fastworld_b200 import ops
+    a, b, bias = _data(700, 768, 512, seed=5)
+    one = ops.gemm(a, b, bias, epi, 256)
+    two = ops.gemm(a, b, bias, epi, 512)
+    torch.cuda.synchronize()
+    assert _rel(two, one) < 1e-6
+
+
+def test_gemm_pair_e4m3_matches_one_cta():
+    from fastworld_b200 import ops
+    a, b, bias = _data(2640, 1536, 1536, seed=6)
+    a8, sa = ops.quant_e4m3(a)
+    b8, sw = ops.quant_e4m3(b)
+    one = ops.gemm_e4m3(a8, sa, b8, sw, bias, "none", 256)
+    two = ops.gemm_e4m3(a8, sa, b8, sw, bias, "none", 512)
+    torch.cuda.synchronize()
+    assert torch.equal(one, two)
