@@ -67,6 +67,7 @@ struct fw_handle {
   void* comm = nullptr;           // NCCL communicator (tp > 1)
   fw::TpPeers peers;              // the other ranks' workspaces (tp > 1, after fw_tp_peers)
   bool use_peers = false;         // reductions over peer memory instead of NCCL
+  bool push = false;              // 2 ranks: row-parallel GEMMs push their partials to the peer
   __nv_bfloat16* part = nullptr;  // [L, D] partial output of a row-parallel linear (tp > 1)
   float* ss = nullptr;            // [max(L, Ctx), 2] sums of squares for the sharded RMSNorms
   size_t lat_elems;
@@ -300,6 +301,7 @@ static int register_tensors(fw_handle* h) {
     ws_add(h, "tp.flags", (size_t)3 * TP_MAX_RANKS * TP_MAX_CTAS * sizeof(unsigned));
     ws_add(h, "tp.gat", (size_t)2 * TP_MAX_RANKS * mx({L, h->Ctx}) * 2 * f4);
     ws_add(h, "tp.epoch", (size_t)2 * TP_MAX_CTAS * sizeof(unsigned));
+    if (h->tp == 2) ws_add(h, "tp.recv", (size_t)2 * L * D * bf);   // partials pushed by the other rank
   }
   h->ws_bytes = (h->ws_bytes + 1023) & ~(size_t)1023;
   add_tensor(h, "workspace", FW_KIND_WORKSPACE, FW_U8, {(int64_t)h->ws_bytes});
@@ -473,8 +475,10 @@ static int rms_norm_op(fw_handle* h, __nv_bfloat16* x0, __nv_bfloat16* x1, const
 // xs += gate[frame] * (sum + bias) (the epilogue the GEMM applies itself at tp 1).  With the
 // peers mapped this is one fused kernel over NVLink; otherwise NCCL + resid_add.
 static int row_parallel_done(fw_handle* h, const std::string& bias, const float* gate, __nv_bfloat16* mirror,
-                             cudaStream_t s) {
+                             int parity, cudaStream_t s) {
   if (h->tp == 1) return 0;
+  if (h->push)
+    return tp_combine2(h->peers, parity, h->part, h->L, h->D, W(h, bias), gate, h->xs, mirror, h->status, s);
   if (h->use_peers) return tp_reduce(h->peers, h->L, h->D, W(h, bias), gate, h->xs, mirror, h->status, s);
   FW_TRY(tp_allreduce(h->comm, h->part, (size_t)h->L * h->D, FW_BF16, s));
   // the adaLN gate is one row for every frame (e0 is per timestep; static.py:204, 220, 225)
@@ -745,18 +749,18 @@ static int forward(fw_handle* h, int step, int first, int write, const __nv_bflo
       }
     }
     FW_TRY(run_from(h, ly.o, h->ao, Dl, s));
-    FW_TRY(row_parallel_done(h, p + "sa.o.b", ee + 2 * D, nullptr, s));
+    FW_TRY(row_parallel_done(h, p + "sa.o.b", ee + 2 * D, nullptr, (3 * i) & 1, s));
     FW_TRY(ln_op(h, L, D, c.eps, nullptr, nullptr, W(h, p + "n3.w"), W(h, p + "n3.b"), s));
     FW_TRY(run(ly.caq, s));
     FW_TRY(rms_norm_op(h, h->q, nullptr, W(h, p + "ca.nq.w"), nullptr, L, nullptr, s));
     FW_TRY(run(ly.cross, s));
     FW_TRY(run_from(h, ly.cao, h->ao, Dl, s));
-    FW_TRY(row_parallel_done(h, p + "ca.o.b", nullptr, nullptr, s));
+    FW_TRY(row_parallel_done(h, p + "ca.o.b", nullptr, nullptr, (3 * i + 1) & 1, s));
     if (ly.act >= 0) FW_TRY(action(h, i, first, write, s));
     FW_TRY(ln_op(h, L, D, c.eps, ee + 3 * D, ee + 4 * D, nullptr, nullptr, s));
     FW_TRY(run(ly.ff0, s));
     FW_TRY(run_from(h, ly.ff2, h->hb, h->FFl, s));
-    FW_TRY(row_parallel_done(h, p + "ffn.2.b", ee + 5 * D, nullptr, s));
+    FW_TRY(row_parallel_done(h, p + "ffn.2.b", ee + 5 * D, nullptr, (3 * i + 2) & 1, s));
   }
   FW_TRY(ln_f32(h->xs, D, L, D, c.eps, h->hmod, h->hmod + D, nullptr, nullptr, h->y, D, s));
   FW_TRY(run(h->head, s));
@@ -947,13 +951,34 @@ int fw_tp_peers(fw_handle* h, void* const* ws_bases, int n) {
   }
   P.epoch = reinterpret_cast<unsigned*>(const_cast<uint8_t*>(own) + off("tp.epoch"));
   h->use_peers = true;
+  // Two ranks: the row-parallel GEMMs (sa.o, ca.o, ffn.2 of every block, call k of a forward
+  // writing the peer's recv[k % 2]) also store their partial into the other rank's memory, so
+  // the transfer runs while the GEMM computes and the reduction reads local memory only.
+  const char* pe = getenv("FW_TP_PUSH");
+  if (h->tp == 2 && !(pe && pe[0] == '0') && !h->fp8) {
+    const size_t LD = (size_t)h->L * h->D;
+    for (int j = 0; j < n; ++j) P.recv[j] = reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<uint8_t*>(ws_bases[j]) + off("tp.recv"));
+    __nv_bfloat16* peer_recv = P.recv[1 - h->tpr];
+    for (int i = 0; i < h->cfg.layers; ++i) {
+      fw::GemmOp* ops[3] = {&h->layers[i].o, &h->layers[i].cao, &h->layers[i].ff2};
+      for (int k = 0; k < 3; ++k) {
+        fw::GemmEpi& e = ops[k]->args.epi;
+        if (e.mode != fw::EPI_BF16 || e.out[0] != h->part) return FW_ESTATE;
+        e.mode = fw::EPI_BF16_PUSH;
+        e.peer_out = peer_recv + (size_t)((3 * i + k) & 1) * LD;
+        int rc = fw::gemm_check(ops[k]->args, ops[k]->bn);
+        if (rc) return rc;
+      }
+    }
+    h->push = true;
+  }
   return 0;
 }
 
 int fw_tp_reduce_once(fw_handle* h, void* stream) {
   if (!h) return FW_EINVAL;
   if (h->tp == 1 || !h->finalized || !(h->use_peers || h->comm)) return FW_ESTATE;
-  return fw::row_parallel_done(h, "b0.sa.o.b", nullptr, nullptr, reinterpret_cast<cudaStream_t>(stream));
+  return fw::row_parallel_done(h, "b0.sa.o.b", nullptr, nullptr, 0, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int fw_tp_allreduce(fw_handle* h, void* buf, size_t count, int dtype, void* stream) {

@@ -128,4 +128,44 @@ __device__ __forceinline__ void epilogue_chunk_tma(const GemmEpi& e, const CUten
   __syncwarp();
 }
 
+// EPI_BF16_PUSH: 64 columns (two accumulator chunks) of the warp's 32 rows become a 32 x 128-byte
+// bf16 box in shared memory (16-byte piece p of row l at position p ^ (l % 8): conflict-free
+// writes by row, conflict-free reads by 8 lanes per row), then the warp stores the box
+// row-contiguously, four rows (512 bytes) per instruction, to out[0] and to peer_out (another
+// GPU's memory, so these stores cross NVLink as whole 128-byte lines).  `row` is clamped for
+// the bias read; rows >= M and columns >= N are not stored.
+__device__ __forceinline__ void epilogue_push64(const GemmEpi& e, int row, int row0, int colb, int M, int N,
+                                                const uint32_t (&r0)[32], const uint32_t (&r1)[32], uint8_t* box,
+                                                int lane) {
+  const int frame = row / e.rows_per_frame;
+#pragma unroll
+  for (int cc = 0; cc < 2; ++cc) {
+    float v[32];
+    const uint32_t (&r)[32] = cc ? r1 : r0;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+    if (colb + cc * 32 < N) add_bias(e, frame, colb + cc * 32, v);
+#pragma unroll
+    for (int pc = 0; pc < 4; ++pc) {
+      const int piece = cc * 4 + pc;
+      *reinterpret_cast<uint4*>(box + lane * 128 + ((piece ^ (lane & 7)) << 4)) =
+          make_uint4(pack_bf16(v[8 * pc + 0], v[8 * pc + 1]), pack_bf16(v[8 * pc + 2], v[8 * pc + 3]),
+                     pack_bf16(v[8 * pc + 4], v[8 * pc + 5]), pack_bf16(v[8 * pc + 6], v[8 * pc + 7]));
+    }
+  }
+  __syncwarp();
+#pragma unroll
+  for (int it = 0; it < 8; ++it) {
+    const int rr = it * 4 + (lane >> 3), p = lane & 7;
+    const uint4 u = *reinterpret_cast<const uint4*>(box + rr * 128 + ((p ^ (rr & 7)) << 4));
+    const int grow = row0 + rr, gcol = colb + p * 8;
+    if (grow < M && gcol < N) {
+      const size_t off = (size_t)grow * e.ld_out + gcol;
+      *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(e.out[0]) + off) = u;
+      *reinterpret_cast<uint4*>(e.peer_out + off) = u;
+    }
+  }
+  __syncwarp();
+}
+
 }  // namespace fw

@@ -58,6 +58,7 @@ enum EpiMode : int {
   EPI_F32 = 3,         // out_f32 = acc + bias
   EPI_GELU_ERF_BF16 = 4,   // out_bf16 = gelu_erf(acc + bias)
   EPI_RESID_TMA = 5,   // resid_f32 += gate[frame] * (acc + bias) by TMA reduce-add (no mirror; needs tmC)
+  EPI_BF16_PUSH = 6,   // out_bf16 = acc + bias, stored coalesced to out[0] and to peer_out (another GPU)
 };
 
 struct GemmEpi {
@@ -73,6 +74,7 @@ struct GemmEpi {
   float* resid = nullptr;                       // [M, ld_resid] fp32
   int ld_resid = 0;
   __nv_bfloat16* mirror = nullptr;              // [M, ld_mirror] bf16 copy of the new residual (optional)
+  __nv_bfloat16* peer_out = nullptr;            // EPI_BF16_PUSH: second destination [M, ld_out], peer memory
   int ld_mirror = 0;
   int rows_per_frame = 1 << 30;
 };

@@ -25,6 +25,7 @@ struct TpPeers {
   __nv_bfloat16* red[TP_MAX_RANKS] = {};         // [L, D] bf16 reduced sums (+ bias)
   unsigned* flags[TP_MAX_RANKS] = {};            // [3][TP_MAX_RANKS][TP_MAX_CTAS] epochs
   float* gat[TP_MAX_RANKS] = {};                 // [2][TP_MAX_RANKS][gat_rows][2] gathered sums of squares
+  __nv_bfloat16* recv[TP_MAX_RANKS] = {};        // 2 ranks: [2][L, D] bf16 partials pushed by the other rank
   unsigned* epoch = nullptr;                     // this rank's [2][TP_MAX_CTAS] call counters
 };
 
@@ -32,6 +33,12 @@ struct TpPeers {
 // mirror (optional) = bf16 copy of the new xs.  gate: one [D] row for all tokens, or null.
 int tp_reduce(const TpPeers& p, int L, int D, const __nv_bfloat16* bias, const float* gate, float* xs,
               __nv_bfloat16* mirror, int* status, cudaStream_t s);
+// Two ranks, after row-parallel GEMMs that pushed their partial sums into the other rank's
+// recv[parity] (EPI_BF16_PUSH): xs += gate * (part[0] + part[1] + bias) from local memory only,
+// the partials summed in rank order (identical on both ranks).
+int tp_combine2(const TpPeers& p, int parity, const __nv_bfloat16* own_part, int L, int D,
+                const __nv_bfloat16* bias, const float* gate, float* xs, __nv_bfloat16* mirror, int* status,
+                cudaStream_t s);
 // ss[M, 2] (fp32, in place) = sum over ranks of ss.
 int tp_sumsq(const TpPeers& p, float* ss, int M, int* status, cudaStream_t s);
 

@@ -186,7 +186,15 @@ __global__ void __launch_bounds__(320, 1)
       tmem_ld_wait();
       tc_fence_before();
       mbar_arrive(tempty + acc);                 // the accumulator buffer is free again
-      if (args.epi.mode == EPI_RESID_TMA) {      // warp-collective: every lane takes part
+      if (args.epi.mode == EPI_BF16_PUSH) {      // warp-collective: every lane takes part
+        uint8_t* box = smem + C::EPI_OFF + (warp - 2) * C::EPI_BOX;
+#pragma unroll
+        for (int b = 0; b < NC / 2; ++b) {
+          const int colb = colh + b * 64;
+          if (colb < N) epilogue_push64(args.epi, min(row, M - 1), mb * 128 + q * 32, colb, M, N, r[2 * b],
+                                        r[2 * b + 1], box, lane);
+        }
+      } else if (args.epi.mode == EPI_RESID_TMA) {      // warp-collective: every lane takes part
         uint8_t* box = smem + C::EPI_OFF + (warp - 2) * C::EPI_BOX;
 #pragma unroll
         for (int c = 0; c < NC; ++c) {
@@ -237,6 +245,10 @@ int gemm_check(const GemmArgs& a, int bn) {
     }
     case EPI_F32:
       if (!e.out[0] || !al16(e.out[0]) || e.ld_out % 4) return FW_EALIGN;
+      break;
+    case EPI_BF16_PUSH:
+      if (bn < 128 || !e.out[0] || !e.peer_out || !al16(e.out[0]) || !al16(e.peer_out) || e.ld_out % 8)
+        return FW_EINVAL;
       break;
     case EPI_RESID_TMA:
       if (e.mirror) return FW_EINVAL;   // the mirror needs the updated residual in registers

@@ -167,6 +167,82 @@ __global__ void __launch_bounds__(512) tp_reduce2_kernel(TpPeers p, int L, int D
   pdl_trigger();
 }
 
+// Two ranks with the transfer folded into the GEMMs: each rank's row-parallel GEMM already
+// stored its partial into the other rank's recv[parity] (EPI_BF16_PUSH), so CTA c only signals
+// "my GEMM is complete" (its stores into the other GPU were issued by the finished kernel),
+// waits for the other rank's signal, and updates rows chunk c of xs from local memory.  recv is
+// double-buffered by call parity: the other rank's GEMM of call e+2 writes recv[parity(e)] only
+// after its combine of call e+1, which waits for this rank's signal of call e+1, given after
+// this rank's combine of call e finished reading.
+__global__ void __launch_bounds__(512) tp_combine2_kernel(TpPeers p, const __nv_bfloat16* __restrict__ own_part,
+                                                          const __nv_bfloat16* __restrict__ recv, int L, int D,
+                                                          const __nv_bfloat16* __restrict__ bias,
+                                                          const float* __restrict__ gate, float* __restrict__ xs,
+                                                          __nv_bfloat16* __restrict__ mirror, int* status) {
+  pdl_wait();
+  const int c = blockIdx.x, G = gridDim.x, r = p.rank;
+  __shared__ unsigned s_e;
+  if (threadIdx.x == 0) {
+    unsigned* ep = p.epoch + c;
+    s_e = *ep + 1u;
+    *ep = s_e;
+  }
+  __syncthreads();
+  const unsigned e = s_e;
+  signal_peers(p, 0, c, e);
+  wait_peers(p.flags[r] + 0, 2, c, e, status);
+  const int nv = D / 8;
+  constexpr int U = 4;
+  const int rows_c = (L + G - 1) / G;
+  const int r0 = c * rows_c, r1 = min(r0 + rows_c, L);
+  const size_t base = (size_t)r0 * D;
+  const int n = max(r1 - r0, 0) * nv;
+  // rank order: part of rank 0 first
+  const uint4* p0 = reinterpret_cast<const uint4*>((r == 0 ? own_part : recv) + base);
+  const uint4* p1 = reinterpret_cast<const uint4*>((r == 0 ? recv : own_part) + base);
+  for (int i0 = threadIdx.x; i0 < n; i0 += U * blockDim.x) {
+    uint4 w0[U], w1[U];
+    float4 x0[U], x1[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int i = i0 + u * blockDim.x;
+      if (i < n) {
+        w0[u] = __ldcg(p0 + i);
+        w1[u] = __ldcg(p1 + i);
+        const float4* xr = reinterpret_cast<const float4*>(xs + base + (size_t)i * 8);
+        x0[u] = xr[0];
+        x1[u] = xr[1];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int i = i0 + u * blockDim.x;
+      if (i >= n) continue;
+      const int col = (i % nv) * 8;
+      float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      add8(v, w0[u]);
+      add8(v, w1[u]);
+      if (bias) add8(v, *reinterpret_cast<const uint4*>(bias + col));
+      float4 a0 = x0[u], a1 = x1[u];
+      if (gate) {
+        const float4 g0 = *reinterpret_cast<const float4*>(gate + col), g1 = *reinterpret_cast<const float4*>(gate + col + 4);
+        a0.x += g0.x * v[0]; a0.y += g0.y * v[1]; a0.z += g0.z * v[2]; a0.w += g0.w * v[3];
+        a1.x += g1.x * v[4]; a1.y += g1.y * v[5]; a1.z += g1.z * v[6]; a1.w += g1.w * v[7];
+      } else {
+        a0.x += v[0]; a0.y += v[1]; a0.z += v[2]; a0.w += v[3];
+        a1.x += v[4]; a1.y += v[5]; a1.z += v[6]; a1.w += v[7];
+      }
+      float4* xw = reinterpret_cast<float4*>(xs + base + (size_t)i * 8);
+      xw[0] = a0;
+      xw[1] = a1;
+      if (mirror)
+        *reinterpret_cast<uint4*>(mirror + base + (size_t)i * 8) =
+            make_uint4(pack_bf16(a0.x, a0.y), pack_bf16(a0.z, a0.w), pack_bf16(a1.x, a1.y), pack_bf16(a1.z, a1.w));
+    }
+  }
+  pdl_trigger();
+}
+
 template <int TP>
 __global__ void __launch_bounds__(512) tp_reduce_kernel(TpPeers p, int L, int D, const __nv_bfloat16* __restrict__ bias,
                                                         const float* __restrict__ gate, float* __restrict__ xs,
@@ -322,6 +398,15 @@ int tp_reduce(const TpPeers& p, int L, int D, const __nv_bfloat16* bias, const f
     case 8: launch_k(tp_reduce_kernel<8>, tp_grid(), 512, 0, s, p, L, D, bias, gate, xs, mirror, status); break;
     default: return FW_EINVAL;
   }
+  return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
+}
+
+int tp_combine2(const TpPeers& p, int parity, const __nv_bfloat16* own_part, int L, int D,
+                const __nv_bfloat16* bias, const float* gate, float* xs, __nv_bfloat16* mirror, int* status,
+                cudaStream_t s) {
+  if (p.tp != 2 || !p.recv[p.rank] || D % 8 || (parity & ~1)) return FW_EINVAL;
+  const __nv_bfloat16* recv = p.recv[p.rank] + (size_t)parity * L * D;
+  launch_k(tp_combine2_kernel, tp_grid(), 512, 0, s, p, own_part, recv, L, D, bias, gate, xs, mirror, status);
   return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
 }
 
