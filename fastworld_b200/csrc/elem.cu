@@ -125,6 +125,22 @@ __global__ void __launch_bounds__(256) ln_kernel(const Tin* __restrict__ x, int 
   }
 }
 
+// Eight consecutive elements into registers (16-byte loads).
+__device__ __forceinline__ void load8(const float* p, float (&v)[8]) {
+  const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+__device__ __forceinline__ void load8(const __nv_bfloat16* p, float (&v)[8]) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = unpack_bf16(w[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
 template <typename Tin>
 static int ln_dispatch(const Tin* x, int ldx, int M, int D, float eps, const float* shift, const float* scale,
                        const __nv_bfloat16* w, const __nv_bfloat16* b, __nv_bfloat16* out, int ldo, cudaStream_t s,
@@ -253,10 +269,68 @@ __global__ void __launch_bounds__(256) rms_rope_kernel(RmsPair pr, int ldx, int 
   }
 }
 
+// The same with eight consecutive elements per lane (D = 256 * NG8): one 16-byte load and store
+// per group; the lane's four RoPE pairs are consecutive table entries (two 16-byte loads).
+template <int NG8>
+__global__ void __launch_bounds__(256) rms_rope8_kernel(RmsPair pr, int ldx, int M, float eps,
+                                                        const float2* __restrict__ rope, int hd, int ldo) {
+  pdl_trigger();
+  pdl_wait();
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (row >= M) return;
+  const __nv_bfloat16* __restrict__ x = pr.x[blockIdx.y];
+  const __nv_bfloat16* __restrict__ w = pr.w[blockIdx.y];
+  __nv_bfloat16* __restrict__ out = pr.out[blockIdx.y];
+  constexpr int D = 256 * NG8;
+  float v[NG8][8];
+  float q = 0.f;
+#pragma unroll
+  for (int g = 0; g < NG8; ++g) {
+    load8(x + (size_t)row * ldx + g * 256 + lane * 8, v[g]);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) q += v[g][i] * v[g][i];
+  }
+  const float tot = pr.ss ? __ldg(pr.ss + (size_t)row * 2 + blockIdx.y) : warp_sum(q);
+  const float r = rsqrtf(tot * (pr.ss ? pr.inv_d : 1.f / D) + eps);
+  const int half = hd >> 1;
+#pragma unroll
+  for (int g = 0; g < NG8; ++g) {
+    const int c = g * 256 + lane * 8;
+    float wv[8], y[8];
+    load8(w + c, wv);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) y[i] = v[g][i] * r * wv[i];
+    if (rope) {
+      const float4* rp = reinterpret_cast<const float4*>(rope + (size_t)row * half + ((c % hd) >> 1));
+      const float4 cs01 = __ldg(rp), cs23 = __ldg(rp + 1);
+      const float cs[8] = {cs01.x, cs01.y, cs01.z, cs01.w, cs23.x, cs23.y, cs23.z, cs23.w};
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+        const float a = y[2 * p], bb = y[2 * p + 1], co = cs[2 * p], si = cs[2 * p + 1];
+        y[2 * p] = a * co - bb * si;
+        y[2 * p + 1] = a * si + bb * co;
+      }
+    }
+    *reinterpret_cast<uint4*>(out + (size_t)row * ldo + c) =
+        make_uint4(pack_bf16(y[0], y[1]), pack_bf16(y[2], y[3]), pack_bf16(y[4], y[5]), pack_bf16(y[6], y[7]));
+  }
+}
+
 static int rms_rope_launch(const RmsPair& pr, bool two, int ldx, int M, int D, float eps, const float2* rope, int hd,
                            int ldo, cudaStream_t s) {
   if (D % 128 || ldx % 4 || ldo % 4 || (rope && (hd % 4 || D % hd))) return FW_ESHAPE;
   const dim3 grid((M + 7) / 8, two ? 2 : 1), block(256);
+  if (D % 256 == 0 && ldx % 8 == 0 && ldo % 8 == 0 && (!rope || hd % 8 == 0)) {
+    switch (D / 256) {
+#define FW_RMS8_CASE(n) \
+  case n: launch_k(rms_rope8_kernel<n>, grid, block, 0, s, pr, ldx, M, eps, rope, hd, ldo); \
+    return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
+      FW_RMS8_CASE(1) FW_RMS8_CASE(2) FW_RMS8_CASE(3) FW_RMS8_CASE(4) FW_RMS8_CASE(5) FW_RMS8_CASE(6)
+      FW_RMS8_CASE(8) FW_RMS8_CASE(10) FW_RMS8_CASE(20)
+#undef FW_RMS8_CASE
+      default: break;
+    }
+  }
   switch (D / 128) {
 #define FW_RMS_CASE(n) \
   case n: launch_k(rms_rope_kernel<n>, grid, block, 0, s, pr, ldx, M, eps, rope, hd, ldo); break;
@@ -621,8 +695,55 @@ __device__ __forceinline__ void st2(__nv_bfloat16* p, float2 v) {
 }
 __device__ __forceinline__ float2 bround(float2 v) { return unpack_bf16(pack_bf16(v.x, v.y)); }
 
-// Mouse branch: one warp per (spatial position s, head h).  qkv [L, 3A] rows f * S + s;
-// history mk/mv [S, F, AH, 64]; out [L, A].  Keys: [history (unless first) | current].
+// 8 lanes per (row, head), 8 consecutive head dims per lane (4 interleaved RoPE pairs); the
+// lane group's reductions use 3 xor-shuffle steps.
+__device__ __forceinline__ float group8_sum(float v) {
+  v += __shfl_xor_sync(0xffffffffu, v, 4);
+  v += __shfl_xor_sync(0xffffffffu, v, 2);
+  v += __shfl_xor_sync(0xffffffffu, v, 1);
+  return v;
+}
+__device__ __forceinline__ void unpack8(const uint4& u, float (&v)[8]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = unpack_bf16(w[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+__device__ __forceinline__ uint4 pack8(const float (&v)[8]) {
+  return make_uint4(pack_bf16(v[0], v[1]), pack_bf16(v[2], v[3]), pack_bf16(v[4], v[5]), pack_bf16(v[6], v[7]));
+}
+// RMSNorm over the head's 64 dims (weights w[8] of this lane's dims) + interleaved-pair RoPE
+// with cos / sin of pair (d + 2i) taken at cs / sn[2i]; the result rounded to bf16 (the
+// reference keeps q and k in bf16).
+__device__ __forceinline__ void norm_rope8(float (&v)[8], const float (&w)[8], const float* cs, const float* sn,
+                                           float eps) {
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) q += v[i] * v[i];
+  const float r = rsqrtf(group8_sum(q) * (1.f / 64.f) + eps);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float a = v[2 * i] * r * w[2 * i], b = v[2 * i + 1] * r * w[2 * i + 1];
+    const float c = cs[2 * i], sv = sn[2 * i];
+    v[2 * i] = a * c - b * sv;
+    v[2 * i + 1] = b * c + a * sv;
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __bfloat162float(__float2bfloat16_rn(v[i]));
+}
+__device__ __forceinline__ float dot8(const float (&a)[8], const float (&b)[8]) {
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) s += a[i] * b[i];
+  return s;
+}
+
+// Mouse branch: 8 lanes per (spatial position s, head h), four per warp.  qkv [L, 3A] rows
+// f * S + s; history mk/mv [S, F, AH, 64]; out [L, A].  Keys: [history (unless first) |
+// current frames].
 template <int F>
 __global__ void __launch_bounds__(256) mouse_attn_kernel(const __nv_bfloat16* __restrict__ qkv,
                                                          const __nv_bfloat16* __restrict__ wq,
@@ -633,21 +754,27 @@ __global__ void __launch_bounds__(256) mouse_attn_kernel(const __nv_bfloat16* __
                                                          __nv_bfloat16* __restrict__ out, int S, int AH, float eps) {
   pdl_trigger();
   pdl_wait();
-  const int wid = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-  if (wid >= S * AH) return;
-  const int s = wid / AH, h = wid % AH, A = AH * 64, d = 2 * lane;
-  const float2 wqv = ld2(wq + d), wkv = ld2(wk + d);
-  float2 q[F], kc[F], vc[F], kh[F], vh[F];
+  const int lane = threadIdx.x & 31;
+  const int slot = (blockIdx.x * 8 + (threadIdx.x >> 5)) * 4 + (lane >> 3);
+  const bool live = slot < S * AH;   // dead groups still take part in the warp shuffles
+  const int sl = live ? slot : 0;
+  const int s = sl / AH, h = sl % AH, A = AH * 64, d = (lane & 7) * 8;
+  float wqv[8], wkv[8];
+  unpack8(*reinterpret_cast<const uint4*>(wq + d), wqv);
+  unpack8(*reinterpret_cast<const uint4*>(wk + d), wkv);
+  float q[F][8], kc[F][8];
+  uint4 vc[F], kh[F], vh[F];
 #pragma unroll
   for (int f = 0; f < F; ++f) {
     const __nv_bfloat16* r = qkv + (size_t)(f * S + s) * 3 * A + h * 64 + d;
-    const float c = acos_[f * 64 + d], sn = asin_[f * 64 + d];
-    q[f] = bround(norm_rope64(ld2(r), wqv.x, wqv.y, c, sn, eps));
-    kc[f] = bround(norm_rope64(ld2(r + A), wkv.x, wkv.y, c, sn, eps));
-    vc[f] = ld2(r + 2 * A);
+    unpack8(*reinterpret_cast<const uint4*>(r), q[f]);
+    unpack8(*reinterpret_cast<const uint4*>(r + A), kc[f]);
+    vc[f] = *reinterpret_cast<const uint4*>(r + 2 * A);
+    norm_rope8(q[f], wqv, acos_ + f * 64 + d, asin_ + f * 64 + d, eps);
+    norm_rope8(kc[f], wkv, acos_ + f * 64 + d, asin_ + f * 64 + d, eps);
     const size_t ho = (((size_t)s * F + f) * AH + h) * 64 + d;
-    kh[f] = first ? make_float2(0.f, 0.f) : ld2(mk + ho);
-    vh[f] = first ? make_float2(0.f, 0.f) : ld2(mv + ho);
+    kh[f] = first ? make_uint4(0, 0, 0, 0) : *reinterpret_cast<const uint4*>(mk + ho);
+    vh[f] = first ? make_uint4(0, 0, 0, 0) : *reinterpret_cast<const uint4*>(mv + ho);
   }
   const float scale = 0.125f;   // 1 / sqrt(64)
 #pragma unroll
@@ -656,26 +783,35 @@ __global__ void __launch_bounds__(256) mouse_attn_kernel(const __nv_bfloat16* __
     float mx = -INFINITY;
 #pragma unroll
     for (int j = 0; j < F; ++j) {
-      sc[j] = first ? -INFINITY : warp_sum(q[f].x * kh[j].x + q[f].y * kh[j].y) * scale;
-      sc[F + j] = warp_sum(q[f].x * kc[j].x + q[f].y * kc[j].y) * scale;
+      float khf[8];
+      unpack8(kh[j], khf);
+      const float a = group8_sum(dot8(q[f], khf)) * scale, b = group8_sum(dot8(q[f], kc[j])) * scale;
+      sc[j] = first ? -INFINITY : a;
+      sc[F + j] = b;
       mx = fmaxf(mx, fmaxf(sc[j], sc[F + j]));
     }
-    float den = 0.f, ox = 0.f, oy = 0.f;
+    float den = 0.f, o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int j = 0; j < F; ++j) {
       const float ph = __expf(sc[j] - mx), pc = __expf(sc[F + j] - mx);
+      float a[8], b[8];
+      unpack8(vh[j], a);
+      unpack8(vc[j], b);
       den += ph + pc;
-      ox += ph * vh[j].x + pc * vc[j].x;
-      oy += ph * vh[j].y + pc * vc[j].y;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] += ph * a[i] + pc * b[i];
     }
-    st2(out + (size_t)(f * S + s) * A + h * 64 + d, make_float2(ox / den, oy / den));
+    const float inv = 1.f / den;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] *= inv;
+    if (live) *reinterpret_cast<uint4*>(out + (size_t)(f * S + s) * A + h * 64 + d) = pack8(o);
   }
-  if (write) {
+  if (write && live) {
 #pragma unroll
     for (int f = 0; f < F; ++f) {
       const size_t ho = (((size_t)s * F + f) * AH + h) * 64 + d;
-      st2(mk + ho, kc[f]);
-      st2(mv + ho, vc[f]);
+      *reinterpret_cast<uint4*>(mk + ho) = pack8(kc[f]);
+      *reinterpret_cast<uint4*>(mv + ho) = vc[f];
     }
   }
 }
@@ -684,7 +820,8 @@ int mouse_attn(const __nv_bfloat16* qkv, const __nv_bfloat16* wq, const __nv_bfl
                const float* asin_, __nv_bfloat16* mk, __nv_bfloat16* mv, int first, int write, __nv_bfloat16* out,
                int S, int F, int AH, float eps, cudaStream_t s) {
   if (F != 3) return FW_ESHAPE;
-  launch_k(mouse_attn_kernel<3>, (S * AH + 7) / 8, 256, 0, s, qkv, wq, wk, acos_, asin_, mk, mv, first, write, out, S, AH, eps);
+  launch_k(mouse_attn_kernel<3>, (S * AH + 31) / 32, 256, 0, s, qkv, wq, wk, acos_, asin_, mk, mv, first, write, out, S,
+           AH, eps);
   return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
 }
 
@@ -710,8 +847,8 @@ int kb_kv(const float* kv, const __nv_bfloat16* wk, const float* acos_, const fl
   return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
 }
 
-// Keyboard attention: one warp per (token, head); q = RoPE(RMSNorm(mq) * wq) at the token's
-// frame; keys [kk (unless first) | current], F each, shared by all tokens.
+// Keyboard attention: 8 lanes per (token row, head), four per warp; q = RoPE(RMSNorm(mq));
+// keys [kh (unless first) | kc] and values of the row's frame-independent keyboard tokens.
 template <int F>
 __global__ void __launch_bounds__(256) kb_attn_kernel(const __nv_bfloat16* __restrict__ mq,
                                                       const __nv_bfloat16* __restrict__ wq,
@@ -724,37 +861,50 @@ __global__ void __launch_bounds__(256) kb_attn_kernel(const __nv_bfloat16* __res
                                                       __nv_bfloat16* __restrict__ out, int L, int S, int AH, float eps) {
   pdl_trigger();
   pdl_wait();
-  const int wid = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-  if (wid >= L * AH) return;
-  const int row = wid / AH, h = wid % AH, f = row / S, A = AH * 64, d = 2 * lane;
-  const float2 w = ld2(wq + d);
-  const float2 q = bround(norm_rope64(ld2(mq + (size_t)row * A + h * 64 + d), w.x, w.y, acos_[f * 64 + d],
-                                      asin_[f * 64 + d], eps));
+  const int lane = threadIdx.x & 31;
+  const int slot = (blockIdx.x * 8 + (threadIdx.x >> 5)) * 4 + (lane >> 3);
+  const bool live = slot < L * AH;
+  const int sl = live ? slot : 0;
+  const int row = sl / AH, h = sl % AH, f = row / S, A = AH * 64, d = (lane & 7) * 8;
+  float w[8], q[8];
+  unpack8(*reinterpret_cast<const uint4*>(wq + d), w);
+  unpack8(*reinterpret_cast<const uint4*>(mq + (size_t)row * A + h * 64 + d), q);
+  norm_rope8(q, w, acos_ + f * 64 + d, asin_ + f * 64 + d, eps);
   float sc[2 * F];
   float mx = -INFINITY;
 #pragma unroll
   for (int j = 0; j < F; ++j) {
-    const float2 a = ld2(kh + (size_t)j * A + h * 64 + d), b = ld2(kc + (size_t)j * A + h * 64 + d);
-    sc[j] = first ? -INFINITY : warp_sum(q.x * a.x + q.y * a.y) * 0.125f;
-    sc[F + j] = warp_sum(q.x * b.x + q.y * b.y) * 0.125f;
+    float a[8], b[8];
+    unpack8(*reinterpret_cast<const uint4*>(kh + (size_t)j * A + h * 64 + d), a);
+    unpack8(*reinterpret_cast<const uint4*>(kc + (size_t)j * A + h * 64 + d), b);
+    const float sa = group8_sum(dot8(q, a)) * 0.125f, sb = group8_sum(dot8(q, b)) * 0.125f;
+    sc[j] = first ? -INFINITY : sa;
+    sc[F + j] = sb;
     mx = fmaxf(mx, fmaxf(sc[j], sc[F + j]));
   }
-  float den = 0.f, ox = 0.f, oy = 0.f;
+  float den = 0.f, o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
   for (int j = 0; j < F; ++j) {
     const float ph = __expf(sc[j] - mx), pc = __expf(sc[F + j] - mx);
-    const float2 a = ld2(vh + (size_t)j * A + h * 64 + d), b = ld2(vc + (size_t)j * A + h * 64 + d);
+    float a[8], b[8];
+    unpack8(*reinterpret_cast<const uint4*>(vh + (size_t)j * A + h * 64 + d), a);
+    unpack8(*reinterpret_cast<const uint4*>(vc + (size_t)j * A + h * 64 + d), b);
     den += ph + pc;
-    ox += ph * a.x + pc * b.x;
-    oy += ph * a.y + pc * b.y;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] += ph * a[i] + pc * b[i];
   }
-  st2(out + (size_t)row * A + h * 64 + d, make_float2(ox / den, oy / den));
+  const float inv = 1.f / den;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) o[i] *= inv;
+  if (live) *reinterpret_cast<uint4*>(out + (size_t)row * A + h * 64 + d) = pack8(o);
 }
+
 int kb_attn(const __nv_bfloat16* mq, const __nv_bfloat16* wq, const float* acos_, const float* asin_,
             const __nv_bfloat16* kh, const __nv_bfloat16* vh, const __nv_bfloat16* kc, const __nv_bfloat16* vc,
             int first, __nv_bfloat16* out, int L, int S, int F, int AH, float eps, cudaStream_t s) {
   if (F != 3) return FW_ESHAPE;
-  launch_k(kb_attn_kernel<3>, (L * AH + 7) / 8, 256, 0, s, mq, wq, acos_, asin_, kh, vh, kc, vc, first, out, L, S, AH, eps);
+  launch_k(kb_attn_kernel<3>, (L * AH + 31) / 32, 256, 0, s, mq, wq, acos_, asin_, kh, vh, kc, vc, first, out, L, S,
+           AH, eps);
   return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
 }
 
