@@ -268,6 +268,14 @@ class B200StaticMG:
             off += (nb + 255) // 256 * 256
         return SessionState(blob, views)
 
+    def state_into(self, st: "SessionState") -> "SessionState":
+        """Snapshot into an existing SessionState's buffer (same session shape) instead of a new
+        allocation: a checkpoint pool recycles evicted checkpoints through this."""
+        if not isinstance(st, SessionState) or st.blob.numel() != self._blob.numel():
+            return self.state()
+        check(lib().fw_copy(ptr(st.blob), ptr(self._blob), self._blob.numel(), stream_ptr()), "fw_copy")
+        return st
+
     def load(self, st) -> None:
         """Restore a snapshot into the live buffers (pointers baked into graphs stay valid)."""
         if isinstance(st, SessionState) and st.blob.numel() == self._blob.numel():

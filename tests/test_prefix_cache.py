@@ -77,3 +77,44 @@ def test_stats_of_a_rewind():
     cache.serve(main)
     _, st = cache.serve(main[:5] + [("img", "a")] * 3)
     assert st["hit"] == 5 and st["restored"] == 1 and st["replayed"] == 1 and st["generated"] == 3
+
+
+class PoolRuntime(FakeRuntime):
+    """FakeRuntime whose snapshots are mutable boxes, recycled through state_into."""
+
+    def __init__(self):
+        super().__init__()
+        self.allocated = 0
+
+    def state(self):
+        self.allocated += 1
+        return [self.h]
+
+    def state_into(self, box):
+        box[0] = self.h
+        return box
+
+    def load(self, st):
+        self.calls["load"] += 1
+        self.h = st[0]
+
+
+def test_bounded_checkpoints_match_scratch_and_recycle():
+    import random
+    rng = random.Random(3)
+    keys = "wasdq"
+    paths = []
+    for _ in range(40):   # random prefixes of a few trunks, like rewinds in an explore workload
+        trunk = [("img", c) for c in rng.choice(["wwwwwwww", "wwssaadd", "wadqwadq"])]
+        cut = rng.randrange(1, 8)
+        paths.append(trunk[:cut] + [("img", rng.choice(keys)) for _ in range(rng.randrange(1, 4))])
+    scratch = PrefixCache(FakeRuntime(), FakeDecoder(), every=None)
+    rt = PoolRuntime()
+    cache = PrefixCache(rt, FakeDecoder(), every=2, max_checkpoints=3)
+    for p in paths:
+        a, _ = scratch.serve(p)
+        b, st = cache.serve(p)
+        assert all(torch.equal(x, y) for x, y in zip(a, b)), p
+    assert len(cache._held) <= 3 and cache.n_evicted > 0
+    assert rt.allocated == 3          # the pool never grew past its bound
+    assert rt.calls["load"] > 0
