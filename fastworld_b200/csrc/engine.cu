@@ -67,7 +67,8 @@ struct fw_handle {
   void* comm = nullptr;           // NCCL communicator (tp > 1)
   fw::TpPeers peers;              // the other ranks' workspaces (tp > 1, after fw_tp_peers)
   bool use_peers = false;         // reductions over peer memory instead of NCCL
-  bool push = false;              // 2 ranks: row-parallel GEMMs push their partials to the peer
+  bool push = false;              // row-parallel GEMMs push their partials to the other ranks
+  size_t recv_stride = 0;         // elements between the two parities of tp.recv (4 / 8 ranks)
   __nv_bfloat16* part = nullptr;  // [L, D] partial output of a row-parallel linear (tp > 1)
   float* ss = nullptr;            // [max(L, Ctx), 2] sums of squares for the sharded RMSNorms
   size_t lat_elems;
@@ -301,7 +302,8 @@ static int register_tensors(fw_handle* h) {
     ws_add(h, "tp.flags", (size_t)3 * TP_MAX_RANKS * TP_MAX_CTAS * sizeof(unsigned));
     ws_add(h, "tp.gat", (size_t)2 * TP_MAX_RANKS * mx({L, h->Ctx}) * 2 * f4);
     ws_add(h, "tp.epoch", (size_t)2 * TP_MAX_CTAS * sizeof(unsigned));
-    if (h->tp == 2) ws_add(h, "tp.recv", (size_t)2 * L * D * bf);   // partials pushed by the other rank
+    // partials pushed by the other ranks' GEMMs: 2 parities x tp slots x ceil(L / tp) rows
+    ws_add(h, "tp.recv", (size_t)2 * h->tp * ((L + h->tp - 1) / h->tp) * D * bf);
   }
   h->ws_bytes = (h->ws_bytes + 1023) & ~(size_t)1023;
   add_tensor(h, "workspace", FW_KIND_WORKSPACE, FW_U8, {(int64_t)h->ws_bytes});
@@ -477,8 +479,11 @@ static int rms_norm_op(fw_handle* h, __nv_bfloat16* x0, __nv_bfloat16* x1, const
 static int row_parallel_done(fw_handle* h, const std::string& bias, const float* gate, __nv_bfloat16* mirror,
                              int parity, cudaStream_t s) {
   if (h->tp == 1) return 0;
-  if (h->push)
+  if (h->push && h->tp == 2)
     return tp_combine2(h->peers, parity, h->part, h->L, h->D, W(h, bias), gate, h->xs, mirror, h->status, s);
+  if (h->push)
+    return tp_reduce(h->peers, h->L, h->D, W(h, bias), gate, h->xs, mirror, h->status, s,
+                     h->peers.recv[h->tpr] + (size_t)parity * h->recv_stride);
   if (h->use_peers) return tp_reduce(h->peers, h->L, h->D, W(h, bias), gate, h->xs, mirror, h->status, s);
   FW_TRY(tp_allreduce(h->comm, h->part, (size_t)h->L * h->D, FW_BF16, s));
   // the adaLN gate is one row for every frame (e0 is per timestep; static.py:204, 220, 225)
@@ -951,21 +956,33 @@ int fw_tp_peers(fw_handle* h, void* const* ws_bases, int n) {
   }
   P.epoch = reinterpret_cast<unsigned*>(const_cast<uint8_t*>(own) + off("tp.epoch"));
   h->use_peers = true;
-  // Two ranks: the row-parallel GEMMs (sa.o, ca.o, ffn.2 of every block, call k of a forward
-  // writing the peer's recv[k % 2]) also store their partial into the other rank's memory, so
-  // the transfer runs while the GEMM computes and the reduction reads local memory only.
+  // The row-parallel GEMMs (sa.o, ca.o, ffn.2 of every block; call k of a forward uses parity
+  // k % 2 of the receive buffers) also store their partial into the other ranks' memory while
+  // they compute: with two ranks the whole partial into the peer's recv, with more the rows of
+  // each rank's slice into that rank's recv slot (reduce-scatter), so the reduction kernels
+  // read the partials from local memory.
   const char* pe = getenv("FW_TP_PUSH");
-  if (h->tp == 2 && !(pe && pe[0] == '0') && !h->fp8) {
+  if (!(pe && pe[0] == '0') && !h->fp8) {
+    const int Ls = (h->L + h->tp - 1) / h->tp;
     const size_t LD = (size_t)h->L * h->D;
+    h->recv_stride = (size_t)h->tp * Ls * h->D;
     for (int j = 0; j < n; ++j) P.recv[j] = reinterpret_cast<__nv_bfloat16*>(reinterpret_cast<uint8_t*>(ws_bases[j]) + off("tp.recv"));
-    __nv_bfloat16* peer_recv = P.recv[1 - h->tpr];
     for (int i = 0; i < h->cfg.layers; ++i) {
       fw::GemmOp* ops[3] = {&h->layers[i].o, &h->layers[i].cao, &h->layers[i].ff2};
       for (int k = 0; k < 3; ++k) {
         fw::GemmEpi& e = ops[k]->args.epi;
+        const int parity = (3 * i + k) & 1;
         if (e.mode != fw::EPI_BF16 || e.out[0] != h->part) return FW_ESTATE;
         e.mode = fw::EPI_BF16_PUSH;
-        e.peer_out = peer_recv + (size_t)((3 * i + k) & 1) * LD;
+        if (h->tp == 2) {
+          e.peer_out = P.recv[1 - h->tpr] + (size_t)parity * LD;
+        } else {
+          e.push_tp = h->tp;
+          e.push_rank = h->tpr;
+          e.push_ls = Ls;
+          for (int j = 0; j < n; ++j)
+            e.push_base[j] = j == h->tpr ? nullptr : P.recv[j] + (size_t)parity * h->recv_stride;
+        }
         int rc = fw::gemm_check(ops[k]->args, ops[k]->bn);
         if (rc) return rc;
       }

@@ -131,8 +131,9 @@ __device__ __forceinline__ void epilogue_chunk_tma(const GemmEpi& e, const CUten
 // EPI_BF16_PUSH: 64 columns (two accumulator chunks) of the warp's 32 rows become a 32 x 128-byte
 // bf16 box in shared memory (16-byte piece p of row l at position p ^ (l % 8): conflict-free
 // writes by row, conflict-free reads by 8 lanes per row), then the warp stores the box
-// row-contiguously, four rows (512 bytes) per instruction, to out[0] and to peer_out (another
-// GPU's memory, so these stores cross NVLink as whole 128-byte lines).  `row` is clamped for
+// row-contiguously, four rows (512 bytes) per instruction, to out[0] and to the other GPUs
+// (peer_out, or the row's owner for push_tp > 2), so the remote stores cross NVLink as whole
+// 128-byte lines.  `row` is clamped for
 // the bias read; rows >= M and columns >= N are not stored.
 __device__ __forceinline__ void epilogue_push64(const GemmEpi& e, int row, int row0, int colb, int M, int N,
                                                 const uint32_t (&r0)[32], const uint32_t (&r1)[32], uint8_t* box,
@@ -162,7 +163,14 @@ __device__ __forceinline__ void epilogue_push64(const GemmEpi& e, int row, int r
     if (grow < M && gcol < N) {
       const size_t off = (size_t)grow * e.ld_out + gcol;
       *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(e.out[0]) + off) = u;
-      *reinterpret_cast<uint4*>(e.peer_out + off) = u;
+      if (e.peer_out) {
+        *reinterpret_cast<uint4*>(e.peer_out + off) = u;
+      } else {   // reduce-scatter: the row's owner gets it in this rank's slot
+        const int j = grow / e.push_ls;
+        if (j != e.push_rank)
+          *reinterpret_cast<uint4*>(e.push_base[j] + ((size_t)e.push_rank * e.push_ls + grow - j * e.push_ls) *
+                                                         e.ld_out + gcol) = u;
+      }
     }
   }
   __syncwarp();

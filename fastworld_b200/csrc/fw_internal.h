@@ -58,7 +58,7 @@ enum EpiMode : int {
   EPI_F32 = 3,         // out_f32 = acc + bias
   EPI_GELU_ERF_BF16 = 4,   // out_bf16 = gelu_erf(acc + bias)
   EPI_RESID_TMA = 5,   // resid_f32 += gate[frame] * (acc + bias) by TMA reduce-add (no mirror; needs tmC)
-  EPI_BF16_PUSH = 6,   // out_bf16 = acc + bias, stored coalesced to out[0] and to peer_out (another GPU)
+  EPI_BF16_PUSH = 6,   // out_bf16 = acc + bias, stored coalesced to out[0] and to other GPUs (see GemmEpi)
 };
 
 struct GemmEpi {
@@ -74,7 +74,13 @@ struct GemmEpi {
   float* resid = nullptr;                       // [M, ld_resid] fp32
   int ld_resid = 0;
   __nv_bfloat16* mirror = nullptr;              // [M, ld_mirror] bf16 copy of the new residual (optional)
-  __nv_bfloat16* peer_out = nullptr;            // EPI_BF16_PUSH: second destination [M, ld_out], peer memory
+  // EPI_BF16_PUSH, besides out[0]: either every row to peer_out [M, ld_out] (two ranks), or
+  // (push_tp > 2) the rows of slice j = row / push_ls to rank j's receive buffer push_base[j],
+  // at slot push_rank: push_base[j] + (push_rank * push_ls + row - j * push_ls) * ld_out
+  // (this rank's own slice stays in out[0] only).
+  __nv_bfloat16* peer_out = nullptr;
+  __nv_bfloat16* push_base[8] = {};
+  int push_tp = 0, push_rank = 0, push_ls = 0;
   int ld_mirror = 0;
   int rows_per_frame = 1 << 30;
 };

@@ -25,14 +25,16 @@ struct TpPeers {
   __nv_bfloat16* red[TP_MAX_RANKS] = {};         // [L, D] bf16 reduced sums (+ bias)
   unsigned* flags[TP_MAX_RANKS] = {};            // [3][TP_MAX_RANKS][TP_MAX_CTAS] epochs
   float* gat[TP_MAX_RANKS] = {};                 // [2][TP_MAX_RANKS][gat_rows][2] gathered sums of squares
-  __nv_bfloat16* recv[TP_MAX_RANKS] = {};        // 2 ranks: [2][L, D] bf16 partials pushed by the other rank
+  __nv_bfloat16* recv[TP_MAX_RANKS] = {};        // [2 parities] x (2 ranks: [L, D]; more: [tp][ceil(L/tp)][D]) pushed partials
   unsigned* epoch = nullptr;                     // this rank's [2][TP_MAX_CTAS] call counters
 };
 
 // xs[L, D] += gate * (sum over ranks of part + bias) on every rank (two-shot over NVLink);
 // mirror (optional) = bf16 copy of the new xs.  gate: one [D] row for all tokens, or null.
+// recv (4 or 8 ranks, optional): this rank's receive buffer holding the other ranks' partial
+// rows of its slice, pushed by their GEMMs ([tp][ceil(L / tp)][D]); phase 1 then reads locally.
 int tp_reduce(const TpPeers& p, int L, int D, const __nv_bfloat16* bias, const float* gate, float* xs,
-              __nv_bfloat16* mirror, int* status, cudaStream_t s);
+              __nv_bfloat16* mirror, int* status, cudaStream_t s, const __nv_bfloat16* recv = nullptr);
 // Two ranks, after row-parallel GEMMs that pushed their partial sums into the other rank's
 // recv[parity] (EPI_BF16_PUSH): xs += gate * (part[0] + part[1] + bias) from local memory only,
 // the partials summed in rank order (identical on both ranks).

@@ -247,8 +247,15 @@ int gemm_check(const GemmArgs& a, int bn) {
       if (!e.out[0] || !al16(e.out[0]) || e.ld_out % 4) return FW_EALIGN;
       break;
     case EPI_BF16_PUSH:
-      if (bn < 128 || !e.out[0] || !e.peer_out || !al16(e.out[0]) || !al16(e.peer_out) || e.ld_out % 8)
+      if (bn < 128 || !e.out[0] || !al16(e.out[0]) || e.ld_out % 8) return FW_EINVAL;
+      if (e.push_tp > 2) {
+        if (e.push_tp > 8 || e.push_ls <= 0 || e.push_rank < 0 || e.push_rank >= e.push_tp || e.peer_out)
+          return FW_EINVAL;
+        for (int j = 0; j < e.push_tp; ++j)
+          if (j != e.push_rank && (!e.push_base[j] || !al16(e.push_base[j]))) return FW_EALIGN;
+      } else if (!e.peer_out || !al16(e.peer_out)) {
         return FW_EINVAL;
+      }
       break;
     case EPI_RESID_TMA:
       if (e.mirror) return FW_EINVAL;   // the mirror needs the updated residual in registers

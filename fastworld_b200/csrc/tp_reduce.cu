@@ -243,10 +243,14 @@ __global__ void __launch_bounds__(512) tp_combine2_kernel(TpPeers p, const __nv_
   pdl_trigger();
 }
 
+// recv != null: the row-parallel GEMMs already pushed every rank's partial rows of this rank's
+// slice into recv (slot j = rank j's rows, [tp][slice][D], EPI_BF16_PUSH with push_tp > 2), so
+// phase 1 reads local memory only; this rank's own partial is p.part[rank].
 template <int TP>
 __global__ void __launch_bounds__(512) tp_reduce_kernel(TpPeers p, int L, int D, const __nv_bfloat16* __restrict__ bias,
                                                         const float* __restrict__ gate, float* __restrict__ xs,
-                                                        __nv_bfloat16* __restrict__ mirror, int* status) {
+                                                        __nv_bfloat16* __restrict__ mirror, int* status,
+                                                        const __nv_bfloat16* __restrict__ recv) {
   pdl_wait();
   const int c = blockIdx.x, G = gridDim.x, tp = TP, r = p.rank;
   __shared__ unsigned s_e;
@@ -276,12 +280,15 @@ __global__ void __launch_bounds__(512) tp_reduce_kernel(TpPeers p, int L, int D,
       float a[U][8];
       uint4 w[TP][U];
 #pragma unroll
-      for (int j = 0; j < TP; ++j)
+      for (int j = 0; j < TP; ++j) {
+        const __nv_bfloat16* src =
+            (recv && j != r) ? recv + ((size_t)j * slice + (r0 - r * slice)) * D : p.part[j] + base;
 #pragma unroll
         for (int u = 0; u < U; ++u) {
           const int i = i0 + u * blockDim.x;
-          w[j][u] = i < n ? __ldcg(reinterpret_cast<const uint4*>(p.part[j] + base) + i) : make_uint4(0, 0, 0, 0);
+          w[j][u] = i < n ? __ldcg(reinterpret_cast<const uint4*>(src) + i) : make_uint4(0, 0, 0, 0);
         }
+      }
 #pragma unroll
       for (int u = 0; u < U; ++u) {
 #pragma unroll
@@ -390,12 +397,12 @@ __global__ void __launch_bounds__(256) tp_sumsq_kernel(TpPeers p, float* __restr
 static int tp_grid() { return num_sms() < TP_MAX_CTAS ? num_sms() : TP_MAX_CTAS; }
 
 int tp_reduce(const TpPeers& p, int L, int D, const __nv_bfloat16* bias, const float* gate, float* xs,
-              __nv_bfloat16* mirror, int* status, cudaStream_t s) {
+              __nv_bfloat16* mirror, int* status, cudaStream_t s, const __nv_bfloat16* recv) {
   if (D % 8) return FW_EINVAL;
   switch (p.tp) {
     case 2: launch_k(tp_reduce2_kernel, tp_grid(), 512, 0, s, p, L, D, bias, gate, xs, mirror, status); break;
-    case 4: launch_k(tp_reduce_kernel<4>, tp_grid(), 512, 0, s, p, L, D, bias, gate, xs, mirror, status); break;
-    case 8: launch_k(tp_reduce_kernel<8>, tp_grid(), 512, 0, s, p, L, D, bias, gate, xs, mirror, status); break;
+    case 4: launch_k(tp_reduce_kernel<4>, tp_grid(), 512, 0, s, p, L, D, bias, gate, xs, mirror, status, recv); break;
+    case 8: launch_k(tp_reduce_kernel<8>, tp_grid(), 512, 0, s, p, L, D, bias, gate, xs, mirror, status, recv); break;
     default: return FW_EINVAL;
   }
   return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
