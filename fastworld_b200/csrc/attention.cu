@@ -36,6 +36,11 @@ constexpr int P_OFF = KV_OFF + 6 * TILE;    // tile t: 2 sub-tiles at P_OFF + t 
 constexpr int BAR_OFF = P_OFF + 4 * TILE;
 constexpr int SMEM = BAR_OFF + 256 + 1024;
 constexpr uint32_t TMEM_COLS = 512;
+// Load order through the K/V ring: K0, K1, V0, K2, V1, K3, V2, ..., K_{n-1}, V_{n-2}, V_{n-1}
+// (the order the MMA issuers consume them: S(0), S(1), PV(0), S(2), PV(1), ...), so each K
+// block is loaded one block further ahead than its V.  Position of each load in that sequence:
+__host__ __device__ constexpr int pos_k(int j) { return j == 0 ? 0 : 2 * j - 1; }
+__host__ __device__ constexpr int pos_v(int j, int n) { return 2 * j + 2 < 2 * n - 1 ? 2 * j + 2 : 2 * n - 1; }
 __host__ __device__ constexpr uint32_t s_col(int t) { return (uint32_t)(t * 256); }
 __host__ __device__ constexpr uint32_t o_col(int t) { return (uint32_t)(t * 256 + 128); }
 }  // namespace attn
@@ -106,13 +111,23 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         tma_load_2d(smem + Q_OFF + t * 2 * TILE, &tmQ, q_full, col, q0 + t * BQ);
         tma_load_2d(smem + Q_OFF + t * 2 * TILE + TILE, &tmQ, q_full, col + 64, q0 + t * BQ);
       }
-      for (int i = 0; i < 2 * nblk; ++i) {   // load i: K_{i/2} (even) or V_{i/2} (odd)
+      for (int i = 0; i < 2 * nblk; ++i) {   // load at position i of the order above
         const int s = i % 3;
         const uint32_t par = (uint32_t)(i / 3) & 1u;
         if (!mbar_wait(kv_free + s, par ^ 1u, abort_flag, args.status, DEV_TIMEOUT_PRODUCER)) break;
-        const int j = i >> 1;
+        bool is_v;
+        int j;
+        if (i == 0) {
+          is_v = false, j = 0;
+        } else if (i == 2 * nblk - 1) {
+          is_v = true, j = nblk - 1;
+        } else if (i & 1) {
+          is_v = false, j = (i + 1) >> 1;
+        } else {
+          is_v = true, j = (i - 2) >> 1;
+        }
         const bool seg0 = j < nb0;
-        const CUtensorMap* m = (i & 1) ? (seg0 ? &tmV0 : &tmV1) : (seg0 ? &tmK0 : &tmK1);
+        const CUtensorMap* m = is_v ? (seg0 ? &tmV0 : &tmV1) : (seg0 ? &tmK0 : &tmK1);
         const int key0 = (seg0 ? j : j - nb0) * BKV;
         uint8_t* dst = smem + KV_OFF + s * 2 * TILE;
         mbar_arrive_expect_tx(kv_full + s, 2 * TILE);
@@ -135,8 +150,8 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
       bool ok = mbar_wait(q_full, 0, abort_flag, args.status, DEV_TIMEOUT_MMA);
       // S_t(j) = Q_t K_j^T into the tile's S columns; needs K_j landed and S_t(j-1) read out
       auto issue_s = [&](int t, int j) -> bool {
-        const int s = (2 * j) % 3;
-        if (!mbar_wait(kv_full + s, (uint32_t)((2 * j) / 3) & 1u, abort_flag, args.status, DEV_TIMEOUT_MMA))
+        const int pk = pos_k(j), s = pk % 3;
+        if (!mbar_wait(kv_full + s, (uint32_t)(pk / 3) & 1u, abort_flag, args.status, DEV_TIMEOUT_MMA))
           return false;
         if (!mbar_wait(s_free + t, ((uint32_t)j & 1u) ^ 1u, abort_flag, args.status, DEV_TIMEOUT_MMA)) return false;
         tc_fence_after();
@@ -154,9 +169,9 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
       };
       // O_t += P_t(j) V_j; needs P_t(j) written and V_j landed
       auto issue_o = [&](int t, int j) -> bool {
-        const int s = (2 * j + 1) % 3;
+        const int pv = pos_v(j, nblk), s = pv % 3;
         if (!mbar_wait(p_full + t, (uint32_t)j & 1u, abort_flag, args.status, DEV_TIMEOUT_MMA)) return false;
-        if (!mbar_wait(kv_full + s, (uint32_t)((2 * j + 1) / 3) & 1u, abort_flag, args.status, DEV_TIMEOUT_MMA))
+        if (!mbar_wait(kv_full + s, (uint32_t)(pv / 3) & 1u, abort_flag, args.status, DEV_TIMEOUT_MMA))
           return false;
         tc_fence_after();
         const uint32_t sp = smem_u32(smem + P_OFF + t * 2 * TILE);
