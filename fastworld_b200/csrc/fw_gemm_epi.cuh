@@ -89,9 +89,12 @@ __device__ __forceinline__ void epilogue_chunk(const GemmEpi& e, int row, int co
 // layout TMA expects, 4-way bank spread) and lane 0 adds the box into the fp32 residual with
 // one TMA reduce-add; rows past M are dropped by TMA.  No residual read leaves the SM.  `row`
 // is clamped to a valid row for the scale / bias / gate reads (its values are discarded).
+// With wait = false the box is not reused by the caller, which waits for all its reduce-adds at
+// the end (several boxes in flight at once).
 __device__ __forceinline__ void epilogue_chunk_tma(const GemmEpi& e, const CUtensorMap* tmC, int row, int row0,
                                                    int col0, const uint32_t (&r)[32], const float* __restrict__ sa,
-                                                   const float* __restrict__ sw, uint8_t* box, int lane) {
+                                                   const float* __restrict__ sw, uint8_t* box, int lane,
+                                                   bool wait = true) {
   float v[32];
 #pragma unroll
   for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
@@ -123,7 +126,68 @@ __device__ __forceinline__ void epilogue_chunk_tma(const GemmEpi& e, const CUten
   if (lane == 0) {
     tma_reduce_add_2d(tmC, box, col0, row0);
     bulk_commit();
-    bulk_wait_read0();   // the box may be rewritten once TMA has read it
+    if (wait) bulk_wait_read0();   // the box may be rewritten once TMA has read it
+  }
+  __syncwarp();
+}
+
+// Bias / activation / e4m3 scales of one 32-column accumulator chunk (bf16 output modes).
+__device__ __forceinline__ void epi_math_bf16(const GemmEpi& e, int row, int frame, int col0, const uint32_t (&r)[32],
+                                              const float* __restrict__ sa, const float* __restrict__ sw,
+                                              float (&v)[32]) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+  if (sa) {
+    const float ra = __ldg(sa + row);
+    const float4* w4 = reinterpret_cast<const float4*>(sw + col0);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float4 w = __ldg(w4 + j);
+      v[4 * j + 0] *= ra * w.x; v[4 * j + 1] *= ra * w.y; v[4 * j + 2] *= ra * w.z; v[4 * j + 3] *= ra * w.w;
+    }
+  }
+  add_bias(e, frame, col0, v);
+  if (e.mode == EPI_GELU_BF16) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
+  } else if (e.mode == EPI_GELU_ERF_BF16) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = 0.5f * v[j] * (1.f + erff(v[j] * 0.7071067811865476f));
+  }
+}
+
+// bf16 output modes (EPI_BF16 / EPI_GELU_BF16 / EPI_GELU_ERF_BF16): NCH (1 or 2) accumulator
+// chunks of the warp's 32 rows become a bf16 box in shared memory (row l's 16-byte piece p at
+// position p ^ (l % 8)), then the warp stores the box row-contiguously: with 64 columns, four
+// whole 128-byte rows per instruction instead of 32 partial lines (one per thread's row).  `row`
+// is clamped for the scale / bias reads; rows >= M and columns >= N are not stored.  The output
+// segment (q / k / v of a fused projection) is that of colb: seg_w is a multiple of the tile width.
+template <int NCH>
+__device__ __forceinline__ void epilogue_bf16_box(const GemmEpi& e, int row, int row0, int colb, int M, int N,
+                                                  const uint32_t (*r)[32], const float* __restrict__ sa,
+                                                  const float* __restrict__ sw, uint8_t* box, int lane) {
+  const int frame = row / e.rows_per_frame;
+#pragma unroll
+  for (int cc = 0; cc < NCH; ++cc) {
+    float v[32];
+    epi_math_bf16(e, row, frame, min(colb + cc * 32, N - 32), r[cc], sa, sw, v);
+#pragma unroll
+    for (int pc = 0; pc < 4; ++pc)
+      *reinterpret_cast<uint4*>(box + lane * 128 + (((cc * 4 + pc) ^ (lane & 7)) << 4)) =
+          make_uint4(pack_bf16(v[8 * pc + 0], v[8 * pc + 1]), pack_bf16(v[8 * pc + 2], v[8 * pc + 3]),
+                     pack_bf16(v[8 * pc + 4], v[8 * pc + 5]), pack_bf16(v[8 * pc + 6], v[8 * pc + 7]));
+  }
+  __syncwarp();
+  constexpr int PPR = 4 * NCH;     // 16-byte pieces per row
+  constexpr int RPI = 32 / PPR;    // rows per instruction
+  const int seg = colb / e.seg_w, scol = colb - seg * e.seg_w;
+  __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(e.out[seg]);
+#pragma unroll
+  for (int it = 0; it < PPR; ++it) {
+    const int rr = it * RPI + lane / PPR, p = lane % PPR;
+    const uint4 u = *reinterpret_cast<const uint4*>(box + rr * 128 + ((p ^ (rr & 7)) << 4));
+    const int grow = row0 + rr;
+    if (grow < M && colb + p * 8 < N) *reinterpret_cast<uint4*>(out + (size_t)grow * e.ld_out + scol + p * 8) = u;
   }
   __syncwarp();
 }

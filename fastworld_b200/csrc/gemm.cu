@@ -9,8 +9,9 @@
 //               tcgen05.commit releases the smem stage and, per tile, signals the epilogue
 //   warps 2..9  epilogue (thread = output row, two warps per TMEM lane quarter splitting the
 //               tile's columns): all accumulator columns loaded with tcgen05.ld, TMEM released,
-//               then fused bias / GELU / gated fp32 residual update and direct vector stores;
-//               the residual rows are prefetched into L2 while the main loop still runs
+//               then fused bias / GELU / scales in registers; bf16 outputs go through a
+//               per-warp shared-memory box so that each store instruction writes whole
+//               128-byte rows, gated fp32 residual updates are TMA reduce-adds of such boxes
 // The TMEM accumulator is double-buffered (2 x BN columns) so the epilogue of tile i overlaps
 // the main loop of tile i + 1.  Tile order is M-fastest so consecutive CTAs share a weight
 // tile in L2.  M, N and K tails are zero-filled by TMA and masked in the epilogue.
@@ -164,6 +165,7 @@ __global__ void __launch_bounds__(320, 1)
     // the tile.  All of a thread's accumulator columns are loaded at once, the TMEM buffer is
     // released, and the bias / activation / residual math and the stores run from registers.
     constexpr int NC = BN / 64;                   // 32-column chunks per thread
+    static_assert(8 * NC * C::EPI_BOX <= C::STAGES * C::STAGE, "last-tile staging must fit in the pipeline stages");
     const int q = warp & 3, h = (warp - 2) >> 2;
     int acc = 0;
     uint32_t acc_phase = 0;
@@ -195,13 +197,28 @@ __global__ void __launch_bounds__(320, 1)
                                         r[2 * b + 1], box, lane);
         }
       } else if (args.epi.mode == EPI_RESID_TMA) {      // warp-collective: every lane takes part
-        uint8_t* box = smem + C::EPI_OFF + (warp - 2) * C::EPI_BOX;
+        // The CTA's last tile: every MMA has completed (tfull) and no load is pending, so the
+        // pipeline stages are idle and each warp stages all its chunks at once (NC boxes in
+        // flight, one wait at the end).  Earlier tiles overlap the next tile's main loop and
+        // reuse the warp's one box.
+        const bool last = t + (int)gridDim.x >= num_tiles;
 #pragma unroll
         for (int c = 0; c < NC; ++c) {
           const int col0 = colh + c * 32;
+          uint8_t* box = last ? smem + ((warp - 2) * NC + c) * C::EPI_BOX : smem + C::EPI_OFF + (warp - 2) * C::EPI_BOX;
           if (col0 < N)
             epilogue_chunk_tma(args.epi, &tmC, min(row, M - 1), mb * 128 + q * 32, col0, r[c],
-                               F8 ? args.sa : nullptr, args.sw, box, lane);
+                               F8 ? args.sa : nullptr, args.sw, box, lane, !last);
+        }
+      } else if (NC >= 2 && (args.epi.mode == EPI_BF16 || args.epi.mode == EPI_GELU_BF16 ||
+                             args.epi.mode == EPI_GELU_ERF_BF16)) {
+        uint8_t* box = smem + C::EPI_OFF + (warp - 2) * C::EPI_BOX;   // warp-collective
+#pragma unroll
+        for (int b = 0; b < NC / 2; ++b) {
+          const int colb = colh + b * 64;
+          if (colb < N)
+            epilogue_bf16_box<2>(args.epi, min(row, M - 1), mb * 128 + q * 32, colb, M, N, r + 2 * b,
+                                 F8 ? args.sa : nullptr, args.sw, box, lane);
         }
       } else if (row < M) {
 #pragma unroll
@@ -293,10 +310,11 @@ int gemm_bf16_launch(const CUtensorMap& tmA, const CUtensorMap& tmB, int bn, con
   const int tiles = ((a.M + 127) / 128) * ((a.N + bn - 1) / bn);
   int grid = ctas > 0 ? ctas : num_sms();
   if (grid > tiles) grid = tiles;
+  GemmArgs b = a;
   switch (bn) {
-    case 256: return a.sa ? launch_bn<256, true>(tmA, tmB, mc, a, s, grid) : launch_bn<256, false>(tmA, tmB, mc, a, s, grid);
-    case 128: return a.sa ? launch_bn<128, true>(tmA, tmB, mc, a, s, grid) : launch_bn<128, false>(tmA, tmB, mc, a, s, grid);
-    default: return a.sa ? launch_bn<64, true>(tmA, tmB, mc, a, s, grid) : launch_bn<64, false>(tmA, tmB, mc, a, s, grid);
+    case 256: return a.sa ? launch_bn<256, true>(tmA, tmB, mc, b, s, grid) : launch_bn<256, false>(tmA, tmB, mc, b, s, grid);
+    case 128: return a.sa ? launch_bn<128, true>(tmA, tmB, mc, b, s, grid) : launch_bn<128, false>(tmA, tmB, mc, b, s, grid);
+    default: return a.sa ? launch_bn<64, true>(tmA, tmB, mc, b, s, grid) : launch_bn<64, false>(tmA, tmB, mc, b, s, grid);
   }
 }
 
