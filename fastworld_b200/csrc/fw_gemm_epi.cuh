@@ -192,6 +192,63 @@ __device__ __forceinline__ void epilogue_bf16_box(const GemmEpi& e, int row, int
   __syncwarp();
 }
 
+// EPI_RESID_F32 (with or without a bf16 mirror): the warp's 32 rows x 32 columns of
+// gate * (acc + bias) go through a swizzled fp32 box; then each instruction updates four whole
+// 128-byte residual rows (8 lanes per row, 16 bytes each: coalesced read-modify-write, all eight
+// loads in flight before the adds) and writes the matching 64-byte pieces of the bf16 mirror.
+// `row` is clamped for the scale / bias / gate reads; rows >= M are not touched.
+__device__ __forceinline__ void epilogue_resid_box(const GemmEpi& e, int row, int row0, int col0, int M,
+                                                   const uint32_t (&r)[32], const float* __restrict__ sa,
+                                                   const float* __restrict__ sw, uint8_t* box, int lane) {
+  float v[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+  if (sa) {
+    const float ra = __ldg(sa + row);
+    const float4* w4 = reinterpret_cast<const float4*>(sw + col0);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float4 w = __ldg(w4 + j);
+      v[4 * j + 0] *= ra * w.x; v[4 * j + 1] *= ra * w.y; v[4 * j + 2] *= ra * w.z; v[4 * j + 3] *= ra * w.w;
+    }
+  }
+  const int frame = row / e.rows_per_frame;
+  add_bias(e, frame, col0, v);
+  if (e.gate) {
+    const float4* gp = reinterpret_cast<const float4*>(e.gate + (size_t)frame * e.gate_stride + col0);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float4 g = __ldg(gp + j);
+      v[4 * j + 0] *= g.x; v[4 * j + 1] *= g.y; v[4 * j + 2] *= g.z; v[4 * j + 3] *= g.w;
+    }
+  }
+#pragma unroll
+  for (int c = 0; c < 8; ++c)
+    *reinterpret_cast<float4*>(box + lane * 128 + ((c ^ (lane & 7)) << 4)) =
+        make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+  __syncwarp();
+  const int p = lane & 7, gcol = col0 + p * 4;
+  float4 x[8];
+#pragma unroll
+  for (int it = 0; it < 8; ++it) {
+    const int grow = row0 + it * 4 + (lane >> 3);
+    if (grow < M) x[it] = *reinterpret_cast<const float4*>(e.resid + (size_t)grow * e.ld_resid + gcol);
+  }
+#pragma unroll
+  for (int it = 0; it < 8; ++it) {
+    const int rr = it * 4 + (lane >> 3), grow = row0 + rr;
+    if (grow < M) {
+      const float4 u = *reinterpret_cast<const float4*>(box + rr * 128 + ((p ^ (rr & 7)) << 4));
+      x[it].x += u.x; x[it].y += u.y; x[it].z += u.z; x[it].w += u.w;
+      *reinterpret_cast<float4*>(e.resid + (size_t)grow * e.ld_resid + gcol) = x[it];
+      if (e.mirror)
+        *reinterpret_cast<uint2*>(e.mirror + (size_t)grow * e.ld_mirror + gcol) =
+            make_uint2(pack_bf16(x[it].x, x[it].y), pack_bf16(x[it].z, x[it].w));
+    }
+  }
+  __syncwarp();
+}
+
 // EPI_BF16_PUSH: 64 columns (two accumulator chunks) of the warp's 32 rows become a 32 x 128-byte
 // bf16 box in shared memory (16-byte piece p of row l at position p ^ (l % 8): conflict-free
 // writes by row, conflict-free reads by 8 lanes per row), then the warp stores the box

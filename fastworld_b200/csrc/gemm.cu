@@ -182,51 +182,53 @@ __global__ void __launch_bounds__(320, 1)
       if (!__all_sync(0xffffffffu, ok)) break;   // keep the warp converged for tcgen05.ld
       tc_fence_after();
       const uint32_t tb = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + h * (BN / 2));
-      uint32_t r[NC][32];
-#pragma unroll
-      for (int c = 0; c < NC; ++c) tmem_ld32(tb + (uint32_t)(c * 32), r[c]);
-      tmem_ld_wait();
-      tc_fence_before();
-      mbar_arrive(tempty + acc);                 // the accumulator buffer is free again
-      if (args.epi.mode == EPI_BF16_PUSH) {      // warp-collective: every lane takes part
-        uint8_t* box = smem + C::EPI_OFF + (warp - 2) * C::EPI_BOX;
-#pragma unroll
-        for (int b = 0; b < NC / 2; ++b) {
-          const int colb = colh + b * 64;
-          if (colb < N) epilogue_push64(args.epi, min(row, M - 1), mb * 128 + q * 32, colb, M, N, r[2 * b],
-                                        r[2 * b + 1], box, lane);
-        }
-      } else if (args.epi.mode == EPI_RESID_TMA) {      // warp-collective: every lane takes part
-        // The CTA's last tile: every MMA has completed (tfull) and no load is pending, so the
-        // pipeline stages are idle and each warp stages all its chunks at once (NC boxes in
-        // flight, one wait at the end).  Earlier tiles overlap the next tile's main loop and
-        // reuse the warp's one box.
-        const bool last = t + (int)gridDim.x >= num_tiles;
-#pragma unroll
-        for (int c = 0; c < NC; ++c) {
-          const int col0 = colh + c * 32;
-          uint8_t* box = last ? smem + ((warp - 2) * NC + c) * C::EPI_BOX : smem + C::EPI_OFF + (warp - 2) * C::EPI_BOX;
-          if (col0 < N)
-            epilogue_chunk_tma(args.epi, &tmC, min(row, M - 1), mb * 128 + q * 32, col0, r[c],
-                               F8 ? args.sa : nullptr, args.sw, box, lane, !last);
-        }
-      } else if (NC >= 2 && (args.epi.mode == EPI_BF16 || args.epi.mode == EPI_GELU_BF16 ||
-                             args.epi.mode == EPI_GELU_ERF_BF16)) {
-        uint8_t* box = smem + C::EPI_OFF + (warp - 2) * C::EPI_BOX;   // warp-collective
+      // Accumulator chunks are read from TMEM as each is needed (tcgen05.ld is warp-collective:
+      // every lane executes it) and the buffer is released after the last one: the next tile's
+      // main loop outlasts this epilogue, so holding TMEM costs nothing and frees the registers.
+      uint8_t* box = smem + C::EPI_OFF + (warp - 2) * C::EPI_BOX;
+      const int rowc = min(row, M - 1), row0 = mb * 128 + q * 32;
+      const float* sa = F8 ? args.sa : nullptr;
+      if (args.epi.mode == EPI_BF16_PUSH ||
+          (NC >= 2 && (args.epi.mode == EPI_BF16 || args.epi.mode == EPI_GELU_BF16 ||
+                       args.epi.mode == EPI_GELU_ERF_BF16))) {   // 64 columns per box
 #pragma unroll
         for (int b = 0; b < NC / 2; ++b) {
+          uint32_t r[2][32];
+          tmem_ld32(tb + (uint32_t)(b * 64), r[0]);
+          tmem_ld32(tb + (uint32_t)(b * 64 + 32), r[1]);
+          tmem_ld_wait();
           const int colb = colh + b * 64;
-          if (colb < N)
-            epilogue_bf16_box<2>(args.epi, min(row, M - 1), mb * 128 + q * 32, colb, M, N, r + 2 * b,
-                                 F8 ? args.sa : nullptr, args.sw, box, lane);
+          if (colb < N) {
+            if (args.epi.mode == EPI_BF16_PUSH)
+              epilogue_push64(args.epi, rowc, row0, colb, M, N, r[0], r[1], box, lane);
+            else
+              epilogue_bf16_box<2>(args.epi, rowc, row0, colb, M, N, r, sa, args.sw, box, lane);
+          }
         }
-      } else if (row < M) {
+      } else {   // 32 columns at a time
+        // EPI_RESID_TMA in the CTA's last tile: every MMA has completed (tfull) and no load is
+        // pending, so the pipeline stages are idle and each warp stages all its chunks at once
+        // (NC boxes in flight, one wait at the end).  Earlier tiles overlap the next tile's main
+        // loop and reuse the warp's one box.
+        const bool last = args.epi.mode == EPI_RESID_TMA && t + (int)gridDim.x >= num_tiles;
 #pragma unroll
         for (int c = 0; c < NC; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tb + (uint32_t)(c * 32), r);
+          tmem_ld_wait();
           const int col0 = colh + c * 32;
-          if (col0 < N) epilogue_chunk(args.epi, row, col0, r[c], F8 ? args.sa : nullptr, args.sw);
+          if (col0 >= N) continue;
+          if (args.epi.mode == EPI_RESID_TMA)
+            epilogue_chunk_tma(args.epi, &tmC, rowc, row0, col0, r, sa, args.sw,
+                               last ? smem + ((warp - 2) * NC + c) * C::EPI_BOX : box, lane, !last);
+          else if (args.epi.mode == EPI_RESID_F32)
+            epilogue_resid_box(args.epi, rowc, row0, col0, M, r, sa, args.sw, box, lane);
+          else if (row < M)
+            epilogue_chunk(args.epi, row, col0, r, sa, args.sw);
         }
       }
+      tc_fence_before();
+      mbar_arrive(tempty + acc);                 // the accumulator buffer is free again
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
