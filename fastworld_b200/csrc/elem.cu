@@ -7,7 +7,7 @@
 //   rms_rope_kernel      norm_q / norm_k (208-209, 189-190) fused with the fp64 complex RoPE
 //                        (_rope, 130-133; computed here in fp32 from an fp64-built table)
 //   rope_table_kernel    the per-chunk RoPE table fi (113-118) and action RoPE acos/asin (120)
-//   smallm_linear_kernel time_embedding / time_projection (199-200), keyboard_embed and
+//   smallm_linear(8)_kernel time_embedding / time_projection (199-200), keyboard_embed and
 //                        keyboard_attn_kv (165-168), the mouse-window part of mouse_mlp (150)
 //   patchify_kernel      cat([x, cc]) + Conv3d(k = s = (1,2,2)) operand layout (197-198)
 //   scheduler_kernel     unpatchify + _convert_flow_pred_to_x0 + add_noise (227-240)
@@ -572,17 +572,69 @@ __global__ void __launch_bounds__(256) smallm_linear_kernel(const Tx* __restrict
   }
 }
 
+// The same with 16-byte loads: each lane takes 8 consecutive k (one uint4 of weights, 8 inputs)
+// per step, so a warp reads 512 contiguous weight bytes per instruction.  K % 8 == 0 and 16-byte
+// aligned rows of W and x.
+template <typename Tx>
+__global__ void __launch_bounds__(256) smallm_linear8_kernel(const Tx* __restrict__ x, int ldx, int M,
+                                                             const __nv_bfloat16* __restrict__ W, int ldw,
+                                                             const __nv_bfloat16* __restrict__ bias, int N, int K,
+                                                             int act_in, int act_out, float* __restrict__ outf,
+                                                             __nv_bfloat16* __restrict__ outb, int ldo) {
+  pdl_trigger();
+  pdl_wait();
+  const int n = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (n >= N) return;
+  const uint4* wr = reinterpret_cast<const uint4*>(W + (size_t)n * ldw);
+  const float bn = bias ? __bfloat162float(bias[n]) : 0.f;
+  const int K8 = K >> 3;
+  for (int m = 0; m < M; ++m) {
+    const Tx* xr = x + (size_t)m * ldx;
+    float acc = 0.f;
+    for (int k8 = lane; k8 < K8; k8 += 32) {
+      const uint4 wu = __ldg(wr + k8);
+      float xv[8], wv[8];
+      load8(xr + k8 * 8, xv);
+      load8(reinterpret_cast<const __nv_bfloat16*>(&wu), wv);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float v = xv[i];
+        if (act_in == ACT_SILU) v = v / (1.f + __expf(-v));
+        acc += v * wv[i];
+      }
+    }
+    acc = warp_sum(acc) + bn;
+    if (act_out == ACT_SILU) acc = acc / (1.f + __expf(-acc));
+    else if (act_out == ACT_GELU_ERF) acc = 0.5f * acc * (1.f + erff(acc * 0.7071067811865476f));
+    if (lane == 0) {
+      if (outf) outf[(size_t)m * ldo + n] = acc;
+      if (outb) outb[(size_t)m * ldo + n] = __float2bfloat16(acc);
+    }
+  }
+}
+
+template <typename Tx>
+static int smallm_dispatch(const Tx* x, int ldx, int M, const __nv_bfloat16* W, int ldw, const __nv_bfloat16* b,
+                           int N, int K, int act_in, int act_out, float* outf, __nv_bfloat16* outb, int ldo,
+                           cudaStream_t s) {
+  auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  if (K % 8 == 0 && ldw % 8 == 0 && ldx % 8 == 0 && al16(W) && al16(x))
+    launch_k(smallm_linear8_kernel<Tx>, (N + 7) / 8, 256, 0, s, x, ldx, M, W, ldw, b, N, K, act_in, act_out, outf,
+             outb, ldo);
+  else
+    launch_k(smallm_linear_kernel<Tx>, (N + 7) / 8, 256, 0, s, x, ldx, M, W, ldw, b, N, K, act_in, act_out, outf,
+             outb, ldo);
+  return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
+}
+
 int smallm_linear_f32(const float* x, int ldx, int M, const __nv_bfloat16* W, int ldw, const __nv_bfloat16* b, int N,
                       int K, int act_in, int act_out, float* outf, __nv_bfloat16* outb, int ldo, cudaStream_t s) {
-  launch_k(smallm_linear_kernel<float>, (N + 7) / 8, 256, 0, s, x, ldx, M, W, ldw, b, N, K, act_in, act_out, outf, outb, ldo);
-  return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
+  return smallm_dispatch<float>(x, ldx, M, W, ldw, b, N, K, act_in, act_out, outf, outb, ldo, s);
 }
 int smallm_linear_bf16(const __nv_bfloat16* x, int ldx, int M, const __nv_bfloat16* W, int ldw,
                        const __nv_bfloat16* b, int N, int K, int act_in, int act_out, float* outf,
                        __nv_bfloat16* outb, int ldo, cudaStream_t s) {
-  launch_k(smallm_linear_kernel<__nv_bfloat16>, (N + 7) / 8, 256, 0, s, x, ldx, M, W, ldw, b, N, K, act_in, act_out, outf,
-                                                                   outb, ldo);
-  return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
+  return smallm_dispatch<__nv_bfloat16>(x, ldx, M, W, ldw, b, N, K, act_in, act_out, outf, outb, ldo, s);
 }
 
 // ------------------------------------------------------------------ time embedding helpers

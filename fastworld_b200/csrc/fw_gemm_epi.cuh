@@ -195,11 +195,19 @@ __device__ __forceinline__ void epilogue_bf16_box(const GemmEpi& e, int row, int
 // EPI_RESID_F32 (with or without a bf16 mirror): the warp's 32 rows x 32 columns of
 // gate * (acc + bias) go through a swizzled fp32 box; then each instruction updates four whole
 // 128-byte residual rows (8 lanes per row, 16 bytes each: coalesced read-modify-write, all eight
-// loads in flight before the adds) and writes the matching 64-byte pieces of the bf16 mirror.
+// loads issued before the epilogue math) and writes the matching 64-byte pieces of the bf16 mirror.
 // `row` is clamped for the scale / bias / gate reads; rows >= M are not touched.
 __device__ __forceinline__ void epilogue_resid_box(const GemmEpi& e, int row, int row0, int col0, int M,
                                                    const uint32_t (&r)[32], const float* __restrict__ sa,
                                                    const float* __restrict__ sw, uint8_t* box, int lane) {
+  // the residual loads go out first: their latency overlaps the scale / bias / gate math
+  const int p = lane & 7, gcol = col0 + p * 4;
+  float4 x[8];
+#pragma unroll
+  for (int it = 0; it < 8; ++it) {
+    const int grow = row0 + it * 4 + (lane >> 3);
+    if (grow < M) x[it] = *reinterpret_cast<const float4*>(e.resid + (size_t)grow * e.ld_resid + gcol);
+  }
   float v[32];
 #pragma unroll
   for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
@@ -227,13 +235,6 @@ __device__ __forceinline__ void epilogue_resid_box(const GemmEpi& e, int row, in
     *reinterpret_cast<float4*>(box + lane * 128 + ((c ^ (lane & 7)) << 4)) =
         make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
   __syncwarp();
-  const int p = lane & 7, gcol = col0 + p * 4;
-  float4 x[8];
-#pragma unroll
-  for (int it = 0; it < 8; ++it) {
-    const int grow = row0 + it * 4 + (lane >> 3);
-    if (grow < M) x[it] = *reinterpret_cast<const float4*>(e.resid + (size_t)grow * e.ld_resid + gcol);
-  }
 #pragma unroll
   for (int it = 0; it < 8; ++it) {
     const int rr = it * 4 + (lane >> 3), grow = row0 + rr;
