@@ -88,7 +88,8 @@ class B200StaticMG:
         packed = pack_weights(cfg, weights)
         self._ccfg = _lib.make_config(cfg, self.tp_size, self.tp_rank)
         h = ctypes.c_void_p()
-        check(lib().fw_create(ctypes.byref(self._ccfg), ctypes.byref(h)), "fw_create")
+        self._lib = lib()   # kept for __del__, which may run after module globals are cleared
+        check(self._lib.fw_create(ctypes.byref(self._ccfg), ctypes.byref(h)), "fw_create")
         self._h = h
         if self.tp_size > 1:
             self._tp_connect(tp_group)
@@ -183,9 +184,9 @@ class B200StaticMG:
             except Exception:
                 pass
         self._peer_maps = []
-        h = getattr(self, "_h", None)
-        if h is not None and h.value:
-            lib().fw_destroy(h)
+        h, L = getattr(self, "_h", None), getattr(self, "_lib", None)
+        if h is not None and h.value and L is not None:
+            L.fw_destroy(h)
             self._h = None
 
     # ------------------------------------------------------------------ images
