@@ -224,6 +224,10 @@ struct RmsPair {
   __nv_bfloat16* out[2];
   const float* ss = nullptr;
   float inv_d = 0.f;
+  // grouped (w_grp set): blockIdx.y = group g normalises x[0] + g * grp_stride into
+  // out[0] + g * grp_stride with weight w_grp[g]
+  const __nv_bfloat16* const* w_grp = nullptr;
+  long long grp_stride = 0;
 };
 
 template <int NG>
@@ -233,9 +237,13 @@ __global__ void __launch_bounds__(256) rms_rope_kernel(RmsPair pr, int ldx, int 
   pdl_wait();
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (row >= M) return;
-  const __nv_bfloat16* __restrict__ x = pr.x[blockIdx.y];
-  const __nv_bfloat16* __restrict__ w = pr.w[blockIdx.y];
-  __nv_bfloat16* __restrict__ out = pr.out[blockIdx.y];
+  // constant indices into the parameter struct (indexing it by blockIdx.y would copy it to
+  // local memory in every thread)
+  const bool y1 = blockIdx.y == 1;
+  const size_t goff = pr.w_grp ? (size_t)blockIdx.y * (size_t)pr.grp_stride : 0;
+  const __nv_bfloat16* __restrict__ x = pr.w_grp ? pr.x[0] + goff : (y1 ? pr.x[1] : pr.x[0]);
+  const __nv_bfloat16* __restrict__ w = pr.w_grp ? pr.w_grp[blockIdx.y] : (y1 ? pr.w[1] : pr.w[0]);
+  __nv_bfloat16* __restrict__ out = pr.w_grp ? pr.out[0] + goff : (y1 ? pr.out[1] : pr.out[0]);
   constexpr int D = 128 * NG;
   float v[NG][4];
   float q = 0.f;
@@ -278,9 +286,13 @@ __global__ void __launch_bounds__(256) rms_rope8_kernel(RmsPair pr, int ldx, int
   pdl_wait();
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (row >= M) return;
-  const __nv_bfloat16* __restrict__ x = pr.x[blockIdx.y];
-  const __nv_bfloat16* __restrict__ w = pr.w[blockIdx.y];
-  __nv_bfloat16* __restrict__ out = pr.out[blockIdx.y];
+  // constant indices into the parameter struct (indexing it by blockIdx.y would copy it to
+  // local memory in every thread)
+  const bool y1 = blockIdx.y == 1;
+  const size_t goff = pr.w_grp ? (size_t)blockIdx.y * (size_t)pr.grp_stride : 0;
+  const __nv_bfloat16* __restrict__ x = pr.w_grp ? pr.x[0] + goff : (y1 ? pr.x[1] : pr.x[0]);
+  const __nv_bfloat16* __restrict__ w = pr.w_grp ? pr.w_grp[blockIdx.y] : (y1 ? pr.w[1] : pr.w[0]);
+  __nv_bfloat16* __restrict__ out = pr.w_grp ? pr.out[0] + goff : (y1 ? pr.out[1] : pr.out[0]);
   constexpr int D = 256 * NG8;
   float v[NG8][8];
   float q = 0.f;
@@ -316,10 +328,10 @@ __global__ void __launch_bounds__(256) rms_rope8_kernel(RmsPair pr, int ldx, int
   }
 }
 
-static int rms_rope_launch(const RmsPair& pr, bool two, int ldx, int M, int D, float eps, const float2* rope, int hd,
+static int rms_rope_launch(const RmsPair& pr, int ny, int ldx, int M, int D, float eps, const float2* rope, int hd,
                            int ldo, cudaStream_t s) {
   if (D % 128 || ldx % 4 || ldo % 4 || (rope && (hd % 4 || D % hd))) return FW_ESHAPE;
-  const dim3 grid((M + 7) / 8, two ? 2 : 1), block(256);
+  const dim3 grid((M + 7) / 8, ny), block(256);
   if (D % 256 == 0 && ldx % 8 == 0 && ldo % 8 == 0 && (!rope || hd % 8 == 0)) {
     switch (D / 256) {
 #define FW_RMS8_CASE(n) \
@@ -346,7 +358,16 @@ int rms_rope2(const __nv_bfloat16* x, const __nv_bfloat16* w, __nv_bfloat16* out
               const __nv_bfloat16* w2, __nv_bfloat16* out2, int ldx, int M, int D, float eps, const float2* rope, int hd,
               int ldo, cudaStream_t s) {
   RmsPair pr{{x, x2}, {w, w2}, {out, out2}};
-  return rms_rope_launch(pr, x2 != nullptr, ldx, M, D, eps, rope, hd, ldo, s);
+  return rms_rope_launch(pr, x2 ? 2 : 1, ldx, M, D, eps, rope, hd, ldo, s);
+}
+
+int rms_grp(__nv_bfloat16* x, long long grp_stride, int groups, const __nv_bfloat16* const* w_grp, int ldx, int M,
+            int D, float eps, cudaStream_t s) {
+  if (!x || !w_grp || groups < 1 || groups > 65535 || grp_stride < 0) return FW_EINVAL;
+  RmsPair pr{{x, nullptr}, {nullptr, nullptr}, {x, nullptr}};
+  pr.w_grp = w_grp;
+  pr.grp_stride = grp_stride;
+  return rms_rope_launch(pr, groups, ldx, M, D, eps, nullptr, 128, ldx, s);
 }
 
 int rms_rope2_ss(const __nv_bfloat16* x, const __nv_bfloat16* w, __nv_bfloat16* out, const __nv_bfloat16* x2,
@@ -354,7 +375,7 @@ int rms_rope2_ss(const __nv_bfloat16* x, const __nv_bfloat16* w, __nv_bfloat16* 
                  float eps, const float2* rope, int hd, int ldo, cudaStream_t s) {
   if (!ss || d_full <= 0) return FW_EINVAL;
   RmsPair pr{{x, x2}, {w, w2}, {out, out2}, ss, 1.f / (float)d_full};
-  return rms_rope_launch(pr, x2 != nullptr, ldx, M, D, eps, rope, hd, ldo, s);
+  return rms_rope_launch(pr, x2 ? 2 : 1, ldx, M, D, eps, rope, hd, ldo, s);
 }
 
 // Per-row partial sums of squares of one or two bf16 tensors [M, D]: ss[row * 2 + t].  One
@@ -540,101 +561,152 @@ int rope_tables(const int* chunk, int F, int th, int tw, int hd, double theta, f
   return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
 }
 
+__device__ __forceinline__ void unpack8(const uint4& u, float (&v)[8]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = unpack_bf16(w[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
 // ------------------------------------------------------------------ small-M linear
 // out[m, n] = act_out(sum_k act_in(x[m, k]) W[n, k] + b[n]), one warp per output column n.
+// Rows are processed four at a time: each weight element is loaded once per four rows and the
+// four dot products are independent, so their loads and reductions overlap (M is small here:
+// 1 for the time embedding, 3 frames or 21 keyboard rows for the action module).
+__device__ __forceinline__ float act_apply(float v, int act) {
+  if (act == ACT_SILU) return v / (1.f + __expf(-v));
+  if (act == ACT_GELU_ERF) return 0.5f * v * (1.f + erff(v * 0.7071067811865476f));
+  return v;
+}
+__device__ __forceinline__ void smallm_store(float acc, float bn, int act_out, int m, int n, int lane,
+                                             float* __restrict__ outf, __nv_bfloat16* __restrict__ outb, int ldo) {
+  acc = act_apply(warp_sum(acc) + bn, act_out);
+  if (lane == 0) {
+    if (outf) outf[(size_t)m * ldo + n] = acc;
+    if (outb) outb[(size_t)m * ldo + n] = __float2bfloat16(acc);
+  }
+}
+
 template <typename Tx>
 __global__ void __launch_bounds__(256) smallm_linear_kernel(const Tx* __restrict__ x, int ldx, int M,
                                                             const __nv_bfloat16* __restrict__ W, int ldw,
                                                             const __nv_bfloat16* __restrict__ bias, int N, int K,
                                                             int act_in, int act_out, float* __restrict__ outf,
-                                                            __nv_bfloat16* __restrict__ outb, int ldo) {
+                                                            __nv_bfloat16* __restrict__ outb, int ldo, SmallmGrp g) {
   pdl_trigger();
   pdl_wait();
   const int n = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (n >= N) return;
+  if (g.w) {   // grouped launch
+    W = g.w[blockIdx.y];
+    bias = g.bias ? g.bias[blockIdx.y] : nullptr;
+    x += (size_t)blockIdx.y * (size_t)g.x_stride;
+    if (outf) outf += (size_t)blockIdx.y * (size_t)g.out_stride;
+    if (outb) outb += (size_t)blockIdx.y * (size_t)g.out_stride;
+  }
   const __nv_bfloat16* wr = W + (size_t)n * ldw;
   const float bn = bias ? __bfloat162float(bias[n]) : 0.f;
-  for (int m = 0; m < M; ++m) {
-    const Tx* xr = x + (size_t)m * ldx;
-    float acc = 0.f;
+  for (int m0 = 0; m0 < M; m0 += 4) {
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
     for (int k = lane; k < K; k += 32) {
-      float xv = (float)xr[k];
-      if (act_in == ACT_SILU) xv = xv / (1.f + __expf(-xv));
-      acc += xv * __bfloat162float(wr[k]);
+      const float wv = __bfloat162float(wr[k]);
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+        if (m0 + r < M) acc[r] += act_apply((float)x[(size_t)(m0 + r) * ldx + k], act_in) * wv;
     }
-    acc = warp_sum(acc) + bn;
-    if (act_out == ACT_SILU) acc = acc / (1.f + __expf(-acc));
-    else if (act_out == ACT_GELU_ERF) acc = 0.5f * acc * (1.f + erff(acc * 0.7071067811865476f));
-    if (lane == 0) {
-      if (outf) outf[(size_t)m * ldo + n] = acc;
-      if (outb) outb[(size_t)m * ldo + n] = __float2bfloat16(acc);
-    }
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+      if (m0 + r < M) smallm_store(acc[r], bn, act_out, m0 + r, n, lane, outf, outb, ldo);
   }
 }
 
-// The same with 16-byte loads: each lane takes 8 consecutive k (one uint4 of weights, 8 inputs)
-// per step, so a warp reads 512 contiguous weight bytes per instruction.  K % 8 == 0 and 16-byte
-// aligned rows of W and x.
-template <typename Tx>
-__global__ void __launch_bounds__(256) smallm_linear8_kernel(const Tx* __restrict__ x, int ldx, int M,
+// The same with 16-byte loads: each lane takes 8 consecutive k (one uint4 of weights, 8 inputs
+// per row) per step, so a warp reads 512 contiguous weight bytes per instruction; a lane keeps
+// four such weight loads in flight.  K % 8 == 0 and 16-byte aligned rows of W and x.
+template <typename Tx, int RB>   // RB rows per pass: 1 (M = 1, high occupancy) or 4
+__global__ void __launch_bounds__(256, RB == 1 ? 4 : 2) smallm_linear8_kernel(const Tx* __restrict__ x, int ldx, int M,
                                                              const __nv_bfloat16* __restrict__ W, int ldw,
                                                              const __nv_bfloat16* __restrict__ bias, int N, int K,
                                                              int act_in, int act_out, float* __restrict__ outf,
-                                                             __nv_bfloat16* __restrict__ outb, int ldo) {
+                                                             __nv_bfloat16* __restrict__ outb, int ldo, SmallmGrp g) {
   pdl_trigger();
   pdl_wait();
   const int n = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (n >= N) return;
+  if (g.w) {   // grouped launch
+    W = g.w[blockIdx.y];
+    bias = g.bias ? g.bias[blockIdx.y] : nullptr;
+    x += (size_t)blockIdx.y * (size_t)g.x_stride;
+    if (outf) outf += (size_t)blockIdx.y * (size_t)g.out_stride;
+    if (outb) outb += (size_t)blockIdx.y * (size_t)g.out_stride;
+  }
   const uint4* wr = reinterpret_cast<const uint4*>(W + (size_t)n * ldw);
   const float bn = bias ? __bfloat162float(bias[n]) : 0.f;
   const int K8 = K >> 3;
-  for (int m = 0; m < M; ++m) {
-    const Tx* xr = x + (size_t)m * ldx;
-    float acc = 0.f;
-    for (int k8 = lane; k8 < K8; k8 += 32) {
-      const uint4 wu = __ldg(wr + k8);
-      float xv[8], wv[8];
-      load8(xr + k8 * 8, xv);
-      load8(reinterpret_cast<const __nv_bfloat16*>(&wu), wv);
+  for (int m0 = 0; m0 < M; m0 += RB) {
+    float acc[RB];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        float v = xv[i];
-        if (act_in == ACT_SILU) v = v / (1.f + __expf(-v));
-        acc += v * wv[i];
+    for (int r = 0; r < RB; ++r) acc[r] = 0.f;
+    for (int kb = lane; kb < K8; kb += 128) {   // four weight vectors in flight per lane
+      uint4 wq[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) wq[u] = kb + 32 * u < K8 ? __ldg(wr + kb + 32 * u) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int k8 = kb + 32 * u;
+        float wv[8];
+        unpack8(wq[u], wv);
+#pragma unroll
+        for (int r = 0; r < RB; ++r) {
+          if (k8 < K8 && m0 + r < M) {
+            float xv[8];
+            load8(x + (size_t)(m0 + r) * ldx + k8 * 8, xv);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[r] += act_apply(xv[i], act_in) * wv[i];
+          }
+        }
       }
     }
-    acc = warp_sum(acc) + bn;
-    if (act_out == ACT_SILU) acc = acc / (1.f + __expf(-acc));
-    else if (act_out == ACT_GELU_ERF) acc = 0.5f * acc * (1.f + erff(acc * 0.7071067811865476f));
-    if (lane == 0) {
-      if (outf) outf[(size_t)m * ldo + n] = acc;
-      if (outb) outb[(size_t)m * ldo + n] = __float2bfloat16(acc);
-    }
+#pragma unroll
+    for (int r = 0; r < RB; ++r)
+      if (m0 + r < M) smallm_store(acc[r], bn, act_out, m0 + r, n, lane, outf, outb, ldo);
   }
 }
 
 template <typename Tx>
 static int smallm_dispatch(const Tx* x, int ldx, int M, const __nv_bfloat16* W, int ldw, const __nv_bfloat16* b,
                            int N, int K, int act_in, int act_out, float* outf, __nv_bfloat16* outb, int ldo,
-                           cudaStream_t s) {
+                           cudaStream_t s, const SmallmGrp* grp) {
   auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
-  if (K % 8 == 0 && ldw % 8 == 0 && ldx % 8 == 0 && al16(W) && al16(x))
-    launch_k(smallm_linear8_kernel<Tx>, (N + 7) / 8, 256, 0, s, x, ldx, M, W, ldw, b, N, K, act_in, act_out, outf,
-             outb, ldo);
+  const SmallmGrp g = grp ? *grp : SmallmGrp{};
+  if (g.w && (g.groups < 1 || g.groups > 65535 || g.x_stride < 0 || g.out_stride < 0)) return FW_EINVAL;
+  const bool vec = K % 8 == 0 && ldw % 8 == 0 && ldx % 8 == 0 && al16(x) && (g.w ? g.aligned : al16(W)) &&
+                   (g.x_stride % 8 == 0);
+  const dim3 grid((N + 7) / 8, g.w ? g.groups : 1);
+  if (vec && M == 1)
+    launch_k(smallm_linear8_kernel<Tx, 1>, grid, 256, 0, s, x, ldx, M, W, ldw, b, N, K, act_in, act_out, outf, outb,
+             ldo, g);
+  else if (vec)
+    launch_k(smallm_linear8_kernel<Tx, 4>, grid, 256, 0, s, x, ldx, M, W, ldw, b, N, K, act_in, act_out, outf, outb,
+             ldo, g);
   else
-    launch_k(smallm_linear_kernel<Tx>, (N + 7) / 8, 256, 0, s, x, ldx, M, W, ldw, b, N, K, act_in, act_out, outf,
-             outb, ldo);
+    launch_k(smallm_linear_kernel<Tx>, grid, 256, 0, s, x, ldx, M, W, ldw, b, N, K, act_in, act_out, outf, outb,
+             ldo, g);
   return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
 }
 
 int smallm_linear_f32(const float* x, int ldx, int M, const __nv_bfloat16* W, int ldw, const __nv_bfloat16* b, int N,
-                      int K, int act_in, int act_out, float* outf, __nv_bfloat16* outb, int ldo, cudaStream_t s) {
-  return smallm_dispatch<float>(x, ldx, M, W, ldw, b, N, K, act_in, act_out, outf, outb, ldo, s);
+                      int K, int act_in, int act_out, float* outf, __nv_bfloat16* outb, int ldo, cudaStream_t s,
+                      const SmallmGrp* grp) {
+  return smallm_dispatch<float>(x, ldx, M, W, ldw, b, N, K, act_in, act_out, outf, outb, ldo, s, grp);
 }
 int smallm_linear_bf16(const __nv_bfloat16* x, int ldx, int M, const __nv_bfloat16* W, int ldw,
                        const __nv_bfloat16* b, int N, int K, int act_in, int act_out, float* outf,
-                       __nv_bfloat16* outb, int ldo, cudaStream_t s) {
-  return smallm_dispatch<__nv_bfloat16>(x, ldx, M, W, ldw, b, N, K, act_in, act_out, outf, outb, ldo, s);
+                       __nv_bfloat16* outb, int ldo, cudaStream_t s, const SmallmGrp* grp) {
+  return smallm_dispatch<__nv_bfloat16>(x, ldx, M, W, ldw, b, N, K, act_in, act_out, outf, outb, ldo, s, grp);
 }
 
 // ------------------------------------------------------------------ time embedding helpers
@@ -755,15 +827,6 @@ __device__ __forceinline__ float group8_sum(float v) {
   v += __shfl_xor_sync(0xffffffffu, v, 1);
   return v;
 }
-__device__ __forceinline__ void unpack8(const uint4& u, float (&v)[8]) {
-  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float2 f = unpack_bf16(w[i]);
-    v[2 * i] = f.x;
-    v[2 * i + 1] = f.y;
-  }
-}
 __device__ __forceinline__ uint4 pack8(const float (&v)[8]) {
   return make_uint4(pack_bf16(v[0], v[1]), pack_bf16(v[2], v[3]), pack_bf16(v[4], v[5]), pack_bf16(v[6], v[7]));
 }
@@ -878,15 +941,22 @@ int mouse_attn(const __nv_bfloat16* qkv, const __nv_bfloat16* wq, const __nv_bfl
 }
 
 // Keyboard K/V of one block: kv [F, 2A] fp32 -> K = RoPE(RMSNorm(k) * wk) and V, bf16 [F, A].
+// blockIdx.y = group (action layer) when wk_grp is set: kv, kout and vout advance by one layer.
 __global__ void kb_kv_kernel(const float* __restrict__ kv, const __nv_bfloat16* __restrict__ wk,
-                             const float* __restrict__ acos_, const float* __restrict__ asin_,
-                             __nv_bfloat16* __restrict__ kout, __nv_bfloat16* __restrict__ vout, int F, int AH,
-                             float eps) {
+                             const __nv_bfloat16* const* __restrict__ wk_grp, const float* __restrict__ acos_,
+                             const float* __restrict__ asin_, __nv_bfloat16* __restrict__ kout,
+                             __nv_bfloat16* __restrict__ vout, int F, int AH, float eps) {
   pdl_trigger();
   pdl_wait();
   const int wid = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (wid >= F * AH) return;
   const int f = wid / AH, h = wid % AH, A = AH * 64, d = 2 * lane;
+  if (wk_grp) {
+    wk = wk_grp[blockIdx.y];
+    kv += (size_t)blockIdx.y * F * 2 * A;
+    kout += (size_t)blockIdx.y * F * A;
+    vout += (size_t)blockIdx.y * F * A;
+  }
   const float2 w = ld2(wk + d);
   const float* r = kv + (size_t)f * 2 * A + h * 64 + d;
   const float2 k = norm_rope64(make_float2(r[0], r[1]), w.x, w.y, acos_[f * 64 + d], asin_[f * 64 + d], eps);
@@ -895,7 +965,15 @@ __global__ void kb_kv_kernel(const float* __restrict__ kv, const __nv_bfloat16* 
 }
 int kb_kv(const float* kv, const __nv_bfloat16* wk, const float* acos_, const float* asin_, __nv_bfloat16* kout,
           __nv_bfloat16* vout, int F, int AH, float eps, cudaStream_t s) {
-  launch_k(kb_kv_kernel, (F * AH + 3) / 4, 128, 0, s, kv, wk, acos_, asin_, kout, vout, F, AH, eps);
+  launch_k(kb_kv_kernel, (F * AH + 3) / 4, 128, 0, s, kv, wk, (const __nv_bfloat16* const*)nullptr, acos_, asin_,
+           kout, vout, F, AH, eps);
+  return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
+}
+int kb_kv_grp(const float* kv, const __nv_bfloat16* const* wk_grp, int groups, const float* acos_,
+              const float* asin_, __nv_bfloat16* kout, __nv_bfloat16* vout, int F, int AH, float eps, cudaStream_t s) {
+  if (!wk_grp || groups < 1 || groups > 65535) return FW_EINVAL;
+  launch_k(kb_kv_kernel, dim3((F * AH + 3) / 4, groups), 128, 0, s, kv, (const __nv_bfloat16*)nullptr, wk_grp,
+           acos_, asin_, kout, vout, F, AH, eps);
   return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
 }
 

@@ -86,6 +86,14 @@ struct fw_handle {
   int* status;
   std::vector<fw::Layer> layers;
   fw::GemmOp patch, head, fc1, fc2;
+  // every layer's cross-attention K/V projection as one grouped launch, and their K norms as one
+  // launch (tp 1); per-layer tensor maps and vector pointers live in the workspace ("ctx.grp")
+  fw::GemmOp cakv_all;
+  bool ctx_grouped = false;
+  const __nv_bfloat16* const* nk_grp = nullptr;
+  // the action blocks' keyboard chains as four grouped launches (pointer arrays in "act.grp")
+  bool kb_grouped = false;
+  const __nv_bfloat16* const* kb_grp = nullptr;
 };
 
 namespace fw {
@@ -273,9 +281,13 @@ static int register_tensors(fw_handle* h) {
   ws_add(h, "ctx_o", (size_t)h->Ctx * D * bf);
   ws_add(h, "ctx", (size_t)h->Ctx * D * bf);
   ws_add(h, "ckv", (size_t)c.layers * 2 * h->Ctx * Dl * bf);
-  ws_add(h, "ke1", (size_t)h->KC * h->Kh * f4);
-  ws_add(h, "ke", (size_t)h->KC * h->Kh * f4);
-  ws_add(h, "kbkv", (size_t)h->F * 2 * A * f4);
+  // keyboard embedding / K-V scratch, one slice per action block (the prologue runs all blocks'
+  // keyboard chains together)
+  const size_t nAs = h->nA ? h->nA : 1;
+  ws_add(h, "ke1", nAs * h->KC * h->Kh * f4);
+  ws_add(h, "ke", nAs * h->KC * h->Kh * f4);
+  ws_add(h, "kbkv", nAs * h->F * 2 * A * f4);
+  ws_add(h, "act.grp", nAs * 7 * sizeof(void*));   // per action block: kbe1.w/b, kbe2.w/b, kbkv.w/b, kkn.w
   ws_add(h, "kbK", (size_t)(h->nA ? h->nA : 1) * h->F * A * bf);
   ws_add(h, "kbV", (size_t)(h->nA ? h->nA : 1) * h->F * A * bf);
   ws_add(h, "fbias", (size_t)h->F * h->Mh * f4);
@@ -305,6 +317,9 @@ static int register_tensors(fw_handle* h) {
     // partials pushed by the other ranks' GEMMs: 2 parities x tp slots x ceil(L / tp) rows
     ws_add(h, "tp.recv", (size_t)2 * h->tp * ((L + h->tp - 1) / h->tp) * D * bf);
   }
+  // per-layer tensor maps (128 B each), bias and K-norm weight pointers for the grouped
+  // cross-attention K/V projection
+  ws_add(h, "ctx.grp", (size_t)c.layers * (sizeof(CUtensorMap) + 2 * sizeof(void*)));
   h->ws_bytes = (h->ws_bytes + 1023) & ~(size_t)1023;
   add_tensor(h, "workspace", FW_KIND_WORKSPACE, FW_U8, {(int64_t)h->ws_bytes});
   return 0;
@@ -634,6 +649,54 @@ static int finalize(fw_handle* h) {
     }
     if (cudaDeviceSynchronize() != cudaSuccess) return FW_ECUDA;
   }
+  if (!tp) {   // the grouped cross-attention K/V projection (all layers in one launch)
+    const int nl = h->cfg.layers;
+    std::vector<CUtensorMap> maps(nl);
+    std::vector<const void*> ptrs(2 * (size_t)nl);
+    bool ok = true;
+    for (int i = 0; i < nl; ++i) {
+      const GemmOp& op = h->layers[i].cakv;
+      ok = ok && !op.pair && op.bn == h->layers[0].cakv.bn;
+      maps[i] = op.b;
+      ptrs[i] = op.args.epi.bias;
+      ptrs[nl + i] = W(h, "b" + std::to_string(i) + ".ca.nk.w");
+    }
+    if (ok) {
+      uint8_t* g = reinterpret_cast<uint8_t*>(WS("ctx.grp"));
+      if (cudaMemcpy(g, maps.data(), sizeof(CUtensorMap) * nl, cudaMemcpyHostToDevice) != cudaSuccess ||
+          cudaMemcpy(g + sizeof(CUtensorMap) * nl, ptrs.data(), sizeof(void*) * 2 * nl, cudaMemcpyHostToDevice) !=
+              cudaSuccess)
+        return FW_ECUDA;
+      h->cakv_all = h->layers[0].cakv;
+      GemmArgs& a = h->cakv_all.args;
+      a.groups = nl;
+      a.tmB_grp = reinterpret_cast<const CUtensorMap*>(g);
+      a.bias_grp = reinterpret_cast<const __nv_bfloat16* const*>(g + sizeof(CUtensorMap) * nl);
+      a.out_grp_stride = (long long)2 * Ctx * Dl;
+      h->nk_grp = reinterpret_cast<const __nv_bfloat16* const*>(g + sizeof(CUtensorMap) * nl + sizeof(void*) * nl);
+      FW_TRY(gemm_check(a, h->cakv_all.bn));
+      h->ctx_grouped = true;
+    }
+  }
+  if (h->nA > 0) {   // keyboard chains of every action block, in action-block order
+    std::vector<const void*> ptrs(7 * (size_t)h->nA, nullptr);
+    bool aligned = true;
+    for (int i = 0; i < h->cfg.layers; ++i) {
+      const int a = h->layers[i].act;
+      if (a < 0) continue;
+      const std::string p = "b" + std::to_string(i) + ".am.";
+      const char* names[7] = {"kbe1.w", "kbe1.b", "kbe2.w", "kbe2.b", "kbkv.w", "kbkv.b", "kkn.w"};
+      for (int k = 0; k < 7; ++k) {
+        ptrs[(size_t)k * h->nA + a] = W(h, p + names[k]);
+        if (k == 2 || k == 4) aligned = aligned && (reinterpret_cast<uintptr_t>(ptrs[(size_t)k * h->nA + a]) & 15u) == 0;
+      }
+    }
+    void* g = WS("act.grp");
+    if (cudaMemcpy(g, ptrs.data(), ptrs.size() * sizeof(void*), cudaMemcpyHostToDevice) != cudaSuccess)
+      return FW_ECUDA;
+    h->kb_grp = reinterpret_cast<const __nv_bfloat16* const*>(g);
+    h->kb_grouped = aligned;
+  }
   h->finalized = true;
   return 0;
 }
@@ -652,11 +715,30 @@ static int prologue(fw_handle* h, cudaStream_t s) {
   FW_TRY(ln_bf16(h->ctx_o, D, Ctx, D, c.eps_ln, nullptr, nullptr, W(h, "img.ln1.w"), W(h, "img.ln1.b"), h->ctx, D, s));
   const int Dl = h->Dl;
   if (h->hc > 1) FW_TRY(hist_meta(P<int>(h, "chunk"), h->hc, h->L, h->consts + 6, s));
-  for (int i = 0; i < c.layers; ++i) {
-    const std::string p = "b" + std::to_string(i) + ".";
-    __nv_bfloat16* ck = h->ckv + (size_t)i * 2 * Ctx * Dl;
-    FW_TRY(run(h->layers[i].cakv, s));
-    FW_TRY(rms_norm_op(h, ck, nullptr, W(h, p + "ca.nk.w"), nullptr, Ctx, nullptr, s));
+  if (h->ctx_grouped) {   // all layers' K/V projections, then all their K norms: two launches
+    FW_TRY(run(h->cakv_all, s));
+    FW_TRY(rms_grp(h->ckv, (long long)2 * Ctx * Dl, c.layers, h->nk_grp, Dl, Ctx, Dl, c.eps, s));
+  } else {
+    for (int i = 0; i < c.layers; ++i) {
+      const std::string p = "b" + std::to_string(i) + ".";
+      __nv_bfloat16* ck = h->ckv + (size_t)i * 2 * Ctx * Dl;
+      FW_TRY(run(h->layers[i].cakv, s));
+      FW_TRY(rms_norm_op(h, ck, nullptr, W(h, p + "ca.nk.w"), nullptr, Ctx, nullptr, s));
+    }
+  }
+  if (h->kb_grouped) {   // every action block's keyboard chain in four launches (blockIdx.y = block)
+    const int A = h->A, Kh = h->Kh, nA = h->nA;
+    const __nv_bfloat16* const* g = h->kb_grp;   // device array: offsets only on the host
+    SmallmGrp g1{g + 0 * nA, g + 1 * nA, 0, (long long)h->KC * Kh, nA, true};
+    SmallmGrp g2{g + 2 * nA, g + 3 * nA, (long long)h->KC * Kh, (long long)h->KC * Kh, nA, true};
+    SmallmGrp g3{g + 4 * nA, g + 5 * nA, (long long)h->KC * Kh, (long long)h->F * 2 * A, nA, true};
+    FW_TRY(smallm_linear_bf16(P<__nv_bfloat16>(h, "kc"), c.keyboard_dim, h->KC, nullptr, c.keyboard_dim, nullptr, Kh,
+                              c.keyboard_dim, ACT_NONE, ACT_SILU, h->ke1, nullptr, Kh, s, &g1));
+    FW_TRY(smallm_linear_f32(h->ke1, Kh, h->KC, nullptr, Kh, nullptr, Kh, Kh, ACT_NONE, ACT_NONE, h->ke, nullptr, Kh,
+                             s, &g2));
+    FW_TRY(smallm_linear_f32(h->ke, c.time_ratio * Kh, h->F, nullptr, Kh * h->PAD, nullptr, 2 * A, Kh * h->PAD,
+                             ACT_NONE, ACT_NONE, h->kbkv, nullptr, 2 * A, s, &g3));
+    return kb_kv_grp(h->kbkv, g + 6 * nA, nA, h->acos_, h->asin_, h->kbK, h->kbV, h->F, h->AH, c.eps, s);
   }
   for (int i = 0; i < c.layers; ++i) {
     const Layer& ly = h->layers[i];

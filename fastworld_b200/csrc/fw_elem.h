@@ -20,6 +20,10 @@ int quant_rows(const __nv_bfloat16* x, int ldx, int M, int K, uint8_t* q, int ld
 int rms_rope(const __nv_bfloat16* x, int ldx, int M, int D, float eps, const __nv_bfloat16* w, const float2* rope,
              int hd, __nv_bfloat16* out, int ldo, cudaStream_t s);
 // Two tensors of the same shape in one launch (x2 may be null).
+// In-place RMSNorm (no RoPE) of `groups` row blocks: block g is x + g * grp_stride ([M, D], row
+// stride ldx) with weight w_grp[g] (a device array of pointers); one launch.
+int rms_grp(__nv_bfloat16* x, long long grp_stride, int groups, const __nv_bfloat16* const* w_grp, int ldx, int M,
+            int D, float eps, cudaStream_t s);
 int rms_rope2(const __nv_bfloat16* x, const __nv_bfloat16* w, __nv_bfloat16* out, const __nv_bfloat16* x2,
               const __nv_bfloat16* w2, __nv_bfloat16* out2, int ldx, int M, int D, float eps, const float2* rope, int hd,
               int ldo, cudaStream_t s);
@@ -40,11 +44,23 @@ int slot_copy(void* dst_base, size_t slot_bytes, const int* chunk, int window, c
               cudaStream_t s);
 int rope_tables(const int* chunk, int F, int th, int tw, int hd, double theta, float2* table, int act_hd,
                 float* act_cos, float* act_sin, cudaStream_t s);
+// Grouped small-M linears (one launch, blockIdx.y = group g): W = w[g], bias = bias[g] (device
+// arrays of pointers; bias may be null), x and the outputs advanced by g * x_stride and
+// g * out_stride elements.  Every w[g] must be 16-byte aligned with ldw % 8 == 0 for the
+// vectorised path (the caller checks; `aligned`).
+struct SmallmGrp {
+  const __nv_bfloat16* const* w = nullptr;
+  const __nv_bfloat16* const* bias = nullptr;
+  long long x_stride = 0, out_stride = 0;
+  int groups = 1;
+  bool aligned = false;
+};
 int smallm_linear_f32(const float* x, int ldx, int M, const __nv_bfloat16* W, int ldw, const __nv_bfloat16* b, int N,
-                      int K, int act_in, int act_out, float* outf, __nv_bfloat16* outb, int ldo, cudaStream_t s);
+                      int K, int act_in, int act_out, float* outf, __nv_bfloat16* outb, int ldo, cudaStream_t s,
+                      const SmallmGrp* grp = nullptr);
 int smallm_linear_bf16(const __nv_bfloat16* x, int ldx, int M, const __nv_bfloat16* W, int ldw,
                        const __nv_bfloat16* b, int N, int K, int act_in, int act_out, float* outf,
-                       __nv_bfloat16* outb, int ldo, cudaStream_t s);
+                       __nv_bfloat16* outb, int ldo, cudaStream_t s, const SmallmGrp* grp = nullptr);
 int sinusoid(double t, int dim, float* out, cudaStream_t s);
 int modulation(const __nv_bfloat16* mods, const float* e0, int layers, int D, float* ee, const __nv_bfloat16* hmod,
                const float* e, float* head, cudaStream_t s);
@@ -58,6 +74,10 @@ int mouse_attn(const __nv_bfloat16* qkv, const __nv_bfloat16* wq, const __nv_bfl
                int S, int F, int AH, float eps, cudaStream_t s);
 int kb_kv(const float* kv, const __nv_bfloat16* wk, const float* acos_, const float* asin_, __nv_bfloat16* kout,
           __nv_bfloat16* vout, int F, int AH, float eps, cudaStream_t s);
+// kb_kv for `groups` action layers in one launch: layer g reads kv + g * F * 2A with weight
+// wk_grp[g] and writes kout / vout + g * F * A.
+int kb_kv_grp(const float* kv, const __nv_bfloat16* const* wk_grp, int groups, const float* acos_,
+              const float* asin_, __nv_bfloat16* kout, __nv_bfloat16* vout, int F, int AH, float eps, cudaStream_t s);
 int kb_attn(const __nv_bfloat16* mq, const __nv_bfloat16* wq, const float* acos_, const float* asin_,
             const __nv_bfloat16* kh, const __nv_bfloat16* vh, const __nv_bfloat16* kc, const __nv_bfloat16* vc,
             int first, __nv_bfloat16* out, int L, int S, int F, int AH, float eps, cudaStream_t s);

@@ -7,9 +7,11 @@
 
 namespace fw {
 
-__device__ __forceinline__ void add_bias(const GemmEpi& e, int frame, int col0, float (&v)[32]) {
-  if (e.bias) {
-    const uint4* bp = reinterpret_cast<const uint4*>(e.bias + col0);
+// bias[col0 .. col0 + 32) (bf16; null = none) and the per-frame fp32 bias of GemmEpi.
+__device__ __forceinline__ void add_bias(const GemmEpi& e, const __nv_bfloat16* bias, int frame, int col0,
+                                         float (&v)[32]) {
+  if (bias) {
+    const uint4* bp = reinterpret_cast<const uint4*>(bias + col0);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       uint4 u = __ldg(bp + j);
@@ -51,7 +53,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmEpi& e, int row, int co
     }
   }
   const int frame = row / e.rows_per_frame;
-  add_bias(e, frame, col0, v);
+  add_bias(e, e.bias, frame, col0, v);
   if (e.mode == EPI_BF16 || e.mode == EPI_GELU_BF16 || e.mode == EPI_GELU_ERF_BF16) {
     if (e.mode == EPI_GELU_BF16) {
 #pragma unroll
@@ -108,7 +110,7 @@ __device__ __forceinline__ void epilogue_chunk_tma(const GemmEpi& e, const CUten
     }
   }
   const int frame = row / e.rows_per_frame;
-  add_bias(e, frame, col0, v);
+  add_bias(e, e.bias, frame, col0, v);
   if (e.gate) {
     const float4* gp = reinterpret_cast<const float4*>(e.gate + (size_t)frame * e.gate_stride + col0);
 #pragma unroll
@@ -132,7 +134,8 @@ __device__ __forceinline__ void epilogue_chunk_tma(const GemmEpi& e, const CUten
 }
 
 // Bias / activation / e4m3 scales of one 32-column accumulator chunk (bf16 output modes).
-__device__ __forceinline__ void epi_math_bf16(const GemmEpi& e, int row, int frame, int col0, const uint32_t (&r)[32],
+__device__ __forceinline__ void epi_math_bf16(const GemmEpi& e, const __nv_bfloat16* bias, int row, int frame,
+                                              int col0, const uint32_t (&r)[32],
                                               const float* __restrict__ sa, const float* __restrict__ sw,
                                               float (&v)[32]) {
 #pragma unroll
@@ -146,7 +149,7 @@ __device__ __forceinline__ void epi_math_bf16(const GemmEpi& e, int row, int fra
       v[4 * j + 0] *= ra * w.x; v[4 * j + 1] *= ra * w.y; v[4 * j + 2] *= ra * w.z; v[4 * j + 3] *= ra * w.w;
     }
   }
-  add_bias(e, frame, col0, v);
+  add_bias(e, bias, frame, col0, v);
   if (e.mode == EPI_GELU_BF16) {
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
@@ -162,15 +165,19 @@ __device__ __forceinline__ void epi_math_bf16(const GemmEpi& e, int row, int fra
 // whole 128-byte rows per instruction instead of 32 partial lines (one per thread's row).  `row`
 // is clamped for the scale / bias reads; rows >= M and columns >= N are not stored.  The output
 // segment (q / k / v of a fused projection) is that of colb: seg_w is a multiple of the tile width.
+//
+// bias / out_off: the group's bias vector and the element offset added to the output segments
+// (a grouped launch); e.bias and 0 otherwise.
 template <int NCH>
-__device__ __forceinline__ void epilogue_bf16_box(const GemmEpi& e, int row, int row0, int colb, int M, int N,
+__device__ __forceinline__ void epilogue_bf16_box(const GemmEpi& e, const __nv_bfloat16* bias, size_t out_off,
+                                                  int row, int row0, int colb, int M, int N,
                                                   const uint32_t (*r)[32], const float* __restrict__ sa,
                                                   const float* __restrict__ sw, uint8_t* box, int lane) {
   const int frame = row / e.rows_per_frame;
 #pragma unroll
   for (int cc = 0; cc < NCH; ++cc) {
     float v[32];
-    epi_math_bf16(e, row, frame, min(colb + cc * 32, N - 32), r[cc], sa, sw, v);
+    epi_math_bf16(e, bias, row, frame, min(colb + cc * 32, N - 32), r[cc], sa, sw, v);
 #pragma unroll
     for (int pc = 0; pc < 4; ++pc)
       *reinterpret_cast<uint4*>(box + lane * 128 + (((cc * 4 + pc) ^ (lane & 7)) << 4)) =
@@ -181,7 +188,7 @@ __device__ __forceinline__ void epilogue_bf16_box(const GemmEpi& e, int row, int
   constexpr int PPR = 4 * NCH;     // 16-byte pieces per row
   constexpr int RPI = 32 / PPR;    // rows per instruction
   const int seg = colb / e.seg_w, scol = colb - seg * e.seg_w;
-  __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(e.out[seg]);
+  __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(e.out[seg]) + out_off;
 #pragma unroll
   for (int it = 0; it < PPR; ++it) {
     const int rr = it * RPI + lane / PPR, p = lane % PPR;
@@ -221,7 +228,7 @@ __device__ __forceinline__ void epilogue_resid_box(const GemmEpi& e, int row, in
     }
   }
   const int frame = row / e.rows_per_frame;
-  add_bias(e, frame, col0, v);
+  add_bias(e, e.bias, frame, col0, v);
   if (e.gate) {
     const float4* gp = reinterpret_cast<const float4*>(e.gate + (size_t)frame * e.gate_stride + col0);
 #pragma unroll
@@ -267,7 +274,7 @@ __device__ __forceinline__ void epilogue_push64(const GemmEpi& e, int row, int r
     const uint32_t (&r)[32] = cc ? r1 : r0;
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-    if (colb + cc * 32 < N) add_bias(e, frame, colb + cc * 32, v);
+    if (colb + cc * 32 < N) add_bias(e, e.bias, frame, colb + cc * 32, v);
 #pragma unroll
     for (int pc = 0; pc < 4; ++pc) {
       const int piece = cc * 4 + pc;

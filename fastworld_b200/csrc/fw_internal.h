@@ -93,6 +93,13 @@ struct GemmArgs {
   const float* sa = nullptr;
   const float* sw = nullptr;
   int* status = nullptr;
+  // Grouped launch (groups > 1; bf16 output modes, tile width >= 128): group g multiplies the
+  // same A by B_g (tensor map tmB_grp[g], in device memory, 64-byte aligned), adds bias_grp[g]
+  // and writes the out[] segments shifted by g * out_grp_stride elements.
+  int groups = 1;
+  const CUtensorMap* tmB_grp = nullptr;
+  const __nv_bfloat16* const* bias_grp = nullptr;
+  long long out_grp_stride = 0;
 };
 
 // C[M,N] = A[M,K] * B[N,K]^T.  tmA: box [128 rows, 64 cols]; tmB: box [bn rows, 64 cols];

@@ -62,7 +62,8 @@ __global__ void __launch_bounds__(320, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int M = args.M, N = args.N, K = args.K;
   const int num_m = (M + 127) / 128, num_n = (N + BN - 1) / BN;
-  const int num_tiles = num_m * num_n, num_kb = (K + KE - 1) / KE;
+  const int tpg = num_m * num_n;   // tiles per group
+  const int num_tiles = tpg * args.groups, num_kb = (K + KE - 1) / KE;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
@@ -97,7 +98,8 @@ __global__ void __launch_bounds__(320, 1)
       uint32_t phase = 0, used = 0, last_par = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-        const int mb = t % num_m, nb = t / num_m;
+        const int g = t / tpg, mb = (t - g * tpg) % num_m, nb = (t - g * tpg) / num_m;
+        const CUtensorMap* mB = args.groups > 1 ? args.tmB_grp + g : &tmB;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(empty + stage, phase ^ 1u, abort_flag, args.status, DEV_TIMEOUT_PRODUCER)) {
             ok = false;
@@ -105,7 +107,7 @@ __global__ void __launch_bounds__(320, 1)
           }
           mbar_arrive_expect_tx(full + stage, C::STAGE);
           tma_load_2d(sA + stage * C::A_BYTES, &tmA, full + stage, kb * KE, mb * 128);
-          tma_load_2d(sB + stage * C::B_BYTES, &tmB, full + stage, kb * KE, nb * BN);
+          tma_load_2d(sB + stage * C::B_BYTES, mB, full + stage, kb * KE, nb * BN);
           used |= 1u << stage;
           last_par = (last_par & ~(1u << stage)) | (phase << stage);
           if (++stage == C::STAGES) {
@@ -170,7 +172,7 @@ __global__ void __launch_bounds__(320, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
-      const int mb = t % num_m, nb = t / num_m;
+      const int g = t / tpg, mb = (t - g * tpg) % num_m, nb = (t - g * tpg) / num_m;
       const int row = mb * 128 + q * 32 + lane;
       const int colh = nb * BN + h * (BN / 2);
       if (args.epi.mode == EPI_RESID_F32 && row < M && colh < N) {   // warm L2 with this thread's residual row part
@@ -202,7 +204,9 @@ __global__ void __launch_bounds__(320, 1)
             if (args.epi.mode == EPI_BF16_PUSH)
               epilogue_push64(args.epi, rowc, row0, colb, M, N, r[0], r[1], box, lane);
             else
-              epilogue_bf16_box<2>(args.epi, rowc, row0, colb, M, N, r, sa, args.sw, box, lane);
+              epilogue_bf16_box<2>(args.epi, args.groups > 1 ? args.bias_grp[g] : args.epi.bias,
+                                   (size_t)g * (size_t)args.out_grp_stride, rowc, row0, colb, M, N, r, sa,
+                                   args.sw, box, lane);
           }
         }
       } else {   // 32 columns at a time
@@ -244,6 +248,12 @@ __global__ void __launch_bounds__(320, 1)
 int gemm_check(const GemmArgs& a, int bn) {
   const GemmEpi& e = a.epi;
   if (a.M <= 0 || a.N <= 0 || a.K <= 0) return FW_EINVAL;
+  if (a.groups < 1) return FW_EINVAL;
+  if (a.groups > 1) {   // grouped launches take the bf16 box epilogue only
+    if (bn < 128 || !a.tmB_grp || !a.bias_grp || (reinterpret_cast<uintptr_t>(a.tmB_grp) & 63u) || a.out_grp_stride < 0)
+      return FW_EINVAL;
+    if (e.mode != EPI_BF16 && e.mode != EPI_GELU_BF16 && e.mode != EPI_GELU_ERF_BF16) return FW_EINVAL;
+  }
   if (bn != 64 && bn != 128 && bn != 256) return FW_EINVAL;
   if (a.N % 32 || a.K % (a.sa ? 16 : 8)) return FW_ESHAPE;
   if (a.sa && (!a.sw || (reinterpret_cast<uintptr_t>(a.sw) & 15u))) return FW_EALIGN;
@@ -309,7 +319,7 @@ int gemm_bf16_launch(const CUtensorMap& tmA, const CUtensorMap& tmB, int bn, con
   if (rc) return rc;
   if (a.epi.mode == EPI_RESID_TMA && !tmC) return FW_EINVAL;
   const CUtensorMap& mc = tmC ? *tmC : tmA;   // unused unless EPI_RESID_TMA
-  const int tiles = ((a.M + 127) / 128) * ((a.N + bn - 1) / bn);
+  const int tiles = ((a.M + 127) / 128) * ((a.N + bn - 1) / bn) * a.groups;
   int grid = ctas > 0 ? ctas : num_sms();
   if (grid > tiles) grid = tiles;
   GemmArgs b = a;

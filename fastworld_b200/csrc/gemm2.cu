@@ -238,7 +238,7 @@ int gemm_pair_launch(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmA
                      const CUtensorMap* tmC) {
   int rc = gemm_check(a, g2::BN);
   if (rc) return rc;
-  if (a.epi.mode == EPI_BF16_PUSH) return FW_EINVAL;   // one-CTA kernel only
+  if (a.epi.mode == EPI_BF16_PUSH || a.groups != 1) return FW_EINVAL;   // one-CTA kernel only
   if (a.epi.mode == EPI_RESID_TMA && !tmC) return FW_EINVAL;
   const CUtensorMap& mc = tmC ? *tmC : tmA;
   const int tiles = ((a.M + g2::BM - 1) / g2::BM) * ((a.N + g2::BN - 1) / g2::BN);
