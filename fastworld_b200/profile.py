@@ -4,6 +4,9 @@
     python -m fastworld_b200.profile gemm  [--reps 3]     FFN-up GEMM, MG2 shape, GELU epilogue
     python -m fastworld_b200.profile gemm_resid           O-projection GEMM (N = K = 1536) with the gated residual
     python -m fastworld_b200.profile attn  [--reps 3]     steady self-attention, 12 heads, 2640 + 2640 keys
+    python -m fastworld_b200.profile fp8_peak             dense e4m3 peak: a library GEMM (cuBLASLt via
+                                                          torch._scaled_mm) at 8192^3, best of 10, next to
+                                                          this library's e4m3 GEMM at the same size
 """
 from __future__ import annotations
 
@@ -65,12 +68,43 @@ def attn(reps: int) -> None:
     print("attn ok")
 
 
+def fp8_peak(reps: int) -> None:
+    from fastworld_b200 import ops
+    n = 8192
+    g = torch.Generator(device="cuda").manual_seed(0)
+    a = torch.randn(n, n, device="cuda", generator=g).to(torch.bfloat16)
+    b = torch.randn(n, n, device="cuda", generator=g).to(torch.bfloat16)
+    a8, sa = ops.quant_e4m3(a)
+    b8, sw = ops.quant_e4m3(b)
+    fa, fb = a8.view(torch.float8_e4m3fn), b8.view(torch.float8_e4m3fn)
+    one = torch.ones((), device="cuda")
+
+    def best(fn, n_rep=10):
+        for _ in range(3):
+            fn()
+        t = 1e9
+        for _ in range(n_rep):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            t = min(t, e0.elapsed_time(e1))
+        return t
+    flop = 2.0 * n ** 3
+    t_lib = best(lambda: torch._scaled_mm(fa, fb.t(), one, one, out_dtype=torch.bfloat16))
+    t_ours = best(lambda: ops.gemm_e4m3(a8, sa, b8, sw, None, "none"))
+    t_bf16 = best(lambda: torch.matmul(a, b.t()))
+    print(f"e4m3 8192^3: library {flop / t_lib / 1e9:.1f} TFLOP/s, fastworld_b200 {flop / t_ours / 1e9:.1f} TFLOP/s; "
+          f"bf16 library {flop / t_bf16 / 1e9:.1f} TFLOP/s (burst, best of 10)")
+
+
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["chunk", "gemm", "gemm_resid", "attn"])
+    ap.add_argument("what", choices=["chunk", "gemm", "gemm_resid", "attn", "fp8_peak"])
     ap.add_argument("--chunks", type=int, default=2)
     ap.add_argument("--reps", type=int, default=3)
     ap.add_argument("--config", default="mg2")
     a = ap.parse_args()
     {"chunk": lambda: chunk(a.chunks, a.config), "gemm": lambda: gemm(a.reps), "gemm_resid": lambda: gemm_resid(a.reps),
-     "attn": lambda: attn(a.reps)}[a.what]()
+     "attn": lambda: attn(a.reps), "fp8_peak": lambda: fp8_peak(a.reps)}[a.what]()
