@@ -186,24 +186,42 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const __nv_bfloat16* __
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (row >= M) return;
   const __nv_bfloat16* xr = x + (size_t)row * ldx;
+  // both passes issue eight 16-byte loads per lane before using them (a row of the FFN hidden
+  // layer is 35 such steps; one load at a time made the kernel latency-bound)
+  constexpr int U = 8;
   float amax = 0.f;
-  for (int c = lane * 8; c < K; c += 256) {
-    const uint4 u = *reinterpret_cast<const uint4*>(xr + c);
-    const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+  for (int c0 = lane * 8; c0 < K; c0 += 256 * U) {
+    uint4 u[U];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float2 f = unpack_bf16(w4[i]);
-      amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
+    for (int i = 0; i < U; ++i)
+      u[i] = c0 + i * 256 < K ? *reinterpret_cast<const uint4*>(xr + c0 + i * 256) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int i = 0; i < U; ++i) {
+      const uint32_t w4[4] = {u[i].x, u[i].y, u[i].z, u[i].w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = unpack_bf16(w4[k]);
+        amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
+      }
     }
   }
   amax = warp_max(amax);
   const float sc = amax > 0.f ? amax * (1.f / 448.f) : 1.f;
   const float inv = 1.f / sc;
-  for (int c = lane * 8; c < K; c += 256) {
-    const uint4 u = *reinterpret_cast<const uint4*>(xr + c);
-    const float2 a = unpack_bf16(u.x), b = unpack_bf16(u.y), cc = unpack_bf16(u.z), d = unpack_bf16(u.w);
-    *reinterpret_cast<uint2*>(q + (size_t)row * ldq + c) =
-        make_uint2(pack4_e4m3(a.x, a.y, b.x, b.y, inv), pack4_e4m3(cc.x, cc.y, d.x, d.y, inv));
+  for (int c0 = lane * 8; c0 < K; c0 += 256 * U) {
+    uint4 u[U];
+#pragma unroll
+    for (int i = 0; i < U; ++i)
+      u[i] = c0 + i * 256 < K ? *reinterpret_cast<const uint4*>(xr + c0 + i * 256) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int i = 0; i < U; ++i) {
+      const int c = c0 + i * 256;
+      if (c < K) {
+        const float2 a = unpack_bf16(u[i].x), b = unpack_bf16(u[i].y), cc = unpack_bf16(u[i].z), d = unpack_bf16(u[i].w);
+        *reinterpret_cast<uint2*>(q + (size_t)row * ldq + c) =
+            make_uint2(pack4_e4m3(a.x, a.y, b.x, b.y, inv), pack4_e4m3(cc.x, cc.y, d.x, d.y, inv));
+      }
+    }
   }
   if (lane == 0) scale[row] = sc;
 }
