@@ -58,7 +58,9 @@ __device__ __forceinline__ uint32_t pack4_e4m3(float a, float b, float c, float 
 }
 
 template <typename Tin, int NG>
-__global__ void __launch_bounds__(256) ln_kernel(const Tin* __restrict__ x, int ldx, int M, float eps,
+// At most 85 registers (three blocks per SM): the 2640 rows of a chunk then run in one wave of
+// warps (at 127 registers only two blocks fit and 34 of the 330 blocks formed a second wave).
+__global__ void __launch_bounds__(256, 3) ln_kernel(const Tin* __restrict__ x, int ldx, int M, float eps,
                                                  const float* __restrict__ shift, const float* __restrict__ scale,
                                                  const __nv_bfloat16* __restrict__ w,
                                                  const __nv_bfloat16* __restrict__ b, __nv_bfloat16* __restrict__ out,
@@ -298,7 +300,9 @@ __global__ void __launch_bounds__(256) rms_rope_kernel(RmsPair pr, int ldx, int 
 // The same with eight consecutive elements per lane (D = 256 * NG8): one 16-byte load and store
 // per group; the lane's four RoPE pairs are consecutive table entries (two 16-byte loads).
 template <int NG8>
-__global__ void __launch_bounds__(256) rms_rope8_kernel(RmsPair pr, int ldx, int M, float eps,
+// At most 64 registers (four blocks per SM): 592 resident blocks against 660 for q and k of a
+// chunk (three per SM, at 70 registers, left half of the grid for a second wave).
+__global__ void __launch_bounds__(256, 4) rms_rope8_kernel(RmsPair pr, int ldx, int M, float eps,
                                                         const float2* __restrict__ rope, int hd, int ldo) {
   pdl_trigger();
   pdl_wait();
