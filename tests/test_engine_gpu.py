@@ -75,6 +75,16 @@ def test_small_rollout_matches_oracle():
         assert all(v < TOL for v in e.values()), e
 
 
+def test_grouped_prologue_three_layers_two_action_blocks():
+    """Three layers and two action blocks: the chunk prologue's grouped launches (all layers'
+    cross-attention K/V projections and K norms, all action blocks' keyboard chains) run with
+    more than one group, so every per-group offset is exercised against the oracle."""
+    cfg = SMALL.replace(name="small_3l2a", layers=3, action_blocks=(0, 2))
+    errs = rollout_vs_oracle(cfg, 2)
+    for e in errs:
+        assert all(v < TOL for v in e.values()), e
+
+
 def test_mg2_width_two_layers_matches_oracle():
     cfg = MG2.replace(name="mg2_2l", layers=2, action_blocks=(1,))
     errs = rollout_vs_oracle(cfg, 2)
