@@ -50,6 +50,12 @@ __host__ __device__ constexpr uint32_t s_col(int t) { return (uint32_t)(t * 256)
 __host__ __device__ constexpr uint32_t o_col(int t) { return (uint32_t)(t * 256 + 128); }
 }  // namespace attn
 
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 __global__ void __launch_bounds__(attn::THREADS, 1)
     attention_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK0,
                      const __grid_constant__ CUtensorMap tmV0, const __grid_constant__ CUtensorMap tmK1,
@@ -236,11 +242,14 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         for (int i = 0; i < 128; ++i)
           if (i >= valid) sv[i] = -INFINITY;
       }
+      // row max with three-input max (64 instructions for 128 scores)
       float mx8[8];
 #pragma unroll
-      for (int a = 0; a < 8; ++a) mx8[a] = sv[a];
+      for (int a = 0; a < 8; ++a) mx8[a] = fmaxf(sv[a], sv[a + 8]);
 #pragma unroll
-      for (int i = 8; i < 128; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], sv[i]);
+      for (int i = 16; i < 128; i += 16)
+#pragma unroll
+        for (int a = 0; a < 8; ++a) mx8[a] = max3f(mx8[a], sv[i + a], sv[i + 8 + a]);
       const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
                              fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]))) * sl2;
       // lazy rescale: keep the running max unless it grows by more than 2^8 (p stays <= 256)
@@ -249,15 +258,20 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         alpha = ex2(m - mx);   // 0 on the first block (m = -inf)
         m = mx;
       }
-      float rs8[8];
+      // exponent arguments and row sums on packed fp32 pairs (half the FFMA / FADD instructions);
+      // rs2[c] holds the sums of elements 8k + 2c and 8k + 2c + 1, in ascending k
+      float2 rs2[4];
 #pragma unroll
-      for (int a = 0; a < 8; ++a) rs8[a] = 0.f;
+      for (int c = 0; c < 4; ++c) rs2[c] = make_float2(0.f, 0.f);
+      const float2 sl2v = make_float2(sl2, sl2), nm = make_float2(-m, -m);
 #pragma unroll
-      for (int i = 0; i < 128; ++i) {
-        sv[i] = ex2(fmaf(sv[i], sl2, -m));
-        rs8[i & 7] += sv[i];
+      for (int j = 0; j < 64; ++j) {
+        const float2 x = __ffma2_rn(make_float2(sv[2 * j], sv[2 * j + 1]), sl2v, nm);
+        sv[2 * j] = ex2(x.x);
+        sv[2 * j + 1] = ex2(x.y);
+        rs2[j & 3] = __fadd2_rn(rs2[j & 3], make_float2(sv[2 * j], sv[2 * j + 1]));
       }
-      l = l * alpha + (((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7])));
+      l = l * alpha + (((rs2[0].x + rs2[0].y) + (rs2[1].x + rs2[1].y)) + ((rs2[2].x + rs2[2].y) + (rs2[3].x + rs2[3].y)));
       if (j > 0) {   // P buffer and O are free once the previous P V finished
         ok = mbar_wait(o_done + t, (uint32_t)(j - 1) & 1u, abort_flag, args.status, DEV_TIMEOUT_SOFTMAX);
         if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
