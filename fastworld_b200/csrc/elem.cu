@@ -68,15 +68,40 @@ __global__ void __launch_bounds__(256, 3) ln_kernel(const Tin* __restrict__ x, i
   pdl_trigger();
   pdl_wait();
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-  if (row >= M) return;
+  const bool live = row < M;
   constexpr int D = 128 * NG;
   float v[NG][4];
+  if (live) {   // the row's loads go out first
+#pragma unroll
+    for (int g = 0; g < NG; ++g) load4(x + (size_t)row * ldx + g * 128 + lane * 4, v[g]);
+  }
+  // The per-column vectors (1 + scale and shift, or w and b) are staged in shared memory by the
+  // whole block while the row loads are in flight, so the second half of the kernel reads them
+  // from shared memory instead of making a second round trip to L2 per warp.  With both an
+  // affine and a modulation (no caller of this engine) they are read from global memory.
+  const bool staged = (scale != nullptr) != (w != nullptr);
+  __shared__ float4 s_a[32 * NG], s_b[32 * NG];
+  if (staged) {
+    for (int i = threadIdx.x; i < 32 * NG; i += blockDim.x) {
+      float a4[4], b4[4];
+      if (scale) {
+        load4(scale + 4 * i, a4);
+        load4(shift + 4 * i, b4);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) a4[k] = 1.f + a4[k];
+      } else {
+        load4(w + 4 * i, a4);
+        load4(b + 4 * i, b4);
+      }
+      s_a[i] = make_float4(a4[0], a4[1], a4[2], a4[3]);
+      s_b[i] = make_float4(b4[0], b4[1], b4[2], b4[3]);
+    }
+    __syncthreads();
+  }
+  if (!live) return;
   float s = 0.f;
 #pragma unroll
-  for (int g = 0; g < NG; ++g) {
-    load4(x + (size_t)row * ldx + g * 128 + lane * 4, v[g]);
-    s += v[g][0] + v[g][1] + v[g][2] + v[g][3];
-  }
+  for (int g = 0; g < NG; ++g) s += v[g][0] + v[g][1] + v[g][2] + v[g][3];
   const float mean = warp_sum(s) * (1.f / D);
   float q = 0.f;
 #pragma unroll
@@ -94,14 +119,20 @@ __global__ void __launch_bounds__(256, 3) ln_kernel(const Tin* __restrict__ x, i
     float* y = v[g];
 #pragma unroll
     for (int i = 0; i < 4; ++i) y[i] = (y[i] - mean) * rstd;
-    if (w) {
+    if (staged) {   // y * (1 + scale) + shift, or y * w + b
+      const float4 A = s_a[g * 32 + lane], B = s_b[g * 32 + lane];
+      y[0] = y[0] * A.x + B.x;
+      y[1] = y[1] * A.y + B.y;
+      y[2] = y[2] * A.z + B.z;
+      y[3] = y[3] * A.w + B.w;
+    } else if (w) {
       float wv[4], bv[4];
       load4(w + c, wv);
       load4(b + c, bv);
 #pragma unroll
       for (int i = 0; i < 4; ++i) y[i] = y[i] * wv[i] + bv[i];
     }
-    if (scale) {
+    if (!staged && scale) {
       float sc[4], sh[4];
       load4(scale + c, sc);
       load4(shift + c, sh);
