@@ -331,9 +331,9 @@ __global__ void __launch_bounds__(256) rms_rope_kernel(RmsPair pr, int ldx, int 
 // The same with eight consecutive elements per lane (D = 256 * NG8): one 16-byte load and store
 // per group; the lane's four RoPE pairs are consecutive table entries (two 16-byte loads).
 template <int NG8>
-// At most 64 registers (four blocks per SM): 592 resident blocks against 660 for q and k of a
-// chunk (three per SM, at 70 registers, left half of the grid for a second wave).
-__global__ void __launch_bounds__(256, 4) rms_rope8_kernel(RmsPair pr, int ldx, int M, float eps,
+// At most 85 registers (three blocks per SM): with the RoPE pairs held from the start, a tighter
+// cap spilled and measured no faster than this one.
+__global__ void __launch_bounds__(256, 3) rms_rope8_kernel(RmsPair pr, int ldx, int M, float eps,
                                                         const float2* __restrict__ rope, int hd, int ldo) {
   pdl_trigger();
   pdl_wait();
@@ -347,6 +347,17 @@ __global__ void __launch_bounds__(256, 4) rms_rope8_kernel(RmsPair pr, int ldx, 
   const __nv_bfloat16* __restrict__ w = pr.w_grp ? pr.w_grp[blockIdx.y] : (y1 ? pr.w[1] : pr.w[0]);
   __nv_bfloat16* __restrict__ out = pr.w_grp ? pr.out[0] + goff : (y1 ? pr.out[1] : pr.out[0]);
   constexpr int D = 256 * NG8;
+  const int half = hd >> 1;
+  // When the head dim divides 256 (64, 128), a lane's four RoPE pairs are the same in every
+  // 256-column group: they are loaded once, together with the row, instead of once per group
+  // after the row's statistics.
+  const bool rope_once = rope && 256 % hd == 0;
+  float4 cs01 = make_float4(0.f, 0.f, 0.f, 0.f), cs23 = cs01;
+  if (rope_once) {
+    const float4* rp = reinterpret_cast<const float4*>(rope + (size_t)row * half + (((lane * 8) % hd) >> 1));
+    cs01 = __ldg(rp);
+    cs23 = __ldg(rp + 1);
+  }
   float v[NG8][8];
   float q = 0.f;
 #pragma unroll
@@ -357,7 +368,6 @@ __global__ void __launch_bounds__(256, 4) rms_rope8_kernel(RmsPair pr, int ldx, 
   }
   const float tot = pr.ss ? __ldg(pr.ss + (size_t)row * 2 + blockIdx.y) : warp_sum(q);
   const float r = rsqrtf(tot * (pr.ss ? pr.inv_d : 1.f / D) + eps);
-  const int half = hd >> 1;
 #pragma unroll
   for (int g = 0; g < NG8; ++g) {
     const int c = g * 256 + lane * 8;
@@ -366,8 +376,11 @@ __global__ void __launch_bounds__(256, 4) rms_rope8_kernel(RmsPair pr, int ldx, 
 #pragma unroll
     for (int i = 0; i < 8; ++i) y[i] = v[g][i] * r * wv[i];
     if (rope) {
-      const float4* rp = reinterpret_cast<const float4*>(rope + (size_t)row * half + ((c % hd) >> 1));
-      const float4 cs01 = __ldg(rp), cs23 = __ldg(rp + 1);
+      if (!rope_once) {
+        const float4* rp = reinterpret_cast<const float4*>(rope + (size_t)row * half + ((c % hd) >> 1));
+        cs01 = __ldg(rp);
+        cs23 = __ldg(rp + 1);
+      }
       const float cs[8] = {cs01.x, cs01.y, cs01.z, cs01.w, cs23.x, cs23.y, cs23.z, cs23.w};
 #pragma unroll
       for (int p = 0; p < 4; ++p) {
