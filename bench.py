@@ -276,7 +276,8 @@ def run_ours(args):
     d2h = S.out.numel() * 2
     variants = {}
     if not args.no_fp8:   # same chunk with e4m3 block linears
-        del S
+        S.graphs = {}
+        S = None
         torch.cuda.empty_cache()
         ms8 = steady_chunk_ms(MG2_FP8, args, rank, world, local)
         variants["fp8"] = {"ms_per_step": ms8, "value": world * FRAMES_PER_CHUNK / (ms8 / 1e3), "unit": "frames/s",
@@ -309,9 +310,10 @@ def run_ours(args):
                              "launch_ms": gemm_ms, "algorithmic_gflop": gflop},
                 "cpu_baseline": cpu, "clocks": clk.summary(), "device_status": status, "variants": variants}
         print(json.dumps(line), flush=True)
+    if S is not None:
+        S.graphs = {}
     if world > 1:
         torch.distributed.barrier()
-        S.graphs = {}
         torch.distributed.destroy_process_group()
 
 

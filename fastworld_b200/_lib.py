@@ -77,6 +77,12 @@ _SIGS = {
     "fw_tp_reduce_once": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
     "fw_tp_allreduce": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int,
                                        ctypes.c_void_p]),
+    "fw_graph_begin": (ctypes.c_int, [ctypes.c_void_p]),
+    "fw_graph_end": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)]),
+    "fw_graph_launch": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
+    "fw_graph_nodes": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_size_t)]),
+    "fw_graph_destroy": (None, [ctypes.c_void_p]),
+    "fw_peer_access": (ctypes.c_int, [ctypes.c_int]),
     "fw_attention": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
                                     ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p,
                                     ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),

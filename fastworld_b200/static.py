@@ -140,6 +140,7 @@ class B200StaticMG:
         self.steps = [int(t) for t in cfg.steps]
         self.images: Dict[str, Dict[str, torch.Tensor]] = {}
         self.graphs, self.cur_img = {}, None
+        self._peers = set()
 
     def _tp_connect(self, tp_group) -> None:
         """Create the engine's NCCL communicator: the group's first rank draws the id, the
@@ -257,10 +258,22 @@ class B200StaticMG:
         else:
             self._prefill(k == 0)
 
-    def state(self) -> SessionState:
-        """Snapshot of the history buffers: one copy kernel into a new device buffer."""
-        blob = torch.empty_like(self._blob)
-        check(lib().fw_copy(ptr(blob), ptr(self._blob), self._blob.numel(), stream_ptr()), "fw_copy")
+    def _reach(self, dev: torch.device) -> None:
+        """Let this session's GPU read and write ``dev``'s memory (peer access, once per device)."""
+        if dev == self.dev or dev.index in self._peers:
+            return
+        with torch.cuda.device(self.dev):
+            check(lib().fw_peer_access(dev.index), f"fw_peer_access({dev})")
+        self._peers.add(dev.index)
+
+    def state(self, device=None) -> SessionState:
+        """Snapshot of the history buffers: one copy kernel into a new device buffer, on this
+        session's GPU or, with ``device``, in another GPU's memory (written over NVLink)."""
+        dev = torch.device(device) if device is not None else self.dev
+        self._reach(dev)
+        blob = torch.empty(self._blob.numel(), dtype=torch.uint8, device=dev)
+        with torch.cuda.device(self.dev):
+            check(lib().fw_copy(ptr(blob), ptr(self._blob), self._blob.numel(), stream_ptr()), "fw_copy")
         views, off = [], 0
         for name in self._state_names:
             t = self.buffers[name]
@@ -274,13 +287,17 @@ class B200StaticMG:
         allocation: a checkpoint pool recycles evicted checkpoints through this."""
         if not isinstance(st, SessionState) or st.blob.numel() != self._blob.numel():
             return self.state()
-        check(lib().fw_copy(ptr(st.blob), ptr(self._blob), self._blob.numel(), stream_ptr()), "fw_copy")
+        self._reach(st.blob.device)
+        with torch.cuda.device(self.dev):
+            check(lib().fw_copy(ptr(st.blob), ptr(self._blob), self._blob.numel(), stream_ptr()), "fw_copy")
         return st
 
     def load(self, st) -> None:
         """Restore a snapshot into the live buffers (pointers baked into graphs stay valid)."""
         if isinstance(st, SessionState) and st.blob.numel() == self._blob.numel():
-            check(lib().fw_copy(ptr(self._blob), ptr(st.blob), self._blob.numel(), stream_ptr()), "fw_copy")
+            self._reach(st.blob.device)     # a checkpoint placed on a peer GPU is read over NVLink
+            with torch.cuda.device(self.dev):
+                check(lib().fw_copy(ptr(self._blob), ptr(st.blob), self._blob.numel(), stream_ptr()), "fw_copy")
             return
         for d, s in zip(self._state_tensors(), st):
             s = s.to(d.device).contiguous()

@@ -18,6 +18,7 @@
  *   fw_prefill                                       StaticMG._prefill        static.py:244-245
  *   fw_forward                                       StaticMG._net            static.py:194-230
  *   fw_copy                                          StaticMG.state / load    static.py:273-278
+ *   fw_graph_*                                       graph.capture            graph.py:13-33
  *   fw_gemm_bf16, fw_attention, fw_* ops             the torch / flash-attn calls inside _net
  */
 #ifndef FASTWORLD_B200_H
@@ -162,6 +163,23 @@ int fw_ipc_get_handle(const void* ptr, void* handle, size_t* offset);
 int fw_ipc_open(const void* handle, void** ptr);
 int fw_ipc_close(void* ptr);
 
+/* ---- CUDA graphs held by the library (replace torch.cuda.CUDAGraph in graph.capture,
+ * fastworld/graph.py:13-33) ----
+ * fw_graph_begin starts recording `stream` (thread-local capture: launches this thread issues on
+ * `stream` are recorded, not executed; not the legacy default stream); fw_graph_end stops
+ * recording and instantiates the executable graph (it always ends the capture, also on error);
+ * fw_graph_launch replays it on any stream of the same device; fw_graph_destroy frees it.
+ * Recorded work must only read and write buffers that outlive the graph. */
+typedef struct fw_graph fw_graph;
+int fw_graph_begin(void* stream);
+int fw_graph_end(void* stream, fw_graph** out);
+int fw_graph_launch(const fw_graph* g, void* stream);
+int fw_graph_nodes(const fw_graph* g, size_t* n);
+void fw_graph_destroy(fw_graph* g);
+/* Let kernels on the current device read and write `peer`'s memory (checkpoints placed on
+ * another GPU; fastworld/prefix_cache.py:85-87 keeps every checkpoint on the GPU that made it). */
+int fw_peer_access(int peer);
+
 /* ---- individual kernels (used by the engine; exported for tests and reuse) ---- */
 /* C[M,N] = A[M,K] B[N,K]^T (+ bias[N]) with A, B, C bf16 row-major, fp32 accumulate.
  * epilogue: 0 = store bf16, 1 = GELU(tanh) then bf16, 3 = store fp32 (out is float*).
@@ -180,9 +198,10 @@ int fw_quant_e4m3(const void* x, int M, int K, void* q, float* scale, void* stre
  * the same computation as fw_quant_e4m3 into caller scratch followed by fw_gemm_e4m3, but the
  * quantised copy of x lives in a fixed array inside the library (32 MiB of activations and
  * 16384 row scales per GPU, held until the process exits): M * K must be <= 32 MiB and
- * M <= 16384, else FW_ESCRATCH.  It calls no cudaMalloc / cudaFree.  The first call on a device
- * looks up the array's device address (once per device, with that device current); make that
- * first call before any stream capture.  All calls share the array and it keeps the last call's
+ * M <= 16384, else FW_ESCRATCH; shapes and alignments the GEMM rejects are refused before
+ * anything is launched.  It calls no cudaMalloc / cudaFree.  The first call in a CUDA context
+ * (with that context's device current) looks up the array's device address and caches it for
+ * that context; make that first call before any stream capture.  All calls share the array and it keeps the last call's
  * contents: calls whose executions overlap on the GPU (other streams, other threads) race. */
 int fw_linear_e4m3_noalloc(const void* x, const void* w8, const float* sw, const void* bias, void* out, int M, int N,
                            int K, void* stream);

@@ -118,3 +118,52 @@ def test_bounded_checkpoints_match_scratch_and_recycle():
     assert len(cache._held) <= 3 and cache.n_evicted > 0
     assert rt.allocated == 3          # the pool never grew past its bound
     assert rt.calls["load"] > 0
+
+
+class PlacedState:
+    def __init__(self, h, device):
+        self.h, self.device = h, device
+
+
+class PlacingRuntime(FakeRuntime):
+    """FakeRuntime whose snapshots record the device they were placed on (labels only; nothing
+    is allocated on a GPU)."""
+
+    dev = torch.device("cuda:0")
+
+    def __init__(self):
+        super().__init__()
+        self.placed = []
+
+    def state(self, device=None):
+        d = torch.device(device) if device is not None else self.dev
+        self.placed.append(d)
+        return PlacedState(self.h, d)
+
+    def state_into(self, box):
+        box.h = self.h
+        return box
+
+    def load(self, st):
+        self.calls["load"] += 1
+        self.h = st.h
+
+
+def test_checkpoints_spill_to_a_peer_device_then_recycle():
+    main = [("img", c) for c in "wwwwwwwwwwww"]       # 12 chunks: checkpoints after chunks 1, 3, 5, 7, 9
+    rt = PlacingRuntime()
+    cache = PrefixCache(rt, FakeDecoder(), every=2, devices=["cuda:0", "cuda:1"], per_device=2)
+    scratch = PrefixCache(FakeRuntime(), FakeDecoder(), every=None)
+    a, _ = scratch.serve(main)
+    b, _ = cache.serve(main)
+    assert all(torch.equal(x, y) for x, y in zip(a, b))
+    # two on the session's own GPU, two spilled to the peer, the fifth recycles the oldest in place
+    assert [d.index for d in rt.placed] == [0, 0, 1, 1]
+    assert cache.n_ckpt == 5 and cache.n_evicted == 1 and len(cache._held) == 4
+    devs = sorted(n.slot.device.index for n in cache._held)
+    assert devs == [0, 0, 1, 1]
+    # a rewind to chunk 6 restores the deepest held checkpoint at or before it (after chunk 5, on the peer)
+    c, st = cache.serve(main[:7] + [("img", "a")])
+    d, _ = scratch.serve(main[:7] + [("img", "a")])
+    assert all(torch.equal(x, y) for x, y in zip(c, d))
+    assert st["restored"] == 1 and st["replayed"] == 1
