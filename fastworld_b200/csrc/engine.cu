@@ -94,6 +94,9 @@ struct fw_handle {
   // the action blocks' keyboard chains as four grouped launches (pointer arrays in "act.grp")
   bool kb_grouped = false;
   const __nv_bfloat16* const* kb_grp = nullptr;
+  // intermediate-tensor tap of one block (fw_set_tap; eager parity checks)
+  int tap_layer = -1;
+  uint8_t* tap = nullptr;
 };
 
 namespace fw {
@@ -819,10 +822,22 @@ static int forward(fw_handle* h, int step, int first, int write, const __nv_bflo
     const std::string p = "b" + std::to_string(i) + ".";
     const float* ee = h->ee + (size_t)i * 6 * D;
     const int Dl = h->Dl;
+    // tap slots: fp32 residual [L, D] at TAP_XS_IN..TAP_XS_OUT, then bf16 [L, Dl] q, k, v, attention
+    const bool tap = h->tap && h->tap_layer == i;
+    const size_t xs_b = (size_t)L * D * 4, qb = (size_t)L * Dl * 2;
+    auto tap_xs = [&](int slot) { return tap ? copy_bytes(h->tap + slot * xs_b, h->xs, xs_b, s) : 0; };
+    auto tap_bf = [&](int slot, const void* src) {
+      return tap ? copy_bytes(h->tap + 5 * xs_b + slot * qb, src, qb, s) : 0;
+    };
+    FW_TRY(tap_xs(0));
     FW_TRY(ln_op(h, L, D, c.eps, ee + 0 * D, ee + 1 * D, nullptr, nullptr, s));
     FW_TRY(run(ly.qkv, s));
     FW_TRY(rms_norm_op(h, h->q, h->kcur, W(h, p + "sa.nq.w"), W(h, p + "sa.nk.w"), L, rope, s));
+    FW_TRY(tap_bf(0, h->q));
+    FW_TRY(tap_bf(1, h->kcur));
+    FW_TRY(tap_bf(2, h->vcur));
     FW_TRY(run(first ? ly.self_first : ly.self_steady, s));
+    FW_TRY(tap_bf(3, h->ao));
     if (write) {   // the history is written after the attention read it (static.py:217-218)
       const size_t bytes = (size_t)L * Dl * 2;
       void* hk = ptr_of(h, "hk." + std::to_string(i));
@@ -837,17 +852,21 @@ static int forward(fw_handle* h, int step, int first, int write, const __nv_bflo
     }
     FW_TRY(run_from(h, ly.o, h->ao, Dl, s));
     FW_TRY(row_parallel_done(h, p + "sa.o.b", ee + 2 * D, nullptr, (3 * i) & 1, s));
+    FW_TRY(tap_xs(1));
     FW_TRY(ln_op(h, L, D, c.eps, nullptr, nullptr, W(h, p + "n3.w"), W(h, p + "n3.b"), s));
     FW_TRY(run(ly.caq, s));
     FW_TRY(rms_norm_op(h, h->q, nullptr, W(h, p + "ca.nq.w"), nullptr, L, nullptr, s));
     FW_TRY(run(ly.cross, s));
     FW_TRY(run_from(h, ly.cao, h->ao, Dl, s));
     FW_TRY(row_parallel_done(h, p + "ca.o.b", nullptr, nullptr, (3 * i + 1) & 1, s));
+    FW_TRY(tap_xs(2));
     if (ly.act >= 0) FW_TRY(action(h, i, first, write, s));
+    FW_TRY(tap_xs(3));
     FW_TRY(ln_op(h, L, D, c.eps, ee + 3 * D, ee + 4 * D, nullptr, nullptr, s));
     FW_TRY(run(ly.ff0, s));
     FW_TRY(run_from(h, ly.ff2, h->hb, h->FFl, s));
     FW_TRY(row_parallel_done(h, p + "ffn.2.b", ee + 5 * D, nullptr, (3 * i + 2) & 1, s));
+    FW_TRY(tap_xs(4));
   }
   FW_TRY(ln_f32(h->xs, D, L, D, c.eps, h->hmod, h->hmod + D, nullptr, nullptr, h->y, D, s));
   FW_TRY(run(h->head, s));
@@ -997,6 +1016,26 @@ int fw_forward(fw_handle* h, int step, int first, int write, void* stream) {
   // one forward from x_in (or lat_in for the context step) into out
   const __nv_bfloat16* x = fw::P<__nv_bfloat16>(h, step < h->cfg.n_steps ? "x_in" : "lat_in");
   return fw::forward(h, step, first, write, x, h->den, fw::P<__nv_bfloat16>(h, "out"), nullptr, 0.f, nullptr, s);
+}
+
+size_t fw_tap_bytes(const fw_handle* h) {
+  if (!h) return 0;
+  return 5 * (size_t)h->L * h->D * 4 + 4 * (size_t)h->L * h->Dl * 2;
+}
+
+int fw_set_tap(fw_handle* h, int layer, void* buf, size_t bytes) {
+  if (!h) return FW_EINVAL;
+  if (!buf || layer < 0) {
+    h->tap = nullptr;
+    h->tap_layer = -1;
+    return 0;
+  }
+  if (layer >= h->cfg.layers) return FW_EINVAL;
+  if (bytes < fw_tap_bytes(h)) return FW_ESIZE;
+  if (reinterpret_cast<uintptr_t>(buf) & 15u) return FW_EALIGN;
+  h->tap = static_cast<uint8_t*>(buf);
+  h->tap_layer = layer;
+  return 0;
 }
 
 void fw_destroy(fw_handle* h) {

@@ -310,6 +310,31 @@ class B200StaticMG:
     def state_bytes(self) -> int:
         return fw_graph.state_bytes(self._state_tensors())
 
+    def set_tap(self, layer: Optional[int]) -> Optional[Dict[str, torch.Tensor]]:
+        """Copy block ``layer``'s intermediates on every following forward (``fw_set_tap``);
+        returns named views of the tap buffer (None clears the tap).  Residual stream fp32
+        [L, dim]: ``xs_in``, ``xs_sa`` (after self-attention), ``xs_ca`` (after cross-attention),
+        ``xs_act`` (after the action module), ``xs_out``; bf16 [L, heads, head_dim] of this
+        rank: ``q`` and ``k`` after RMSNorm + RoPE, ``v``, ``attn`` (self-attention output)."""
+        if layer is None:
+            check(lib().fw_set_tap(self._h, -1, None, 0), "fw_set_tap")
+            self._tap = None
+            return None
+        nb = lib().fw_tap_bytes(self._h)
+        buf = torch.zeros(nb, dtype=torch.uint8, device=self.dev)
+        check(lib().fw_set_tap(self._h, int(layer), ptr(buf), nb), "fw_set_tap")
+        self._tap = buf
+        c = self.cfg
+        L, D, hl = c.tokens, c.dim, c.heads // self.tp_size
+        xs_b, qb = L * D * 4, L * hl * c.head_dim * 2
+        views = {}
+        for j, name in enumerate(("xs_in", "xs_sa", "xs_ca", "xs_act", "xs_out")):
+            views[name] = buf[j * xs_b:(j + 1) * xs_b].view(torch.float32).view(L, D)
+        for j, name in enumerate(("q", "k", "v", "attn")):
+            o = 5 * xs_b + j * qb
+            views[name] = buf[o:o + qb].view(torch.bfloat16).view(L, hl, c.head_dim)
+        return views
+
     def device_status(self) -> List[int]:
         """Device status words (0 = ok; otherwise a bounded wait gave up).  Synchronises."""
         return [int(v) for v in self.status.cpu()]

@@ -124,6 +124,17 @@ int fw_forward(fw_handle* h, int step, int first, int write, void* stream);
  * that captured this handle's launches first). */
 void fw_destroy(fw_handle* h);
 
+/* Parity tap (the reference's exactness ladder compares one forward layer by layer,
+ * scripts/mg2/test_static.py:50-57): while set, every forward copies block `layer`'s
+ * intermediates into `buf` (fw_tap_bytes(h) bytes, 16-byte aligned):
+ *   fp32 [L, D] residual stream at 5 points: block input, after self-attention (+ gated o-proj),
+ *   after cross-attention, after the action module (= the previous one without it), block output;
+ *   then bf16 [L, Dl]: q and k after RMSNorm + RoPE, v, and the self-attention output.
+ * layer < 0 or buf == NULL clears it.  Meant for eager launches; a graph recorded while a tap is
+ * set replays the copies. */
+size_t fw_tap_bytes(const fw_handle* h);
+int fw_set_tap(fw_handle* h, int layer, void* buf, size_t bytes);
+
 /* ---- tensor parallelism (no counterpart in the reference, whose runtimes are single-GPU;
  * BASELINE configs[4]) ----
  * NCCL is loaded at run time (libnccl.so.2: the copy already in the process if any).

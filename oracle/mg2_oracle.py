@@ -280,11 +280,14 @@ class Oracle:
         a = a.transpose(0, 1).reshape(F * S, AH * AD)
         return hs + self.lin(a, f"{p}.pkb")
 
-    def block(self, i: int, xs, e0, fi, st, first: bool, write: bool, ctx_kv, gm=None, kc=None, s=0):
-        """One transformer block of ``_net`` (static.py:203-225)."""
+    def block(self, i: int, xs, e0, fi, st, first: bool, write: bool, ctx_kv, gm=None, kc=None, s=0, taps=None):
+        """One transformer block of ``_net`` (static.py:203-225).  ``taps`` (a dict) receives
+        the intermediates the engine's block tap copies (same names)."""
         c, p, W = self.cfg, f"b{i}", self.W
         F, S = c.frames, c.tok_per_frame
         ee = (W[f"{p}.mod"][None] + e0).unbind(1)                            # 6 x [F, dim]
+        tap = taps.__setitem__ if taps is not None else (lambda k, v: None)
+        tap("xs_in", xs)
 
         def per_frame(x, fn):
             return fn(x.view(F, S, c.dim)).reshape(F * S, c.dim)
@@ -295,6 +298,9 @@ class Oracle:
         v = self.lin(y_in, f"{p}.sa.v").view(-1, c.heads, c.head_dim)
         rq, rk = self.r(apply_rope(q, fi)), self.i(apply_rope(k, fi))
         v = self.i(v)
+        tap("q", rq)
+        tap("k", rk)
+        tap("v", v)
         L, Wn, k_idx = c.tokens, c.hist_chunks, s // c.frames
         # keys: the filled history slots (one chunk for MG2, static.py:213-216), then the
         # current chunk; with a window of Wn > 1 chunks, chunk k has min(k, Wn) filled slots
@@ -306,14 +312,20 @@ class Oracle:
         if write:   # ring slot k % Wn (static.py:217-218 for Wn = 1)
             sl = slice((k_idx % Wn) * L, (k_idx % Wn + 1) * L)
             st["hk"][i][sl], st["hv"][i][sl] = rk, v
+        tap("attn", self.r(y))
         y = self.lin(self.r(y).reshape(-1, c.dim), f"{p}.sa.o")
         xs = xs + per_frame(y, lambda t: t * ee[2][:, None])
+        tap("xs_sa", xs)
         xs = xs + self.cross(i, self.r(layer_norm(xs, W[f"{p}.n3.w"], W[f"{p}.n3.b"], c.eps)), ctx_kv)
+        tap("xs_ca", xs)
         if i in c.action_blocks:
             xs = self.action(i, xs, st, first, write, gm, kc, s)
+        tap("xs_act", xs)
         y_in = self.r(per_frame(layer_norm(xs, eps=c.eps), lambda t: t * (1 + ee[4][:, None]) + ee[3][:, None]))
         y = self.lin(self.r(gelu_tanh(self.lin(y_in, f"{p}.ffn.0"))), f"{p}.ffn.2")
-        return xs + per_frame(y, lambda t: t * ee[5][:, None])
+        xs = xs + per_frame(y, lambda t: t * ee[5][:, None])
+        tap("xs_out", xs)
+        return xs
 
     def head(self, xs, e):
         c, W = self.cfg, self.W
@@ -363,13 +375,14 @@ class Oracle:
         """``_prefill`` (static.py:244-245): one context forward over a known latent."""
         self.net(st, self.i(lat.float()), 0.0, first, True, inputs)
 
-    def block_forward(self, xs, t: float, hist_k, hist_v, vis, k: int = 0):
+    def block_forward(self, xs, t: float, hist_k, hist_v, vis, k: int = 0, taps=None):
         """one block, residual tokens in, residual tokens out; keys are
-        [history | current] (steady chunk)."""
+        [history | current] (steady chunk k; with a window of W chunks the first min(k, W)
+        slots of ``hist_k`` / ``hist_v`` are filled).  ``taps`` as in :meth:`block`."""
         c = self.cfg
         st = self.new_state()
         st["hk"][0], st["hv"][0] = hist_k, hist_v
         _, e0 = self.time_embed(t)
         ctx = self.context(vis)
         return self.block(0, xs.float(), e0[None].expand(c.frames, 6, c.dim), rope_table(c, k, self.freqs),
-                          st, False, False, self.cross_kv(0, ctx))
+                          st, False, False, self.cross_kv(0, ctx), s=c.frames * k, taps=taps)

@@ -7,8 +7,10 @@ bitwise equality because the kernels differ):
   2. CUDA-graph replay is bitwise equal to the eager launch sequence;
   3. save -> alternative chunk -> restore -> continue is bitwise equal to the uninterrupted run;
   4. state() / load() round trip is bit-exact.
-Tolerances (bf16 GEMM operands and activations vs an fp32 oracle): latent rel-L2 <= 3e-2,
-history K/V rel-L2 <= 3e-2 per layer.
+Tolerances (bf16 GEMM operands and activations vs an fp32 oracle), about three times the
+errors measured on B200: latent and every layer's history K/V rel-L2 <= 1.2e-2, action-module
+state rel-L2 <= 1.5e-2; the full-depth chunk also bounds the largest absolute error (relative
+to the reference's largest magnitude) of the latent and of every layer's history K/V.
 """
 import pytest
 import torch
@@ -21,7 +23,12 @@ pytestmark = pytest.mark.gpu
 
 PATH = [("img0", ("w", "u")), ("img0", ("a", "l")), ("img0", ("q", "i")), ("img0", ("d", "j")),
         ("img0", ("s", "k"))]
-TOL = 3e-2
+TOL = {"out": 1.2e-2, "hk": 1.2e-2, "hv": 1.2e-2, "mk": 1.5e-2, "mv": 1.5e-2, "kk": 1.5e-2, "kv": 1.5e-2}
+MAXABS = {"out": 4e-2, "hk": 4e-2, "hv": 4e-2}
+
+
+def within(e):
+    return all(v < TOL[k] for k, v in e.items())
 
 
 def rel(a, b):
@@ -72,7 +79,7 @@ def rollout_vs_oracle(cfg, nchunks, seed=0):
 def test_small_rollout_matches_oracle():
     errs = rollout_vs_oracle(SMALL, 3)
     for e in errs:
-        assert all(v < TOL for v in e.values()), e
+        assert within(e), e
 
 
 def test_grouped_prologue_three_layers_two_action_blocks():
@@ -82,14 +89,62 @@ def test_grouped_prologue_three_layers_two_action_blocks():
     cfg = SMALL.replace(name="small_3l2a", layers=3, action_blocks=(0, 2))
     errs = rollout_vs_oracle(cfg, 2)
     for e in errs:
-        assert all(v < TOL for v in e.values()), e
+        assert within(e), e
 
 
 def test_mg2_width_two_layers_matches_oracle():
     cfg = MG2.replace(name="mg2_2l", layers=2, action_blocks=(1,))
     errs = rollout_vs_oracle(cfg, 2)
     for e in errs:
-        assert all(v < TOL for v in e.values()), e
+        assert within(e), e
+
+
+def maxabs(a, b):
+    a, b = a.float().cpu(), b.float().cpu()
+    return float((a - b).abs().max() / b.abs().max().clamp_min(1e-30))
+
+
+def test_mg2_full_depth_steady_chunk():
+    """BASELINE configs[1] at full depth (30 blocks, 15 action blocks): chunk 0 on the GPU, its
+    state handed to the oracle, then one steady chunk (4 denoising forwards + the context
+    forward) on both from the same latent and noise.  Latent and all 30 layers' history K/V
+    (and the action state) within the rel-L2 bounds; latent and history K/V also within the
+    max-abs bounds."""
+    from fastworld_b200.config import MG2
+    from oracle.mg2_oracle import Oracle
+    cfg = MG2
+    S, sd, img = make(cfg)
+    S._prep(PATH, 0)
+    S._chunk(True)
+    torch.cuda.synchronize()
+    orc = Oracle(cfg, sd)
+    del sd
+    st = orc.new_state()
+    for i in range(cfg.layers):
+        st["hk"][i].copy_(S.hk[i][0].float().cpu())
+        st["hv"][i].copy_(S.hv[i][0].float().cpu())
+    for nm in ("mk", "mv", "kk", "kv"):
+        for i in cfg.action_blocks:
+            st[nm][i] = getattr(S, nm)[i].float().cpu().reshape(st[nm][i].shape)
+    S._prep(PATH, 1)
+    x_in, noise = S.x_in.cpu(), [n.cpu() for n in S.noise]
+    S._chunk(False)
+    torch.cuda.synchronize()
+    assert S.device_status()[0] == 0
+    with torch.no_grad():
+        ref = orc.chunk(st, x_in[0].float(), [n.float() for n in noise], oracle_inputs(cfg, img, PATH, 1), False)
+    e = {"out": rel(S.out[0], ref),
+         "hk": max(rel(S.hk[i][0], st["hk"][i]) for i in range(cfg.layers)),
+         "hv": max(rel(S.hv[i][0], st["hv"][i]) for i in range(cfg.layers))}
+    for nm in ("mk", "mv", "kk", "kv"):
+        e[nm] = max(rel(getattr(S, nm)[i], st[nm][i]) for i in cfg.action_blocks)
+    m = {"out": maxabs(S.out[0], ref),
+         "hk": max(maxabs(S.hk[i][0], st["hk"][i]) for i in range(cfg.layers)),
+         "hv": max(maxabs(S.hv[i][0], st["hv"][i]) for i in range(cfg.layers))}
+    print("mg2 30 layers rel-L2: " + " ".join(f"{a}={b:.2e}" for a, b in e.items()) +
+          "; max-abs: " + " ".join(f"{a}={b:.2e}" for a, b in m.items()))
+    assert within(e), e
+    assert all(v < MAXABS[k] for k, v in m.items()), m
 
 
 def test_graph_replay_and_branch_bitwise():
