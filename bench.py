@@ -16,18 +16,26 @@ weights and inputs.  Metric: frames per second (12 pixel frames per chunk), whol
 * ``roofline``: the dominant kernel (the tcgen05 GEMM; FFN-up shape [2640 x 1536] x [8960 x 1536])
   timed alone with CUDA events; algorithmic flops 2 M N K per launch against the measured bf16
   burst peak.
-* ``cpu_baseline`` / ``--impl reference``: the reference forward restated on the CPU (the oracle
-  port; the reference's own GPU path needs the un-vendored official package), all host threads,
-  on a bounded sample: one full forward of a 2-block MG2-width slice (one action block),
-  scaled by 15 slices x 5 forwards per chunk.
+* ``cpu_baseline`` (N = 1): the reference forward restated on the CPU (the oracle port; the
+  reference's own GPU path needs the un-vendored official package), all host threads: the
+  chunk prologue and one complete 30-block steady forward are timed, chunk = prologue + 5
+  forwards.  ``--impl reference``: each step is one complete 30-block forward of a steady chunk
+  on the oracle port, cycling through the chunk's 5 forwards (prologue in the first), so every 5
+  steps are one complete chunk; warm-up steps are one block forward each.
+* ``variants``: ``fp8`` (configs[2], every N); ``tp14b`` (configs[4]: a steady Wan-14B-shaped chunk
+  tensor-parallel over the N ranks, every N); for N > 1 also ``explore`` (configs[3]: 64 sessions
+  from one image, prefix-cache branching, cross-GPU checkpoint restores over NVLink) and
+  ``tp_parity`` (a tensor-parallel test model over the N ranks: ranks bit-identical, latents
+  against the CPU oracle).
 
 Multi-GPU (torchrun): every rank runs its own session; there is no collective on the data path
-(sessions are independent).  Timing is bracketed by a barrier and synchronize; the job time is
-the max over ranks.
+of ``value`` (sessions are independent).  Timing is bracketed by a barrier and synchronize; the
+job time is the max over ranks.
 """
 from __future__ import annotations
 
 import argparse
+import datetime
 import json
 import os
 import subprocess
@@ -97,29 +105,87 @@ class Clocks:
                 "reasons": reasons, "samples": len(self.rows)}
 
 
-def cpu_sample_seconds(threads=None):
-    """Time one forward of a 2-block MG2-width slice (block 1 with the action module) with the
-    CPU oracle; returns (seconds per chunk extrapolated, sample seconds, threads)."""
-    from fastworld_b200.config import MG2
-    from fastworld_b200.prep import action_windows, synthetic_image
-    from fastworld_b200.weights import synthetic_state_dict
-    from oracle.mg2_oracle import Oracle
-    threads = threads or os.cpu_count()
-    torch.set_num_threads(threads)
-    cfg = MG2.replace(name="mg2_slice", layers=2, action_blocks=(1,))
-    orc = Oracle(cfg, synthetic_state_dict(cfg, 0))
-    img = synthetic_image(cfg, 1, 4)
-    path = [("img0", ("w", "u"))] * 3
-    kc, gm = action_windows(cfg, path, 1)
-    inputs = {"cc": img["cond_concat"][0, :, 3:6].float(), "vis": img["visual_context"][0].float(), "gm": gm,
-              "kc": kc, "k": 1}
-    st = orc.new_state()
-    x = torch.randn(16, 3, 44, 80)
+class CpuChunk:
+    """The steady chunk of configs[1] on the CPU oracle port, one forward per call of ``step``:
+    calls 0-3 are the denoising forwards (flow-matching update between them), call 4 the
+    context forward that rewrites the history; call 0 also runs the chunk prologue (context MLP
+    and every layer's cross-attention K/V).  History and action state start as N(0, 1)."""
+
+    def __init__(self, threads=None, cfg=None):
+        from fastworld_b200.config import MG2
+        from fastworld_b200.prep import action_windows, synthetic_image
+        from fastworld_b200.weights import synthetic_state_dict
+        from oracle.mg2_oracle import Oracle
+        self.threads = threads or os.cpu_count()
+        torch.set_num_threads(self.threads)
+        self.cfg = cfg = cfg or MG2
+        self.orc = Oracle(cfg, synthetic_state_dict(cfg, 0))
+        g = torch.Generator().manual_seed(3)
+        self.st = st = self.orc.new_state()
+        for nm in ("hk", "hv"):
+            st[nm].copy_(torch.randn(st[nm].shape, generator=g).bfloat16().float())
+        for nm in ("mk", "mv", "kk", "kv"):
+            for i in st[nm]:
+                st[nm][i] = torch.randn(st[nm][i].shape, generator=g).bfloat16().float()
+        img = synthetic_image(cfg, 1, 2)
+        path = [("img0", ("w", "u")), ("img0", ("a", "l"))]
+        kc, gm = action_windows(cfg, path, 1)
+        self.inputs = {"cc": img["cond_concat"][0, :, 3:6].float(), "vis": img["visual_context"][0].float(),
+                       "gm": gm, "kc": kc, "k": 1}
+        self.x_in = torch.randn(cfg.lat_ch, cfg.frames, cfg.lat_h, cfg.lat_w, generator=g).bfloat16().float()
+        self.noise = [torch.randn(cfg.frames, cfg.lat_ch, cfg.lat_h, cfg.lat_w, generator=g).bfloat16().float()
+                      for _ in cfg.steps[1:]]
+        self.j, self.x, self.den, self.ctx = 0, None, None, None
+
+    def prologue(self):
+        o = self.orc
+        ctx = o.context(self.inputs["vis"])
+        self.ctx = [o.cross_kv(i, ctx) for i in range(self.cfg.layers)]
+        self.x = self.x_in
+
+    @torch.no_grad()
+    def step(self):
+        from oracle.mg2_oracle import sigma_of
+        o, c, j = self.orc, self.cfg, self.j
+        if j == 0:
+            self.prologue()
+        n = len(c.steps)
+        if j < n:
+            self.den = o.net(self.st, self.x, c.steps[j], False, False, self.inputs, self.ctx)
+            if j < n - 1:
+                sg = sigma_of(c.steps[j + 1])
+                self.x = o.i((1 - sg) * self.den + sg * self.noise[j].transpose(0, 1))
+        else:
+            o.net(self.st, self.den, 0.0, False, True, self.inputs, self.ctx)
+        self.j = (j + 1) % (n + 1)
+
+    @torch.no_grad()
+    def warm(self):
+        """One block forward (the CPU path has only its allocator and thread pool to warm)."""
+        from oracle.mg2_oracle import rope_table
+        o, c = self.orc, self.cfg
+        if self.ctx is None:
+            self.prologue()
+        _, e0 = o.time_embed(750.0)
+        xs = torch.zeros(c.tokens, c.dim)
+        st = {k: (dict(v) if isinstance(v, dict) else v) for k, v in self.st.items()}
+        o.block(c.action_blocks[0], xs, e0[None].expand(c.frames, 6, c.dim), rope_table(c, 1, o.freqs), st, False,
+                False, self.ctx[c.action_blocks[0]], self.inputs["gm"], self.inputs["kc"], c.frames)
+
+
+def cpu_chunk_seconds():
+    """Our arm's CPU baseline: the chunk prologue and one complete steady forward (t = 750),
+    each timed once; a chunk is the prologue + 5 forwards (the five cost the same but for the
+    context forward's history write).  Returns (chunk s, forward s, prologue s, threads)."""
+    cc = CpuChunk()
+    t0 = time.time()
+    cc.prologue()
+    t_pro = time.time() - t0
     t0 = time.time()
     with torch.no_grad():
-        orc.net(st, x, 750.0, False, False, inputs)
-    dt = time.time() - t0
-    return dt * (MG2.layers // 2) * MG2.n_fwd, dt, threads
+        cc.orc.net(cc.st, cc.x, 750.0, False, False, cc.inputs, cc.ctx)
+    t_fwd = time.time() - t0
+    return t_pro + (len(cc.cfg.steps) + 1) * t_fwd, t_fwd, t_pro, cc.threads
 
 
 def run_reference(args):
@@ -127,21 +193,29 @@ def run_reference(args):
     if rank != 0:
         return
     from fastworld_b200.config import MG2
+    cc = CpuChunk()
+    for _ in range(args.warmup):
+        cc.warm()
+    per_chunk = len(MG2.steps) + 1
     times = []
-    for i in range(args.warmup + args.steps):
-        chunk_s, sample_s, threads = cpu_sample_seconds()
-        if i >= args.warmup:
-            times.append(chunk_s)
-    chunk_s = sum(times) / len(times)
+    for _ in range(args.steps):
+        t0 = time.time()
+        cc.step()
+        times.append(time.time() - t0)
+    step_s = sum(times) / len(times)
+    chunk_s = step_s * per_chunk
     fps = FRAMES_PER_CHUNK / chunk_s
-    sample = ("one forward of a 2-block MG2-width slice (1 action block) on the CPU oracle port, "
-              "x15 slices x5 forwards per chunk")
+    sample = (f"{args.steps} complete 30-block forwards of steady chunks ({args.steps / per_chunk:g} chunks: "
+              f"4 denoising forwards + the context forward each, prologue in the first), measured; "
+              f"warm-up steps one block forward each")
     line = {"metric": METRIC, "value": fps, "unit": "frames/s", "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": chunk_s * 1e3, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
             "config": {"workload": "mg2_steady_chunk", "model": MG2.name, "layers": MG2.layers,
-                       "tokens": MG2.tokens, "steps": list(MG2.steps) + [0.0]},
-            "cpu_baseline": {"value": fps, "unit": "frames/s", "cores": threads, "kind": "port", "sample": sample},
+                       "tokens": MG2.tokens, "steps": list(MG2.steps) + [0.0],
+                       "step": "one complete 30-block forward; 5 steps = one steady chunk",
+                       "chunk_ms": chunk_s * 1e3, "forward_ms": [t * 1e3 for t in times]},
+            "cpu_baseline": {"value": fps, "unit": "frames/s", "cores": cc.threads, "kind": "port", "sample": sample},
             "e2e": {"value": fps, "unit": "frames/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -180,10 +254,10 @@ def steady_chunk_ms(cfg, args, rank, world, local):
 
 
 def run_ours(args):
+    t_start = time.time()
     rank, world, local = dist_env()
     torch.cuda.set_device(local)
     if world > 1:
-        import datetime
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
     from fastworld_b200 import _lib, ops
     from fastworld_b200.config import MG2, MG2_FP8
@@ -275,23 +349,33 @@ def run_ours(args):
     h2d = S.gm.numel() * 2 + S.kc.numel() * 2 + 16
     d2h = S.out.numel() * 2
     variants = {}
-    if not args.no_fp8:   # same chunk with e4m3 block linears
-        S.graphs = {}
-        S = None
-        torch.cuda.empty_cache()
-        ms8 = steady_chunk_ms(MG2_FP8, args, rank, world, local)
-        variants["fp8"] = {"ms_per_step": ms8, "value": world * FRAMES_PER_CHUNK / (ms8 / 1e3), "unit": "frames/s",
-                           "speedup_vs_bf16": ms / ms8, "linear": "e4m3, per-channel weight / per-token scales"}
+    ctl = torch.distributed.new_group(backend="gloo", timeout=datetime.timedelta(seconds=600)) if world > 1 else None
+    if world > 1 and not args.no_explore and agree(time.time() - t_start < args.variant_budget, world, ctl):
+        variants["explore"] = guarded(lambda: explore_variant(S, rank, world, ctl), world, ctl)
+    S.graphs = {}
+    S = None
+    torch.cuda.empty_cache()
+    if not args.no_fp8 and agree(time.time() - t_start < args.variant_budget, world, ctl):
+        # same chunk with e4m3 block linears
+        def fp8():
+            ms8 = steady_chunk_ms(MG2_FP8, args, rank, world, local)
+            return {"ms_per_step": ms8, "value": world * FRAMES_PER_CHUNK / (ms8 / 1e3), "unit": "frames/s",
+                    "speedup_vs_bf16": ms / ms8, "linear": "e4m3, per-channel weight / per-token scales"}
+        variants["fp8"] = guarded(fp8, world, ctl)
+    if not args.no_tp and agree(time.time() - t_start < args.variant_budget, world, ctl):
+        variants["tp14b"] = guarded(lambda: tp14b_variant(rank, world, local, ctl), world, ctl)
+    if world > 1 and not args.no_tp and agree(time.time() - t_start < args.variant_budget, world, ctl):
+        variants["tp_parity"] = guarded(lambda: tp_parity_variant(rank, world, local, ctl), world, ctl)
     line = None
     if rank == 0:
         fps = world * FRAMES_PER_CHUNK / (ms / 1e3)
         e2e_fps = world * FRAMES_PER_CHUNK / (e2e_ms / 1e3)
         cpu = None
         if world == 1 and not args.no_cpu:
-            cpu_chunk_s, sample_s, threads = cpu_sample_seconds()
+            cpu_chunk_s, fwd_s, pro_s, threads = cpu_chunk_seconds()
             cpu = {"value": FRAMES_PER_CHUNK / cpu_chunk_s, "unit": "frames/s", "cores": threads, "kind": "port",
-                   "sample": f"one forward of a 2-block MG2-width slice (1 action block), {sample_s:.1f} s, "
-                             "x15 slices x5 forwards per chunk"}
+                   "sample": f"the chunk prologue ({pro_s:.1f} s) and one complete 30-block steady forward "
+                             f"({fwd_s:.1f} s), measured; chunk = prologue + 5 forwards"}
         line = {"metric": METRIC, "value": fps, "unit": "frames/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
@@ -310,11 +394,116 @@ def run_ours(args):
                              "launch_ms": gemm_ms, "algorithmic_gflop": gflop},
                 "cpu_baseline": cpu, "clocks": clk.summary(), "device_status": status, "variants": variants}
         print(json.dumps(line), flush=True)
-    if S is not None:
-        S.graphs = {}
     if world > 1:
-        torch.distributed.barrier()
+        torch.distributed.barrier(group=ctl)
         torch.distributed.destroy_process_group()
+
+
+def agree(flag: bool, world: int, ctl) -> bool:
+    """True when every rank passes True (the ranks must take the same collective steps)."""
+    if world == 1:
+        return bool(flag)
+    got = [None] * world
+    torch.distributed.all_gather_object(got, bool(flag), group=ctl)
+    return all(got)
+
+
+def guarded(fn, world: int, ctl):
+    """Run a variant on every rank; rank 0 gets its result, or the first error any rank hit."""
+    try:
+        res, err = fn(), None
+    except Exception as e:   # a variant's failure must not lose the main line
+        res, err = None, f"{type(e).__name__}: {e}"[:400]
+    if world > 1:
+        errs = [None] * world
+        torch.distributed.all_gather_object(errs, err, group=ctl)
+        err = next((e for e in errs if e), None)
+    return {"error": err} if err else res
+
+
+def explore_variant(S, rank, world, ctl):
+    """configs[3] over the N ranks on this rank's captured session (64 sessions x 16 chunks,
+    6 rewinds each, a checkpoint every 2 chunks, at most 48 held per GPU, cross-GPU restores)."""
+    from fastworld_b200 import explore
+    S.add_image("explore", seed=7, max_chunks=18)
+    res = explore.run(S, rank, world, sessions=64, chunks=16, n_rewinds=6, every=2, migrations=2,
+                      max_checkpoints=48, group=ctl, img="explore")
+    allres = [None] * world
+    torch.distributed.all_gather_object(allres, res, group=ctl)
+    return explore.summarize(allres, world, 64, 16, 6, 2, "mg2") if rank == 0 else None
+
+
+def tp14b_variant(rank, world, local, ctl):
+    """one Wan-14B-shaped session tensor-parallel over the N ranks (peer-memory
+    reductions), steady chunks replayed from captured graphs."""
+    from fastworld_b200 import tp
+    from fastworld_b200.config import WAN14B
+    res = tp.measure(WAN14B, rank, world, local, chunks=3, warmup=1, graph=True, nccl=False, group=ctl)
+    allres = [res]
+    if world > 1:
+        allres = [None] * world
+        torch.distributed.all_gather_object(allres, res, group=ctl)
+    if rank != 0:
+        return None
+    out = tp.summarize(allres, WAN14B, world, True, False, 3)
+    if out["row_parallel_step_ms"]:
+        out["row_parallel_share_of_chunk"] = (out["row_parallel_step_ms"] * out["row_parallel_steps_per_chunk"] /
+                                              out["chunk_ms_median"])
+    return out
+
+
+TP_PARITY_PATH = [("img0", ("w", "u")), ("img0", ("a", "l")), ("img0", ("q", "i")), ("img0", ("d", "j"))]
+
+
+def tp_parity_variant(rank, world, local, ctl):
+    """A tensor-parallel test model (8 heads, FFN 2048, 2 blocks, 2-chunk history) over the N
+    ranks, chunks 0-3: every rank's latent must be bit-identical; rank 0 checks the latents
+    and every rank's history heads against the CPU oracle (rel-L2)."""
+    from fastworld_b200.config import SMALL_TP
+    from fastworld_b200.prep import action_windows, synthetic_image
+    from fastworld_b200.static import B200StaticMG
+    from fastworld_b200.weights import synthetic_state_dict
+    cfg = SMALL_TP.replace(name="small_tp8", heads=8, dim=1024, ffn=2048)
+    sd = synthetic_state_dict(cfg, 0)
+    img = synthetic_image(cfg, 5, 5)
+    S = B200StaticMG(cfg, sd, device=f"cuda:{local}", tp_group=True)
+    S.add_image("img0", img)
+    outs, inputs = [], []
+    for k in range(4):
+        S._prep(TP_PARITY_PATH, k)
+        inputs.append((S.x_in.cpu(), [n.cpu() for n in S.noise]))
+        S._chunk(k == 0)
+        outs.append(S.out.cpu())
+    torch.cuda.synchronize()
+    res = {"outs": outs, "hk": [h.cpu() for h in S.hk], "status": S.device_status()}
+    del S
+    allres = [None] * world
+    torch.distributed.all_gather_object(allres, res, group=ctl)
+    if rank != 0:
+        return None
+    from oracle.mg2_oracle import Oracle
+    same = all(torch.equal(allres[0]["outs"][k], r["outs"][k]) for r in allres for k in range(4))
+    orc = Oracle(cfg, sd)
+    st = orc.new_state()
+    rel = lambda a, b: float((a.float() - b.float()).norm() / b.float().norm().clamp_min(1e-30))  # noqa: E731
+    e_out = []
+    with torch.no_grad():
+        for k in range(4):
+            s = cfg.frames * k
+            kc, gm = action_windows(cfg, TP_PARITY_PATH, k)
+            inp = {"cc": img["cond_concat"][0, :, s:s + cfg.frames].float(), "vis": img["visual_context"][0].float(),
+                   "gm": gm, "kc": kc, "k": k}
+            x_in, noise = inputs[k]
+            ref = orc.chunk(st, x_in[0].float(), [n.float() for n in noise], inp, k == 0)
+            e_out.append(rel(outs[k][0], ref))
+    hl = cfg.heads // world
+    e_hist = max(rel(allres[r]["hk"][i][0], st["hk"][i][:, r * hl:(r + 1) * hl]) for r in range(world)
+                 for i in range(cfg.layers))
+    return {"config": f"{cfg.name}: dim {cfg.dim}, {cfg.heads} heads, ffn {cfg.ffn}, {cfg.layers} blocks, "
+                      f"{cfg.hist_chunks}-chunk history", "tp": world, "chunks": 4, "ranks_identical": same,
+            "oracle_rel_l2": e_out, "history_rel_l2_max": e_hist, "bound": 1.2e-2,
+            "pass": same and max(e_out) < 1.2e-2 and e_hist < 1.2e-2,
+            "status_ok": all(r["status"][0] == 0 for r in allres)}
 
 
 def main():
@@ -325,6 +514,10 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--no-fp8", action="store_true", help="skip the e4m3 variant (configs[2])")
+    ap.add_argument("--no-tp", action="store_true", help="skip the 14B tensor-parallel variants (configs[4])")
+    ap.add_argument("--no-explore", action="store_true", help="skip the explore variant (configs[3], N > 1)")
+    ap.add_argument("--variant-budget", type=float, default=600.0,
+                    help="start no further variant once this many seconds have passed")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

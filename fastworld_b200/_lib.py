@@ -85,6 +85,9 @@ _SIGS = {
     "fw_graph_nodes": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_size_t)]),
     "fw_graph_destroy": (None, [ctypes.c_void_p]),
     "fw_peer_access": (ctypes.c_int, [ctypes.c_int]),
+    "fw_selftest_bytes": (ctypes.c_size_t, [ctypes.c_int]),
+    "fw_selftest_wait": (ctypes.c_int, [ctypes.c_int, ctypes.c_ulonglong, ctypes.c_void_p, ctypes.c_size_t,
+                                        ctypes.c_void_p, ctypes.c_void_p]),
     "fw_attention": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
                                     ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p,
                                     ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]),

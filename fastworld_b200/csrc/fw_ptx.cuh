@@ -75,16 +75,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Bounded wait for the phase of parity `parity` to complete.  Gives up (returning false)
-// after FW_WAIT_LIMIT_NS, or as soon as another thread of the CTA raised `abort`.
+// after `limit_ns` (default FW_WAIT_LIMIT_NS), or as soon as another thread of the CTA raised
+// `abort`.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* status,
-                                          int code) {
+                                          int code, uint64_t limit_ns = FW_WAIT_LIMIT_NS) {
   if (mbar_try_wait(bar, parity)) return true;
   uint64_t t0 = globaltimer();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 63u) == 0) {
       if (*abort) return false;
-      if (globaltimer() - t0 > FW_WAIT_LIMIT_NS) {
+      if (globaltimer() - t0 > limit_ns) {
         *abort = 1;
         record_status(status, code);
         return false;

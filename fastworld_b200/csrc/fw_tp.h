@@ -27,6 +27,7 @@ struct TpPeers {
   float* gat[TP_MAX_RANKS] = {};                 // [2][TP_MAX_RANKS][gat_rows][2] gathered sums of squares
   __nv_bfloat16* recv[TP_MAX_RANKS] = {};        // [2 parities] x (2 ranks: [L, D]; more: [tp][ceil(L/tp)][D]) pushed partials
   unsigned* epoch = nullptr;                     // this rank's [2][TP_MAX_CTAS] call counters
+  unsigned long long wait_ns = 2000000000ull;    // bound of every wait on another rank's flag (2 s)
 };
 
 // xs[L, D] += gate * (sum over ranks of part + bias) on every rank (two-shot over NVLink);

@@ -33,7 +33,8 @@
 // Stores of data are ordered before the flag by __syncthreads + a system-scope fence and a
 // release store; the waiter uses acquire loads.  Every wait is bounded (FW_WAIT_LIMIT_NS):
 // on timeout the CTA records DEV_TIMEOUT_PEER in the status word and carries on without the
-// missing data, so no GPU is left spinning.
+// missing data, so no GPU is left spinning.  (The limit is TpPeers::wait_ns; a self-test
+// shortens it.)
 #include "../../include/fastworld_b200.h"
 #include "fw_internal.h"
 #include "fw_ptx.cuh"
@@ -53,7 +54,8 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
 }
 
 // Threads 0..tp-1 each wait until flags[t * TP_MAX_CTAS + c] >= e; then the CTA syncs.
-__device__ __forceinline__ void wait_peers(const unsigned* flags, int tp, int c, unsigned e, int* status) {
+__device__ __forceinline__ void wait_peers(const unsigned* flags, int tp, int c, unsigned e, int* status,
+                                           uint64_t limit_ns) {
   const int t = threadIdx.x;
   if (t < tp) {
     const unsigned* f = flags + (size_t)t * TP_MAX_CTAS + c;
@@ -61,7 +63,7 @@ __device__ __forceinline__ void wait_peers(const unsigned* flags, int tp, int c,
       const uint64_t t0 = globaltimer();
       for (uint32_t i = 1;; ++i) {
         if ((int)(ld_acquire_sys(f) - e) >= 0) break;
-        if ((i & 63u) == 0 && globaltimer() - t0 > FW_WAIT_LIMIT_NS) {
+        if ((i & 63u) == 0 && globaltimer() - t0 > limit_ns) {
           record_status(status, DEV_TIMEOUT_PEER);
           break;
         }
@@ -113,7 +115,7 @@ __global__ void __launch_bounds__(512) tp_reduce2_kernel(TpPeers p, int L, int D
   const unsigned e = s_e;
   const int nv = D / 8;
   signal_peers(p, 0, c, e);
-  wait_peers(p.flags[r] + 0, 2, c, e, status);
+  wait_peers(p.flags[r] + 0, 2, c, e, status, p.wait_ns);
   constexpr int U = 4;
   const int rows_c = (L + G - 1) / G;
   const int r0 = c * rows_c, r1 = min(r0 + rows_c, L);
@@ -163,7 +165,7 @@ __global__ void __launch_bounds__(512) tp_reduce2_kernel(TpPeers p, int L, int D
   }
   __syncthreads();
   signal_peers(p, (size_t)TP_MAX_RANKS * TP_MAX_CTAS, c, e);
-  wait_peers(p.flags[r] + (size_t)TP_MAX_RANKS * TP_MAX_CTAS, 2, c, e, status);
+  wait_peers(p.flags[r] + (size_t)TP_MAX_RANKS * TP_MAX_CTAS, 2, c, e, status, p.wait_ns);
   pdl_trigger();
 }
 
@@ -190,7 +192,7 @@ __global__ void __launch_bounds__(512) tp_combine2_kernel(TpPeers p, const __nv_
   __syncthreads();
   const unsigned e = s_e;
   signal_peers(p, 0, c, e);
-  wait_peers(p.flags[r] + 0, 2, c, e, status);
+  wait_peers(p.flags[r] + 0, 2, c, e, status, p.wait_ns);
   const int nv = D / 8;
   constexpr int U = 4;
   const int rows_c = (L + G - 1) / G;
@@ -266,7 +268,7 @@ __global__ void __launch_bounds__(512) tp_reduce_kernel(TpPeers p, int L, int D,
   const int nv = D / 8;                       // 16-byte vectors per row
   // A: partials are final on this rank (the GEMM that wrote them completed before this kernel)
   signal_peers(p, 0, c, e);
-  wait_peers(p.flags[r] + 0, tp, c, e, status);
+  wait_peers(p.flags[r] + 0, tp, c, e, status, p.wait_ns);
   // 1: reduce rows chunk c of slice r, push bf16(sum + bias) to every rank.  U vectors of each
   // of the TP partials per thread per step (8 loads), all issued before any use so the NVLink
   // latency overlaps.
@@ -310,7 +312,7 @@ __global__ void __launch_bounds__(512) tp_reduce_kernel(TpPeers p, int L, int D,
   }
   __syncthreads();
   signal_peers(p, (size_t)TP_MAX_RANKS * TP_MAX_CTAS, c, e);
-  wait_peers(p.flags[r] + (size_t)TP_MAX_RANKS * TP_MAX_CTAS, tp, c, e, status);
+  wait_peers(p.flags[r] + (size_t)TP_MAX_RANKS * TP_MAX_CTAS, tp, c, e, status, p.wait_ns);
   // 2: residual update of rows chunk c of every slice from the local `red`
   constexpr int U2 = 4;
   const __nv_bfloat16* red = p.red[r];
@@ -384,7 +386,7 @@ __global__ void __launch_bounds__(256) tp_sumsq_kernel(TpPeers p, float* __restr
   __syncthreads();
   const size_t foff = (size_t)2 * TP_MAX_RANKS * TP_MAX_CTAS;
   signal_peers(p, foff, c, e);
-  wait_peers(p.flags[r] + foff, tp, c, e, status);
+  wait_peers(p.flags[r] + foff, tp, c, e, status, p.wait_ns);
   const float* g = p.gat[r] + par;
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
     float s = 0.f;

@@ -7,8 +7,8 @@ All sessions start from the same seeded image latent and diverge by seeded rando
 mouse actions.  Session i is served by rank i % N through that rank's ``PrefixCache``
 (fastworld/prefix_cache.py:35-92) over one ``B200StaticMG``: 16 chunks, a checkpoint every 2
 chunks, then 6 random rewinds (restore the deepest checkpoint before a random chunk, replay,
-and play 2 new chunks).  A final cross-GPU phase restores, on every rank, checkpoints made by
-the next rank: the owner exports the snapshot buffer by CUDA IPC and the receiver pulls it with
+and play 2 new chunks).  A final cross-GPU phase restores, on every rank, checkpoints held by
+the next rank (its most recently used ones): the owner exports the snapshot buffer by CUDA IPC and the receiver pulls it with
 the engine's copy kernel over NVLink, then plays 2 chunks from it.
 
 Reports (rank 0, one JSON line): aggregate served frames per second (max-over-ranks wall time),
@@ -78,39 +78,22 @@ def timed_ms(fn):
     return r, e0.elapsed_time(e1)
 
 
-def main():
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--sessions", type=int, default=64)
-    ap.add_argument("--chunks", type=int, default=16)
-    ap.add_argument("--rewinds", type=int, default=6)
-    ap.add_argument("--every", type=int, default=2)
-    ap.add_argument("--migrations", type=int, default=2, help="cross-GPU restores per rank")
-    ap.add_argument("--config", default="mg2")
-    a = ap.parse_args()
-    rank, world, local = (int(os.environ.get(k, d)) for k, d in (("RANK", 0), ("WORLD_SIZE", 1), ("LOCAL_RANK", 0)))
-    torch.cuda.set_device(local)
-    pg = None
-    if world > 1:
-        import datetime
-        torch.distributed.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
-        pg = torch.distributed.group.WORLD
+def run(S, rank: int, world: int, sessions: int = 64, chunks: int = 16, n_rewinds: int = 6, every: int = 2,
+        migrations: int = 2, max_checkpoints=None, group=None, img: str = "img0"):
+    """Serve this rank's share of the explore workload on session ``S`` (captured graphs) and
+    return this rank's counters and bandwidths.  Collective over ``group`` when world > 1
+    (IPC descriptors and a barrier only)."""
     from . import migrate
-    from .config import PRESETS
-    from .static import B200StaticMG
-    cfg = PRESETS[a.config]
-    S = B200StaticMG(cfg, device=f"cuda:{local}", seed=0)
-    S.add_image("img0", seed=7, max_chunks=a.chunks + 2)
-    S.capture(warmup=1)
-    cache = PrefixCache(S, NullDecoder(), every=a.every)
-    paths = make_paths(a.sessions, a.chunks, seed=1)
-    mine = sessions_of(rank, world, a.sessions)
+    cache = PrefixCache(S, NullDecoder(), every=every, max_checkpoints=max_checkpoints)
+    paths = make_paths(sessions, chunks, seed=1, img=img)
+    mine = sessions_of(rank, world, sessions)
     stats = {"generated": 0, "replayed": 0, "hit": 0, "frames": 0, "restored": 0}
-    if pg is not None:
-        torch.distributed.barrier()
+    if world > 1:
+        torch.distributed.barrier(group=group)
     torch.cuda.synchronize()
     t0 = time.time()
     for i in mine:
-        for p in [paths[i]] + rewinds(paths[i], a.rewinds, a.every, seed=1000 + i):
+        for p in [paths[i]] + rewinds(paths[i], n_rewinds, every, seed=1000 + i):
             frames, st = cache.serve(p)
             for k in ("generated", "replayed", "hit", "restored"):
                 stats[k] += st[k]
@@ -123,51 +106,78 @@ def main():
     torch.cuda.synchronize()
     _, save_ms = timed_ms(lambda: migrate.pull_local(snap.blob, S._blob))
     _, load_ms = timed_ms(lambda: S.load(snap))
-    # cross-GPU phase: restore the next rank's checkpoints here and play 2 chunks from each
+    del snap
+    # cross-GPU phase: restore checkpoints held by the next rank here and play 2 chunks from each
     mig = {"count": 0, "ms": 0.0, "bytes": 0}
     if world > 1:
-        offers = []
-        for i in mine[:a.migrations]:
-            node = cache.root
-            for key in paths[i][:a.every]:
-                node = node.children[key]
-            offers.append((i, migrate.export_blob(node.ckpt[0].blob)))
+        held = sorted(cache.pool.holders, key=lambda n: -n.slot.stamp)[:migrations]   # most recently used
+        offers = [([c.key for c in node.lineage()], migrate.export_blob(node.slot.runtime_state.blob))
+                  for node in held]
         got = [None] * world
-        torch.distributed.all_gather_object(got, offers)
+        torch.distributed.all_gather_object(got, offers, group=group)
         torch.cuda.synchronize()
         t1 = time.time()
-        for i, desc in got[(rank + 1) % world]:
+        for prefix, desc in got[(rank + 1) % world]:
             with migrate.PeerBuffer(desc, S._blob.device) as peer:
                 _, ms = timed_ms(lambda: migrate.pull(S._blob, peer))
             mig["count"] += 1
             mig["ms"] += ms
             mig["bytes"] += nbytes
-            p = paths[i][:a.every] + [("img0", ("w", "u"))] * 2
-            for k in range(a.every, a.every + 2):
+            p = list(prefix) + [(prefix[0][0], ("w", "u"))] * 2
+            for k in range(len(prefix), len(prefix) + 2):
                 S.gen_chunk(p, k)
                 stats["generated"] += 1
                 stats["frames"] += 12
         torch.cuda.synchronize()
         t_local += time.time() - t1
-        torch.distributed.barrier()   # owners keep their snapshots alive until every pull is done
-    res = {"rank": rank, "time": t_local, **stats, "save_gbs": 2 * nbytes / save_ms / 1e6,
-           "load_gbs": 2 * nbytes / load_ms / 1e6, "state_bytes": nbytes,
-           "peer_restore_gbs": (2 * mig["bytes"] / mig["ms"] / 1e6) if mig["ms"] else None,
-           "migrations": mig["count"]}
+        torch.distributed.barrier(group=group)   # owners keep their snapshots alive until every pull is done
+    return {"rank": rank, "time": t_local, **stats, "save_gbs": 2 * nbytes / save_ms / 1e6,
+            "load_gbs": 2 * nbytes / load_ms / 1e6, "state_bytes": nbytes,
+            "peer_restore_gbs": (2 * mig["bytes"] / mig["ms"] / 1e6) if mig["ms"] else None,
+            "migrations": mig["count"], "checkpoints": cache.n_ckpt, "evicted": cache.n_evicted}
+
+
+def summarize(allres, world: int, sessions: int, chunks: int, n_rewinds: int, every: int, config: str):
+    """One result over every rank: frames served / slowest rank's time, summed counters."""
+    tmax = max(r["time"] for r in allres)
+    keys = ("generated", "replayed", "hit", "frames", "restored", "migrations", "checkpoints", "evicted")
+    tot = {k: sum(r[k] for r in allres) for k in keys}
+    return {"workload": "explore (BASELINE configs[3])", "config": config, "n_gpus": world,
+            "sessions": sessions, "chunks": chunks, "rewinds_per_session": n_rewinds, "every": every,
+            "served_fps": tot["frames"] / tmax, "time_s": tmax, **tot,
+            "save_gbs": min(r["save_gbs"] for r in allres), "load_gbs": min(r["load_gbs"] for r in allres),
+            "peer_restore_gbs": min((r["peer_restore_gbs"] for r in allres if r["peer_restore_gbs"]), default=None),
+            "state_bytes": allres[0]["state_bytes"], "note": "GB/s counts read + write bytes"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--sessions", type=int, default=64)
+    ap.add_argument("--chunks", type=int, default=16)
+    ap.add_argument("--rewinds", type=int, default=6)
+    ap.add_argument("--every", type=int, default=2)
+    ap.add_argument("--migrations", type=int, default=2, help="cross-GPU restores per rank")
+    ap.add_argument("--max-checkpoints", type=int, default=None, help="checkpoints held per rank (LRU)")
+    ap.add_argument("--config", default="mg2")
+    a = ap.parse_args()
+    rank, world, local = (int(os.environ.get(k, d)) for k, d in (("RANK", 0), ("WORLD_SIZE", 1), ("LOCAL_RANK", 0)))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        torch.distributed.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
+    from .config import PRESETS
+    from .static import B200StaticMG
+    cfg = PRESETS[a.config]
+    S = B200StaticMG(cfg, device=f"cuda:{local}", seed=0)
+    S.add_image("img0", seed=7, max_chunks=a.chunks + 2)
+    S.capture(warmup=1)
+    res = run(S, rank, world, a.sessions, a.chunks, a.rewinds, a.every, a.migrations, a.max_checkpoints)
     allres = [res]
     if world > 1:
         allres = [None] * world
         torch.distributed.all_gather_object(allres, res)
     if rank == 0:
-        tmax = max(r["time"] for r in allres)
-        tot = {k: sum(r[k] for r in allres) for k in ("generated", "replayed", "hit", "frames", "restored", "migrations")}
-        line = {"workload": "explore (BASELINE configs[3])", "config": cfg.name, "n_gpus": world,
-                "sessions": a.sessions, "chunks": a.chunks, "rewinds_per_session": a.rewinds, "every": a.every,
-                "served_fps": tot["frames"] / tmax, "time_s": tmax, **tot,
-                "save_gbs": min(r["save_gbs"] for r in allres), "load_gbs": min(r["load_gbs"] for r in allres),
-                "peer_restore_gbs": min((r["peer_restore_gbs"] for r in allres if r["peer_restore_gbs"]), default=None),
-                "state_bytes": res["state_bytes"], "note": "GB/s counts read + write bytes"}
-        print(json.dumps(line), flush=True)
+        print(json.dumps(summarize(allres, world, a.sessions, a.chunks, a.rewinds, a.every, cfg.name)), flush=True)
     S.graphs = {}
     if world > 1:
         torch.distributed.destroy_process_group()

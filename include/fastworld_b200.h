@@ -191,6 +191,17 @@ void fw_graph_destroy(fw_graph* g);
  * another GPU; fastworld/prefix_cache.py:85-87 keeps every checkpoint on the GPU that made it). */
 int fw_peer_access(int peer);
 
+/* ---- failure-path self-tests (no counterpart in the reference, which has no device-side
+ * failure detection) ----
+ * Runs a bounded wait that nothing satisfies, so that it runs out after `limit_ns`
+ * (0 < limit_ns <= 2 s): which 0 = an mbarrier wait of the kind every tcgen05 kernel's warp roles
+ * use (a CTA holding TMEM; expected status DEV_TIMEOUT_TEST = 6), which 1 = the two-rank peer
+ * reduction kernel waiting for a rank that never runs (its buffers are this GPU's own memory;
+ * expected status DEV_TIMEOUT_PEER = 7).  `scratch`: fw_selftest_bytes(which) zeroed bytes,
+ * 256-byte aligned; `status`: int32[4], zeroed.  Nothing faults; the context stays usable. */
+size_t fw_selftest_bytes(int which);
+int fw_selftest_wait(int which, unsigned long long limit_ns, void* scratch, size_t bytes, int* status, void* stream);
+
 /* ---- individual kernels (used by the engine; exported for tests and reuse) ---- */
 /* C[M,N] = A[M,K] B[N,K]^T (+ bias[N]) with A, B, C bf16 row-major, fp32 accumulate.
  * epilogue: 0 = store bf16, 1 = GELU(tanh) then bf16, 3 = store fp32 (out is float*).
