@@ -506,6 +506,175 @@ def tp_parity_variant(rank, world, local, ctl):
             "status_ok": all(r["status"][0] == 0 for r in allres)}
 
 
+# ---------------------------------------------------------------- single-kernel workloads
+# Small, self-terminating runs of one kernel for ncu captures and CUDA-event timing:
+#   python bench.py --kernel gemm|gemm_resid|attn|ln|rms|copy|fp8_peak [--reps 3]
+#   python bench.py --kernel chunk [--chunks 2] [--config mg2|mg2_fp8]   (eager chunks)
+
+def chunk(n: int, config: str = "mg2") -> None:
+    from fastworld_b200 import _lib
+    from fastworld_b200.config import PRESETS
+    from fastworld_b200.static import B200StaticMG
+    S = B200StaticMG(PRESETS[config], seed=0)
+    S.add_image("img0", seed=3, max_chunks=n + 1)
+    path = [("img0", ("w", "u"))] * (n + 1)
+    for k in range(n):
+        S._prep(path, k)
+        c0 = _lib.lib().fw_launch_count()
+        S._chunk(k == 0)
+        torch.cuda.synchronize()
+        print(f"chunk {k}: {_lib.lib().fw_launch_count() - c0} launches, status {S.device_status()}")
+
+
+def gemm(reps: int) -> None:
+    from fastworld_b200 import ops
+    g = torch.Generator(device="cuda").manual_seed(0)
+    A = torch.randn(2640, 1536, device="cuda", generator=g).to(torch.bfloat16)
+    B = (torch.randn(8960, 1536, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    bias = torch.zeros(8960, device="cuda", dtype=torch.bfloat16)
+    for _ in range(reps):
+        ops.gemm(A, B, bias, "gelu_tanh")
+    torch.cuda.synchronize()
+    print("gemm ok")
+
+
+def gemm_resid(reps: int) -> None:
+    from fastworld_b200 import ops
+    g = torch.Generator(device="cuda").manual_seed(0)
+    A = torch.randn(2640, 1536, device="cuda", generator=g).to(torch.bfloat16)
+    B = (torch.randn(1536, 1536, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    bias = torch.zeros(1536, device="cuda", dtype=torch.bfloat16)
+    resid = torch.zeros(2640, 1536, device="cuda")
+    gate = torch.ones(3, 1536, device="cuda")
+    for _ in range(reps):
+        ops.gemm_resid_(resid, A, B, bias, gate, 880)
+    torch.cuda.synchronize()
+    print("gemm_resid ok")
+
+
+def attn(reps: int) -> None:
+    from fastworld_b200 import ops
+    g = torch.Generator(device="cuda").manual_seed(0)
+    r = lambda n: torch.randn(n, 12, 128, device="cuda", generator=g).to(torch.bfloat16)
+    q, k0, v0, k1, v1 = r(2640), r(2640), r(2640), r(2640), r(2640)
+    meta = torch.tensor([2640, 2640], dtype=torch.int32, device="cuda")
+    for _ in range(reps):
+        ops.attention(q, k0, v0, k1, v1, meta)
+    torch.cuda.synchronize()
+    print("attn ok")
+
+
+def fp8_peak(reps: int) -> None:
+    from fastworld_b200 import ops
+    n = 8192
+    g = torch.Generator(device="cuda").manual_seed(0)
+    a = torch.randn(n, n, device="cuda", generator=g).to(torch.bfloat16)
+    b = torch.randn(n, n, device="cuda", generator=g).to(torch.bfloat16)
+    a8, sa = ops.quant_e4m3(a)
+    b8, sw = ops.quant_e4m3(b)
+    fa, fb = a8.view(torch.float8_e4m3fn), b8.view(torch.float8_e4m3fn)
+    one = torch.ones((), device="cuda")
+
+    def best(fn, n_rep=10):
+        for _ in range(3):
+            fn()
+        t = 1e9
+        for _ in range(n_rep):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            t = min(t, e0.elapsed_time(e1))
+        return t
+    flop = 2.0 * n ** 3
+    t_lib = best(lambda: torch._scaled_mm(fa, fb.t(), one, one, out_dtype=torch.bfloat16))
+    t_ours = best(lambda: ops.gemm_e4m3(a8, sa, b8, sw, None, "none"))
+    t_bf16 = best(lambda: torch.matmul(a, b.t()))
+    print(f"e4m3 8192^3: library {flop / t_lib / 1e9:.1f} TFLOP/s, fastworld_b200 {flop / t_ours / 1e9:.1f} TFLOP/s; "
+          f"bf16 library {flop / t_bf16 / 1e9:.1f} TFLOP/s (burst, best of 10)")
+
+
+
+
+def _events_ms(fn, reps):
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps
+
+
+def _rows(n_sets, make):
+    """n_sets independent operand sets (cycled so that back-to-back launches stream from HBM once
+    their total exceeds the 126 MB L2)."""
+    return [make(i) for i in range(n_sets)]
+
+
+def ln(reps: int) -> None:
+    """norm1 / norm2 of the MG2 block: LayerNorm of the fp32 residual [2640, 1536] + adaLN
+    modulate into bf16; algorithmic bytes 16.2 MB read + 8.1 MB written."""
+    from fastworld_b200 import ops
+    M, D = 2640, 1536
+    g = torch.Generator(device="cuda").manual_seed(0)
+    sets = _rows(8, lambda i: (torch.randn(M, D, device="cuda", generator=g),
+                               torch.empty(M, D, device="cuda", dtype=torch.bfloat16)))
+    shift, scale = torch.randn(D, device="cuda", generator=g) * 0.1, torch.randn(D, device="cuda", generator=g) * 0.1
+    it = iter(range(1 << 30))
+    fn = lambda: (lambda x, o: ops.layernorm(x, 1e-6, shift=shift, scale=scale, out=o))(*sets[next(it) % 8])  # noqa
+    for _ in range(reps):
+        fn()
+    ms = _events_ms(fn, 50)
+    nb = M * D * 6
+    print(f"ln_kernel 2640x1536: {ms * 1e3:.2f} us/launch back to back over 8 sets (194 MB > L2), "
+          f"{nb / ms / 1e6:.0f} GB/s")
+
+
+def rms(reps: int) -> None:
+    """q and k RMSNorm + RoPE of the MG2 block ([2640, 1536] bf16 each, one launch);
+    algorithmic bytes 2 x (8.1 MB read + 8.1 MB written) + the RoPE table 1.35 MB."""
+    from fastworld_b200 import _lib, ops
+    from fastworld_b200._lib import check, lib, ptr, stream_ptr
+    M, D, hd = 2640, 1536, 128
+    g = torch.Generator(device="cuda").manual_seed(0)
+    sets = _rows(8, lambda i: (torch.randn(M, D, device="cuda", generator=g).bfloat16(),
+                               torch.randn(M, D, device="cuda", generator=g).bfloat16()))
+    w = (torch.rand(D, device="cuda", generator=g) + 0.5).bfloat16()
+    ang = torch.rand(M, hd // 2, device="cuda", generator=g) * 6.3
+    rope = torch.stack([ang.cos(), ang.sin()], -1).contiguous()
+    it = iter(range(1 << 30))
+
+    def fn():
+        q, k = sets[next(it) % 8]
+        ops.rms_rope(q, w, rope, hd, out=q)
+        ops.rms_rope(k, w, rope, hd, out=k)
+    for _ in range(reps):
+        fn()
+    ms = _events_ms(fn, 50) / 2
+    nb = M * D * 4
+    print(f"rms_rope8_kernel 2640x1536: {ms * 1e3:.2f} us/launch back to back over 8 sets (130 MB > L2), "
+          f"{nb / ms / 1e6:.0f} GB/s (+ rope table)")
+
+
+def copy(reps: int) -> None:
+    """Checkpoint save / restore: one copy of the 649 MB MG2 session state."""
+    from fastworld_b200 import ops
+    nb = 648990720
+    a = torch.empty(nb, dtype=torch.uint8, device="cuda")
+    b = torch.empty(nb, dtype=torch.uint8, device="cuda")
+    for _ in range(reps):
+        ops.copy_(b, a)
+    ms = _events_ms(lambda: ops.copy_(b, a), 20)
+    print(f"copy_kernel 649 MB: {ms * 1e3:.1f} us, {2 * nb / ms / 1e6:.0f} GB/s (read + write)")
+
+
+KERNELS = {"chunk": lambda a: chunk(a.chunks, a.config), "gemm": lambda a: gemm(a.reps),
+           "gemm_resid": lambda a: gemm_resid(a.reps), "attn": lambda a: attn(a.reps), "ln": lambda a: ln(a.reps),
+           "rms": lambda a: rms(a.reps), "copy": lambda a: copy(a.reps), "fp8_peak": lambda a: fp8_peak(a.reps)}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -513,12 +682,19 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--kernel", choices=sorted(KERNELS), help="run one kernel's small workload instead")
+    ap.add_argument("--reps", type=int, default=3)
+    ap.add_argument("--chunks", type=int, default=2)
+    ap.add_argument("--config", default="mg2")
     ap.add_argument("--no-fp8", action="store_true", help="skip the e4m3 variant (configs[2])")
     ap.add_argument("--no-tp", action="store_true", help="skip the 14B tensor-parallel variants (configs[4])")
     ap.add_argument("--no-explore", action="store_true", help="skip the explore variant (configs[3], N > 1)")
     ap.add_argument("--variant-budget", type=float, default=600.0,
                     help="start no further variant once this many seconds have passed")
     args = ap.parse_args()
+    if args.kernel:
+        KERNELS[args.kernel](args)
+        return
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

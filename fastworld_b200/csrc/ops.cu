@@ -204,6 +204,22 @@ int fw_gemm_bf16_resid(const void* A, const void* B, const void* bias, float* re
   return gemm_bf16_launch(ta, tb, bn, a, reinterpret_cast<cudaStream_t>(stream), 0, &tc);
 }
 
+int fw_layernorm(const float* x, int M, int D, float eps, const float* shift, const float* scale, const void* w,
+                 const void* b, void* out, void* stream) {
+  if (!x || !out || M <= 0 || D <= 0 || (!shift) != (!scale) || (!w) != (!b)) return FW_EINVAL;
+  return fw::ln_f32(x, D, M, D, eps, shift, scale, reinterpret_cast<const __nv_bfloat16*>(w),
+                    reinterpret_cast<const __nv_bfloat16*>(b), reinterpret_cast<__nv_bfloat16*>(out), D,
+                    reinterpret_cast<cudaStream_t>(stream));
+}
+
+int fw_rms_rope(const void* x, int M, int D, float eps, const void* w, const float* rope, int head_dim, void* out,
+                void* stream) {
+  if (!x || !w || !out || M <= 0 || D <= 0 || head_dim <= 0 || D % head_dim) return FW_EINVAL;
+  return fw::rms_rope2(reinterpret_cast<const __nv_bfloat16*>(x), reinterpret_cast<const __nv_bfloat16*>(w),
+                       reinterpret_cast<__nv_bfloat16*>(out), nullptr, nullptr, nullptr, D, M, D, eps,
+                       reinterpret_cast<const float2*>(rope), head_dim, D, reinterpret_cast<cudaStream_t>(stream));
+}
+
 int fw_attention(const void* q, int Lq, int heads, const void* k0, const void* v0, int max_keys0, const void* k1,
                  const void* v1, int max_keys1, const int* meta, void* out, int* status, void* stream) {
   using namespace fw;

@@ -94,3 +94,33 @@ def copy_(dst: torch.Tensor, src: torch.Tensor) -> torch.Tensor:
         raise ValueError("copy_: contiguous tensors of equal byte size required")
     check(lib().fw_copy(ptr(dst), ptr(src), nb, stream_ptr()), "copy")
     return dst
+
+
+def layernorm(x: torch.Tensor, eps: float = 1e-6, shift=None, scale=None, w=None, b=None, out=None) -> torch.Tensor:
+    """bf16 LN(x) of fp32 rows x [M, D], then * (1 + scale) + shift (fp32 [D]) or * w + b (bf16 [D])."""
+    _req(x, torch.float32, "x")
+    for n, t, d in (("shift", shift, torch.float32), ("scale", scale, torch.float32), ("w", w, torch.bfloat16),
+                    ("b", b, torch.bfloat16)):
+        if t is not None:
+            _req(t, d, n)
+    M, D = x.shape
+    out = torch.empty(M, D, device=x.device, dtype=torch.bfloat16) if out is None else out
+    _req(out, torch.bfloat16, "out")
+    check(lib().fw_layernorm(ptr(x), M, D, float(eps), ptr(shift), ptr(scale), ptr(w), ptr(b), ptr(out),
+                             stream_ptr()), "layernorm")
+    return out
+
+
+def rms_rope(x: torch.Tensor, w: torch.Tensor, rope=None, head_dim: int = 128, eps: float = 1e-6,
+             out=None) -> torch.Tensor:
+    """bf16 RMSNorm(x) * w over the full row of x [M, D], then RoPE of every head's (even, odd)
+    pairs by rope [M, head_dim // 2, 2] (cos, sin) fp32 when given."""
+    _req(x, torch.bfloat16, "x")
+    _req(w, torch.bfloat16, "w")
+    if rope is not None:
+        _req(rope, torch.float32, "rope")
+    M, D = x.shape
+    out = torch.empty_like(x) if out is None else out
+    check(lib().fw_rms_rope(ptr(x), M, D, float(eps), ptr(w), ptr(rope), head_dim, ptr(out), stream_ptr()),
+          "rms_rope")
+    return out

@@ -230,6 +230,17 @@ int fw_linear_e4m3_noalloc(const void* x, const void* w8, const float* sw, const
 /* resid[M,N] (fp32) += gate[row / rows_per_frame, N] * (A B^T + bias); gate may be NULL. */
 int fw_gemm_bf16_resid(const void* A, const void* B, const void* bias, float* resid, const float* gate,
                        int rows_per_frame, int M, int N, int K, void* stream);
+/* LayerNorm of fp32 rows x [M, D] (no affine) into bf16 out [M, D], fp32 statistics, followed by
+ * y * (1 + scale) + shift (adaLN modulate, fp32 [D] each; norm1 / norm2, static.py:206, 224) or
+ * y * w + b (bf16 [D] each; norm3, static.py:221), or neither (all four NULL). */
+int fw_layernorm(const float* x, int M, int D, float eps, const float* shift, const float* scale, const void* w,
+                 const void* b, void* out, void* stream);
+/* RMSNorm over the full row of bf16 x [M, D] times w (bf16 [D]), then, when rope != NULL, each
+ * (even, odd) pair of every head of head_dim rotated by rope[row, pair] = (cos, sin) (fp32
+ * [M, head_dim / 2, 2]); bf16 out [M, D] (may equal x).  static.py:207-212 (norm_q / norm_k,
+ * then _rope at static.py:130-133 in fp32 instead of fp64). */
+int fw_rms_rope(const void* x, int M, int D, float eps, const void* w, const float* rope, int head_dim, void* out,
+                void* stream);
 /* Non-causal attention, head_dim 128: out[Lq, H*128] = softmax(q k^T / sqrt(128)) v over the
  * keys of segment 0 then segment 1.  meta = device int32 {n_keys0, n_keys1}.  max_keys0/1
  * are the row capacities of the segment buffers. */
