@@ -13,7 +13,9 @@ Bounds: bf16 operands and activations against an fp32 oracle.  ``rel`` is the re
 error of the tensor, ``max`` its largest absolute error divided by the reference's largest
 magnitude; for the residual stream both are taken on the sub-block's update (the difference
 to the previous tap point), which is what the kernels computed.  The bounds are about three
-times the errors measured on B200.
+times the errors measured on B200 (configs[0] block: q/k/v rel-L2 2.6-3.3e-3, max 5.6-6.1e-3;
+attention 2.1e-3 / 4.2e-3; sub-block updates 2.0-3.1e-3 / 2.4-4.0e-3; block output
+1.9e-3 / 2.0e-3; the 14B-width block within 10 % of those).
 """
 import pytest
 import torch
@@ -26,8 +28,8 @@ pytestmark = pytest.mark.gpu
 
 # name: (rel-L2 bound, relative max-abs bound)
 BOUNDS = {
-    "q": (1.2e-2, 3e-2), "k": (1.2e-2, 3e-2), "v": (1.2e-2, 3e-2), "attn": (1.5e-2, 4e-2),
-    "d_sa": (1.5e-2, 4e-2), "d_ca": (1.5e-2, 4e-2), "d_ffn": (1.5e-2, 4e-2), "xs_out": (5e-3, 2e-2),
+    "q": (1e-2, 2e-2), "k": (1e-2, 2e-2), "v": (1e-2, 2e-2), "attn": (7e-3, 1.5e-2),
+    "d_sa": (7e-3, 1e-2), "d_ca": (7e-3, 1e-2), "d_ffn": (1e-2, 1.6e-2), "xs_out": (6e-3, 8e-3),
 }
 
 

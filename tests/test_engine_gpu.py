@@ -8,7 +8,8 @@ bitwise equality because the kernels differ):
   3. save -> alternative chunk -> restore -> continue is bitwise equal to the uninterrupted run;
   4. state() / load() round trip is bit-exact.
 Tolerances (bf16 GEMM operands and activations vs an fp32 oracle), about three times the
-errors measured on B200: latent and every layer's history K/V rel-L2 <= 1.2e-2, action-module
+errors measured on B200 (full-depth steady chunk: latent 2.9e-3, history K/V 3.8-4.1e-3,
+mouse state 4.8-5.1e-3 rel-L2; max-abs 7.8e-3 to 9.2e-3): latent and every layer's history K/V rel-L2 <= 1.2e-2, action-module
 state rel-L2 <= 1.5e-2; the full-depth chunk also bounds the largest absolute error (relative
 to the reference's largest magnitude) of the latent and of every layer's history K/V.
 """
@@ -24,7 +25,7 @@ pytestmark = pytest.mark.gpu
 PATH = [("img0", ("w", "u")), ("img0", ("a", "l")), ("img0", ("q", "i")), ("img0", ("d", "j")),
         ("img0", ("s", "k"))]
 TOL = {"out": 1.2e-2, "hk": 1.2e-2, "hv": 1.2e-2, "mk": 1.5e-2, "mv": 1.5e-2, "kk": 1.5e-2, "kv": 1.5e-2}
-MAXABS = {"out": 4e-2, "hk": 4e-2, "hv": 4e-2}
+MAXABS = {"out": 3e-2, "hk": 3e-2, "hv": 3e-2}
 
 
 def within(e):
