@@ -613,49 +613,61 @@ def _rows(n_sets, make):
     return [make(i) for i in range(n_sets)]
 
 
+def _graph_ms(fns, replays=20):
+    """Record the launches of ``fns`` (one per operand set) as one library-held graph and time its
+    replays with CUDA events: back-to-back launches with no host overhead between them, as inside
+    a captured chunk.  Returns ms per launch."""
+    from fastworld_b200.graph import LibGraph
+
+    def all_sets():
+        for f in fns:
+            f()
+    all_sets()
+    g = LibGraph.record(all_sets)
+    for _ in range(3):
+        g.replay()
+    return _events_ms(g.replay, replays) / len(fns)
+
+
 def ln(reps: int) -> None:
     """norm1 / norm2 of the MG2 block: LayerNorm of the fp32 residual [2640, 1536] + adaLN
-    modulate into bf16; algorithmic bytes 16.2 MB read + 8.1 MB written."""
+    modulate into bf16; algorithmic bytes 16.2 MB read + 8.1 MB written per launch."""
     from fastworld_b200 import ops
     M, D = 2640, 1536
     g = torch.Generator(device="cuda").manual_seed(0)
     sets = _rows(8, lambda i: (torch.randn(M, D, device="cuda", generator=g),
                                torch.empty(M, D, device="cuda", dtype=torch.bfloat16)))
     shift, scale = torch.randn(D, device="cuda", generator=g) * 0.1, torch.randn(D, device="cuda", generator=g) * 0.1
-    it = iter(range(1 << 30))
-    fn = lambda: (lambda x, o: ops.layernorm(x, 1e-6, shift=shift, scale=scale, out=o))(*sets[next(it) % 8])  # noqa
+    fns = [lambda x=x, o=o: ops.layernorm(x, 1e-6, shift=shift, scale=scale, out=o) for x, o in sets]
     for _ in range(reps):
-        fn()
-    ms = _events_ms(fn, 50)
+        for f in fns:
+            f()
+    torch.cuda.synchronize()
+    ms = _graph_ms(fns)
     nb = M * D * 6
-    print(f"ln_kernel 2640x1536: {ms * 1e3:.2f} us/launch back to back over 8 sets (194 MB > L2), "
-          f"{nb / ms / 1e6:.0f} GB/s")
+    print(f"ln_kernel 2640x1536: {ms * 1e3:.2f} us/launch, graph of back-to-back launches over 8 operand sets "
+          f"(194 MB > L2): {nb / ms / 1e6:.0f} GB/s")
 
 
 def rms(reps: int) -> None:
-    """q and k RMSNorm + RoPE of the MG2 block ([2640, 1536] bf16 each, one launch);
-    algorithmic bytes 2 x (8.1 MB read + 8.1 MB written) + the RoPE table 1.35 MB."""
-    from fastworld_b200 import _lib, ops
-    from fastworld_b200._lib import check, lib, ptr, stream_ptr
+    """q and k RMSNorm + RoPE of the MG2 block ([2640, 1536] bf16 each, in place, as the engine
+    runs them); algorithmic bytes 8.1 MB read + 8.1 MB written per tensor + the 1.35 MB RoPE table."""
+    from fastworld_b200 import ops
     M, D, hd = 2640, 1536, 128
     g = torch.Generator(device="cuda").manual_seed(0)
-    sets = _rows(8, lambda i: (torch.randn(M, D, device="cuda", generator=g).bfloat16(),
-                               torch.randn(M, D, device="cuda", generator=g).bfloat16()))
+    sets = _rows(8, lambda i: torch.randn(M, D, device="cuda", generator=g).bfloat16())
     w = (torch.rand(D, device="cuda", generator=g) + 0.5).bfloat16()
     ang = torch.rand(M, hd // 2, device="cuda", generator=g) * 6.3
     rope = torch.stack([ang.cos(), ang.sin()], -1).contiguous()
-    it = iter(range(1 << 30))
-
-    def fn():
-        q, k = sets[next(it) % 8]
-        ops.rms_rope(q, w, rope, hd, out=q)
-        ops.rms_rope(k, w, rope, hd, out=k)
+    fns = [lambda x=x: ops.rms_rope(x, w, rope, hd, out=x) for x in sets]
     for _ in range(reps):
-        fn()
-    ms = _events_ms(fn, 50) / 2
+        for f in fns:
+            f()
+    torch.cuda.synchronize()
+    ms = _graph_ms(fns)
     nb = M * D * 4
-    print(f"rms_rope8_kernel 2640x1536: {ms * 1e3:.2f} us/launch back to back over 8 sets (130 MB > L2), "
-          f"{nb / ms / 1e6:.0f} GB/s (+ rope table)")
+    print(f"rms_rope8_kernel 2640x1536: {ms * 1e3:.2f} us/launch, graph of back-to-back launches over 8 operand "
+          f"sets (130 MB > L2): {nb / ms / 1e6:.0f} GB/s (+ RoPE table)")
 
 
 def copy(reps: int) -> None:
