@@ -41,6 +41,15 @@ class FwTensorInfo(ctypes.Structure):
                 ("shape", ctypes.c_int64 * 5), ("bytes", ctypes.c_size_t)]
 
 
+FW_PREP_MAX_ACT = 4
+
+
+class FwPrepArgs(ctypes.Structure):
+    _fields_ = [("chunk", ctypes.c_int), ("seed", ctypes.c_ulonglong), ("draw_noise", ctypes.c_int),
+                ("cond", ctypes.c_void_p), ("cond_frames", ctypes.c_int), ("j_lo", ctypes.c_int),
+                ("n_act", ctypes.c_int), ("actions", ctypes.c_float * (FW_PREP_MAX_ACT * 8))]
+
+
 _SIGS = {
     "fw_abi_version": (ctypes.c_int, []),
     "fw_launch_count": (ctypes.c_ulonglong, []),
@@ -55,6 +64,9 @@ _SIGS = {
     "fw_forward": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]),
     "fw_destroy": (None, [ctypes.c_void_p]),
     "fw_tap_bytes": (ctypes.c_size_t, [ctypes.c_void_p]),
+    "fw_prep": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(FwPrepArgs), ctypes.c_void_p]),
+    "fw_philox4x32_10": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint), ctypes.POINTER(ctypes.c_uint),
+                                        ctypes.POINTER(ctypes.c_uint)]),
     "fw_set_tap": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t]),
     "fw_copy": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
     "fw_gemm_bf16": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,

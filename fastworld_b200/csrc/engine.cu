@@ -1018,6 +1018,18 @@ int fw_forward(fw_handle* h, int step, int first, int write, void* stream) {
   return fw::forward(h, step, first, write, x, h->den, fw::P<__nv_bfloat16>(h, "out"), nullptr, 0.f, nullptr, s);
 }
 
+int fw_prep(fw_handle* h, const fw_prep_args* args, void* stream) {
+  if (!h || !args) return FW_EINVAL;
+  if (!h->finalized) return FW_ESTATE;
+  const int n = h->cfg.n_steps;   // x_in + (n_steps - 1) renoising tensors
+  __nv_bfloat16* dst[FW_MAX_STEPS];
+  dst[0] = fw::P<__nv_bfloat16>(h, "x_in");
+  for (int i = 1; i < n; ++i) dst[i] = fw::P<__nv_bfloat16>(h, "noise." + std::to_string(i - 1));
+  return fw::prep_launch(h->cfg, *args, fw::P<int>(h, "chunk"), fw::P<__nv_bfloat16>(h, "kc"),
+                         fw::P<__nv_bfloat16>(h, "gm"), fw::P<__nv_bfloat16>(h, "cc"), dst, n, h->status,
+                         reinterpret_cast<cudaStream_t>(stream));
+}
+
 size_t fw_tap_bytes(const fw_handle* h) {
   if (!h) return 0;
   return 5 * (size_t)h->L * h->D * 4 + 4 * (size_t)h->L * h->Dl * 2;

@@ -1,5 +1,6 @@
 // Host launchers of the memory-bound kernels in elem.cu (all return 0 or a negative FW_E* code).
 #pragma once
+#include "../../include/fastworld_b200.h"
 #include "fw_internal.h"
 
 namespace fw {
@@ -82,5 +83,8 @@ int kb_attn(const __nv_bfloat16* mq, const __nv_bfloat16* wq, const float* acos_
             const __nv_bfloat16* kh, const __nv_bfloat16* vh, const __nv_bfloat16* kc, const __nv_bfloat16* vc,
             int first, __nv_bfloat16* out, int L, int S, int F, int AH, float eps, cudaStream_t s);
 int copy_bytes(void* dst, const void* src, size_t bytes, cudaStream_t s);
+// fw_prep's kernel (prep.cu): noise_dst[0] = x_in, noise_dst[t] = the noise of step t - 1.
+int prep_launch(const fw_config& c, const fw_prep_args& p, int* chunk, __nv_bfloat16* kc, __nv_bfloat16* gm,
+                __nv_bfloat16* cc, __nv_bfloat16* const* noise_dst, int n_noise, int* status, cudaStream_t s);
 
 }  // namespace fw

@@ -27,6 +27,7 @@ enum : int {
   DEV_TIMEOUT_DRAIN = 5,
   DEV_TIMEOUT_TEST = 6,
   DEV_TIMEOUT_PEER = 7,   // a tensor-parallel peer did not signal in time
+  DEV_PREP_ACTIONS = 8,   // fw_prep: the action window read a chunk whose actions were not passed
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

@@ -53,6 +53,21 @@ def action_windows(cfg, path: Sequence, k: int):
     return kc, gm
 
 
+def window_chunks(cfg, k: int) -> Tuple[int, int]:
+    """First and last chunk whose actions the action module's window at chunk k reads."""
+    r, F, pad = cfg.time_ratio, cfg.frames, cfg.pad_t
+    lo, hi = r * F * k - pad, r * F * k + cfg.kc_len - 1 - pad
+    j = lambda q: 0 if q < 0 else chunk_of_pixel_frame(q, F, r)  # noqa: E731
+    return j(lo), j(hi)
+
+
+def device_prep_actions(cfg, path: Sequence, k: int) -> Tuple[int, List[Tuple[float, ...]]]:
+    """(j_lo, per-chunk action vectors) that ``fw_prep`` needs for chunk k: keyboard then mouse
+    values of chunks j_lo .. (the last chunk the window reads)."""
+    lo, hi = window_chunks(cfg, k)
+    return lo, [_vec(KEYS, path[j][1][0]) + _vec(CAM, path[j][1][1]) for j in range(lo, hi + 1)]
+
+
 def synthetic_image(cfg, seed: int, max_chunks: int = 24, device="cpu") -> Dict[str, torch.Tensor]:
     """A seeded stand-in for ``Model.add_image`` (model.py:53-68): ``cond_concat`` = 4 mask
     channels (1 on the first latent frame) + 16 N(0,1) latent channels, ``visual_context`` =

@@ -26,7 +26,7 @@ import torch
 from . import _lib, graph as fw_graph
 from ._lib import check, lib, ptr, stream_ptr
 from .config import MG2, DiTConfig
-from .prep import action_windows, path_seed, synthetic_image
+from .prep import action_windows, device_prep_actions, path_seed, synthetic_image
 
 _DT = {_lib.DT_BF16: torch.bfloat16, _lib.DT_F32: torch.float32, _lib.DT_I32: torch.int32, _lib.DT_U8: torch.uint8}
 
@@ -68,9 +68,10 @@ class B200StaticMG:
     every rank; the output latent is identical on all ranks."""
 
     def __init__(self, cfg: DiTConfig = MG2, weights: Optional[Dict[str, torch.Tensor]] = None, device="cuda",
-                 seed: int = 0, tp_group=None, tp_peers: bool = True):
+                 seed: int = 0, tp_group=None, tp_peers: bool = True, device_prep: bool = False):
         cfg.validate()
         self.cfg = cfg
+        self.device_prep = bool(device_prep)
         self.dev = torch.device(device)
         if self.dev.type != "cuda":
             raise RuntimeError("B200StaticMG runs on a CUDA device (sm_100a) only")
@@ -201,7 +202,13 @@ class B200StaticMG:
 
     # ------------------------------------------------------------------ inputs
     def _prep(self, path: Sequence, k: int, noise: bool = True) -> None:
-        """Fill the static inputs for chunk k of `path` (static.py:76-127)."""
+        """Fill the static inputs for chunk k of `path` (static.py:76-127).  With
+        ``device_prep`` set, one library kernel does it (``fw_prep``: no host copy, no torch
+        kernel; the noise then comes from the library's counter-based generator instead of
+        torch.randn, so it differs from the reference's stream); otherwise the host path
+        reproduces the reference's inputs exactly."""
+        if self.device_prep:
+            return self._prep_device(path, k, noise)
         c = self.cfg
         img_name = path[0][0]
         img = self.images[img_name]
@@ -220,6 +227,26 @@ class B200StaticMG:
         self.x_in.copy_(torch.randn(self.x_in.shape, generator=g, device=self.dev, dtype=torch.bfloat16))
         for nb in self.noise:
             nb.copy_(torch.randn(nb.shape, generator=g, device=self.dev, dtype=torch.bfloat16))
+
+    def _prep_device(self, path: Sequence, k: int, noise: bool = True) -> None:
+        c = self.cfg
+        img_name = path[0][0]
+        img = self.images[img_name]
+        if self.cur_img != img_name:
+            vis = img["visual_context"]
+            check(lib().fw_copy(ptr(self.vis), ptr(vis), vis.numel() * 2, stream_ptr()), "fw_copy(vis)")
+            self.cur_img = img_name
+        cond = img["cond_concat"]
+        j_lo, acts = device_prep_actions(c, path, k)
+        if len(acts) > _lib.FW_PREP_MAX_ACT:
+            raise ValueError(f"action window spans {len(acts)} chunks (at most {_lib.FW_PREP_MAX_ACT})")
+        a = _lib.FwPrepArgs()
+        a.chunk, a.seed, a.draw_noise = k, path_seed(path[:k + 1]), int(bool(noise))
+        a.cond, a.cond_frames, a.j_lo, a.n_act = ptr(cond), cond.shape[2], j_lo, len(acts)
+        for j, v in enumerate(acts):
+            for d, x in enumerate(v):
+                a.actions[8 * j + d] = float(x)
+        check(lib().fw_prep(self._h, ctypes.byref(a), stream_ptr()), "fw_prep")
 
     # ------------------------------------------------------------------ network
     def _chunk(self, first: bool) -> None:

@@ -124,6 +124,28 @@ int fw_forward(fw_handle* h, int step, int first, int write, void* stream);
  * that captured this handle's launches first). */
 void fw_destroy(fw_handle* h);
 
+/* Chunk preparation on the device (StaticMG._prep, static.py:76-127), one launch that reads no
+ * host memory: writes the chunk info {k, frames * k}, the action module's keyboard / mouse
+ * windows (kc, gm), the image condition slice cc = cond[:, frames * k : frames * (k + 1)] and,
+ * with draw_noise, x_in and the per-step renoising noise as N(0, 1) bf16 from Philox-4x32-10
+ * keyed by `seed` (a different stream from the reference's torch.randn; see prep.cu).
+ * actions: chunks j_lo .. j_lo + n_act - 1, 8 floats each (keyboard then mouse values); they
+ * must cover every chunk the window reads (else status DEV_PREP_ACTIONS = 8, zeros written).
+ * cond: bf16 [cond_ch, cond_frames, H, W] on the device, cond_frames >= frames * (chunk + 1). */
+#define FW_PREP_MAX_ACT 4
+typedef struct fw_prep_args {
+  int chunk;
+  unsigned long long seed;
+  int draw_noise;
+  const void* cond;
+  int cond_frames;
+  int j_lo, n_act;
+  float actions[FW_PREP_MAX_ACT * 8];
+} fw_prep_args;
+int fw_prep(fw_handle* h, const fw_prep_args* args, void* stream);
+/* Philox-4x32-10 of one counter under one key (host function; the generator fw_prep uses). */
+int fw_philox4x32_10(const unsigned* counter4, const unsigned* key2, unsigned* out4);
+
 /* Parity tap (the reference's exactness ladder compares one forward layer by layer,
  * scripts/mg2/test_static.py:50-57): while set, every forward copies block `layer`'s
  * intermediates into `buf` (fw_tap_bytes(h) bytes, 16-byte aligned):
