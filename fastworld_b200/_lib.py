@@ -153,9 +153,10 @@ def make_config(cfg, tp_size: int = 1, tp_rank: int = 0) -> FwConfig:
     for i, t in enumerate(cfg.steps):
         c.steps[i] = float(t)
     c.eps, c.eps_ln, c.rope_theta = float(cfg.eps), 1e-5, float(cfg.rope_theta)
-    if cfg.linear not in ("bf16", "fp8"):
+    modes = {"bf16": 0, "fp8": 1, "fp8_ffn": 2}
+    if cfg.linear not in modes:
         raise ValueError(f"linear dtype {cfg.linear!r}")
-    c.linear_fp8 = int(cfg.linear == "fp8")
+    c.linear_fp8 = modes[cfg.linear]
     c.hist_chunks = int(cfg.hist_chunks)
     c.tp_size, c.tp_rank = int(tp_size), int(tp_rank)
     return c

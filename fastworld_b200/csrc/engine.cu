@@ -81,6 +81,7 @@ struct fw_handle {
       *ctx_o, *ctx, *ckv, *kbK, *kbV;
   int* consts;
   bool fp8 = false;         // e4m3 block linears (per-channel weight / per-token activation scales)
+  bool fp8_ffn_only = false;  // ... only the FFN linears (ffn.0, ffn.2); the others stay bf16
   uint8_t* a8 = nullptr;    // e4m3 operand of the next block linear
   float* sa = nullptr;      // its per-row scales
   int* status;
@@ -218,12 +219,13 @@ static int register_tensors(fw_handle* h) {
     };
     for (int i = 0; i < c.layers; ++i) {
       const std::string p = "b" + std::to_string(i) + ".";
+      der(p + "ffn.0", FFl, D);
+      der(p + "ffn.2", D, FFl);
+      if (h->fp8_ffn_only) continue;
       der(p + "sa.qkv", 3 * Dl, D);
       der(p + "sa.o", D, Dl);
       der(p + "ca.q", Dl, D);
       der(p + "ca.o", D, Dl);
-      der(p + "ffn.0", FFl, D);
-      der(p + "ffn.2", D, FFl);
       if (h->layers[i].act >= 0) {
         const std::string a = p + "am.";
         der(a + "mlp1", h->Mh, D);
@@ -340,6 +342,7 @@ static int config_check(const fw_config& c) {
   for (int i = 0; i < c.n_action; ++i)
     if (c.action_blocks[i] < 0 || c.action_blocks[i] >= c.layers) return FW_EINVAL;
   if (c.hist_chunks < 1 || c.tp_size < 1 || c.tp_rank < 0 || c.tp_rank >= c.tp_size) return FW_EINVAL;
+  if (c.linear_fp8 < 0 || c.linear_fp8 > 2) return FW_EINVAL;
   if (c.tp_size > 1) {   // whole heads and 32-column FFN shards per rank; no action module
     if (c.heads % c.tp_size || c.ffn % (32 * c.tp_size) || c.n_action) return FW_ESHAPE;
   }
@@ -445,7 +448,8 @@ static int run(const AttnOp& op, cudaStream_t s) { return attention_launch(op.q,
 
 static int make_lin(fw_handle* h, GemmOp& op, const std::string& wname, const void* A, int lda, int M, int K, int N,
                     int ldb, int bn, const GemmEpi& epi) {
-  if (!h->fp8) return make_gemm(op, A, M, K, lda, W(h, wname + ".w"), N, ldb, bn, epi, h->status);
+  if (!h->fp8 || !ptr_of(h, wname + ".q8")) return make_gemm(op, A, M, K, lda, W(h, wname + ".w"), N, ldb, bn, epi,
+                                                            h->status);
   op.bn = bn;
   FW_TRY(make_tmap_2d(&op.a, h->a8, 1, M, K, K, 128, 128, true));
   FW_TRY(make_tmap_2d(&op.b, P<uint8_t>(h, wname + ".q8"), 1, N, K, K, bn, 128, true));
@@ -464,14 +468,16 @@ static int make_lin(fw_handle* h, GemmOp& op, const std::string& wname, const vo
 // The operand of an e4m3 GEMM is quantised from `src` (bf16 [M, ld]) with per-token scales;
 // in bf16 mode the GEMM reads `src` directly and this only launches the GEMM.
 static int run_from(fw_handle* h, const GemmOp& op, const __nv_bfloat16* src, int ld, cudaStream_t s) {
-  if (h->fp8) FW_TRY(quant_rows(src, ld, op.args.M, op.args.K, h->a8, op.args.K, h->sa, s));
+  if (op.args.sa) FW_TRY(quant_rows(src, ld, op.args.M, op.args.K, h->a8, op.args.K, h->sa, s));
   return run(op, s);
 }
 
 // LayerNorm of the fp32 residual into the next GEMM's operand (bf16 y, or e4m3 a8 + scales).
-static int ln_op(fw_handle* h, int M, int D, float eps, const float* shift, const float* scale,
-                 const __nv_bfloat16* w, const __nv_bfloat16* b, cudaStream_t s) {
-  if (h->fp8) return ln_f32_q8(h->xs, D, M, D, eps, shift, scale, w, b, h->a8, h->sa, D, s);
+// `consumer` is the GEMM that reads the normalised rows: e4m3 (a8 + per-row scales) when it is
+// an e4m3 linear, bf16 (y) otherwise.
+static int ln_op(fw_handle* h, const GemmOp& consumer, int M, int D, float eps, const float* shift,
+                 const float* scale, const __nv_bfloat16* w, const __nv_bfloat16* b, cudaStream_t s) {
+  if (consumer.args.sa) return ln_f32_q8(h->xs, D, M, D, eps, shift, scale, w, b, h->a8, h->sa, D, s);
   return ln_f32(h->xs, D, M, D, eps, shift, scale, w, b, h->y, D, s);
 }
 
@@ -772,7 +778,7 @@ static int action(fw_handle* h, int i, int first, int write, cudaStream_t s) {
                             W(h, a + "mlp1.b"), Mh, c.mouse_dim * h->PAD, ACT_NONE, ACT_NONE, h->fbias, nullptr, Mh, s));
   FW_TRY(run_from(h, ly.mlp1, h->xbf, D, s));
   FW_TRY(run_from(h, ly.mlp2, h->hb, Mh, s));
-  if (h->fp8)
+  if (ly.tqkv.args.sa)
     FW_TRY(ln_bf16_q8(h->hb2, Mh, h->L, Mh, c.eps_ln, nullptr, nullptr, W(h, a + "mln.w"), W(h, a + "mln.b"), h->a8,
                       h->sa, Mh, s));
   else
@@ -830,7 +836,7 @@ static int forward(fw_handle* h, int step, int first, int write, const __nv_bflo
       return tap ? copy_bytes(h->tap + 5 * xs_b + slot * qb, src, qb, s) : 0;
     };
     FW_TRY(tap_xs(0));
-    FW_TRY(ln_op(h, L, D, c.eps, ee + 0 * D, ee + 1 * D, nullptr, nullptr, s));
+    FW_TRY(ln_op(h, ly.qkv, L, D, c.eps, ee + 0 * D, ee + 1 * D, nullptr, nullptr, s));
     FW_TRY(run(ly.qkv, s));
     FW_TRY(rms_norm_op(h, h->q, h->kcur, W(h, p + "sa.nq.w"), W(h, p + "sa.nk.w"), L, rope, s));
     FW_TRY(tap_bf(0, h->q));
@@ -853,7 +859,7 @@ static int forward(fw_handle* h, int step, int first, int write, const __nv_bflo
     FW_TRY(run_from(h, ly.o, h->ao, Dl, s));
     FW_TRY(row_parallel_done(h, p + "sa.o.b", ee + 2 * D, nullptr, (3 * i) & 1, s));
     FW_TRY(tap_xs(1));
-    FW_TRY(ln_op(h, L, D, c.eps, nullptr, nullptr, W(h, p + "n3.w"), W(h, p + "n3.b"), s));
+    FW_TRY(ln_op(h, ly.caq, L, D, c.eps, nullptr, nullptr, W(h, p + "n3.w"), W(h, p + "n3.b"), s));
     FW_TRY(run(ly.caq, s));
     FW_TRY(rms_norm_op(h, h->q, nullptr, W(h, p + "ca.nq.w"), nullptr, L, nullptr, s));
     FW_TRY(run(ly.cross, s));
@@ -862,7 +868,7 @@ static int forward(fw_handle* h, int step, int first, int write, const __nv_bflo
     FW_TRY(tap_xs(2));
     if (ly.act >= 0) FW_TRY(action(h, i, first, write, s));
     FW_TRY(tap_xs(3));
-    FW_TRY(ln_op(h, L, D, c.eps, ee + 3 * D, ee + 4 * D, nullptr, nullptr, s));
+    FW_TRY(ln_op(h, ly.ff0, L, D, c.eps, ee + 3 * D, ee + 4 * D, nullptr, nullptr, s));
     FW_TRY(run(ly.ff0, s));
     FW_TRY(run_from(h, ly.ff2, h->hb, h->FFl, s));
     FW_TRY(row_parallel_done(h, p + "ffn.2.b", ee + 5 * D, nullptr, (3 * i + 2) & 1, s));
@@ -945,6 +951,7 @@ int fw_create(const fw_config* cfg, fw_handle** out) {
   h->KC = c.frames * c.time_ratio + h->PAD - 3;
   h->lat_elems = (size_t)c.lat_ch * c.frames * c.lat_h * c.lat_w;
   h->fp8 = c.linear_fp8 != 0;
+  h->fp8_ffn_only = c.linear_fp8 == 2;
   h->tp = c.tp_size;
   h->tpr = c.tp_rank;
   h->hc = c.hist_chunks;
@@ -1095,7 +1102,7 @@ int fw_tp_peers(fw_handle* h, void* const* ws_bases, int n) {
   // each rank's slice into that rank's recv slot (reduce-scatter), so the reduction kernels
   // read the partials from local memory.
   const char* pe = getenv("FW_TP_PUSH");
-  if (!(pe && pe[0] == '0') && !h->fp8) {
+  if (!(pe && pe[0] == '0') && !h->fp8) {   // (the e4m3 row-parallel GEMMs do not push)
     const int Ls = (h->L + h->tp - 1) / h->tp;
     const size_t LD = (size_t)h->L * h->D;
     h->recv_stride = (size_t)h->tp * Ls * h->D;

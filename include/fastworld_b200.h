@@ -77,7 +77,8 @@ typedef struct fw_config {
   float eps;                                          /* block LayerNorm / RMSNorm eps */
   float eps_ln;                                       /* img_emb / mouse_mlp LayerNorm eps */
   float rope_theta;
-  int linear_fp8;                                     /* 1: block linears in e4m3 */
+  int linear_fp8;                                     /* 1: block linears in e4m3;
+                                                         2: only the FFN linears in e4m3 */
   /* KV history window in chunks (1 = MG2: the previous chunk only).  With W > 1 the history
    * buffer holds W chunk slots; chunk k's context forward writes slot k % W and a steady
    * chunk attends to the min(k, W) filled slots and the current chunk. */

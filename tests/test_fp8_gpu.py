@@ -2,11 +2,16 @@
 
 * the row quantiser matches torch's float8_e4m3fn conversion of x / (absmax / 448) bit for bit;
 * the e4m3 GEMM matches an fp32 reference of the same dequantised operands (rel-L2 <= 6e-3);
-* a whole chunk with e4m3 block linears against the bf16 engine on the same weights and inputs,
-  chunk 0 and a steady chunk.  BASELINE asks for rel-L2 <= 2e-2; per-token / per-channel e4m3
-  quantisation adds ~3-4 % rel-L2 noise to every GEMM output (3 mantissa bits), which compounds
-  to 3.9e-2 at this 2-layer config and 5.8-6.5e-2 at the 30-layer MG2 config (measured on a
-  B200), so the asserted bound is 5e-2 here and the gap to the target is reported, not hidden.
+* the engine with e4m3 FFN linears ("fp8_ffn": ffn.0 and ffn.2, 65 % of the block's GEMM
+  flops) against the bf16 engine on the same weights and inputs: latent and every layer's
+  history K/V within BASELINE's rel-L2 <= 2e-2, at MG2 width (2 layers) and at full depth
+  (30 layers), chunk 0 and a steady chunk;
+* the engine with every block linear in e4m3 ("fp8"): rel-L2 is bounded at the measured level
+  (3.9e-2 at 2 layers); BASELINE's 2e-2 is not met and is kept as a strict expected failure.
+  E4m3 has 3 mantissa bits: rounding both operands adds 3.3-3.8 % rel-L2 to every GEMM output
+  whatever the scale granularity (per token / per channel, 1 x 128 or 1 x 32 blocks, measured
+  on the CPU), and the attention-side and action-module linears carry that noise into the
+  latent (5.0e-2 at 30 layers on the CPU emulation, 5.8-6.5e-2 measured on a B200).
 """
 import math
 
@@ -53,21 +58,56 @@ def test_gemm_e4m3(M, N, K, tile):
     assert float((out.float() - full).norm() / full.norm()) < 6e-2
 
 
-def test_engine_fp8_close_to_bf16():
-    from fastworld_b200.config import SMALL
+def fp8_vs_bf16(cfg, linear, chunks=2, seed=3):
+    """Latent and per-layer history K/V rel-L2 of the e4m3 engine against the bf16 engine."""
     from fastworld_b200.prep import synthetic_image
     from fastworld_b200.static import B200StaticMG
     from fastworld_b200.weights import synthetic_state_dict
-    sd = synthetic_state_dict(SMALL, 3)
-    img = synthetic_image(SMALL, 4, 4)
-    path = [("img0", ("w", "u")), ("img0", ("a", "l"))]
-    outs = {}
-    for lin in ("bf16", "fp8"):
-        S = B200StaticMG(SMALL.replace(linear=lin), sd)
+    sd = synthetic_state_dict(cfg, seed)
+    img = synthetic_image(cfg, 4, chunks + 1)
+    path = [("img0", ("w", "u")), ("img0", ("a", "l")), ("img0", ("d", "i"))][:chunks]
+    runs = {}
+    for lin in ("bf16", linear):
+        S = B200StaticMG(cfg.replace(linear=lin), sd)
         S.add_image("img0", img)
-        outs[lin] = [S.gen_chunk(path, k, graph=False).float() for k in range(2)]
+        outs = []
+        for k in range(chunks):
+            outs.append((S.gen_chunk(path, k, graph=False).float().cpu(), [h.float().cpu() for h in S.hk],
+                         [v.float().cpu() for v in S.hv]))
         assert S.device_status()[0] == 0
-    for a, b in zip(outs["fp8"], outs["bf16"]):
-        err = float((a - b).norm() / b.norm())
-        print("fp8 vs bf16 rel-L2", err)
-        assert err < 5e-2
+        runs[lin] = outs
+        del S
+        torch.cuda.empty_cache()
+    rel = lambda a, b: float((a - b).norm() / b.norm())  # noqa: E731
+    errs = []
+    for (o8, k8, v8), (o, k, v) in zip(runs[linear], runs["bf16"]):
+        errs.append({"out": rel(o8, o), "hk": max(rel(a, b) for a, b in zip(k8, k)),
+                     "hv": max(rel(a, b) for a, b in zip(v8, v))})
+    print(cfg.name, linear, errs)
+    return errs
+
+
+def test_engine_fp8_ffn_meets_2e2_mg2_width():
+    from fastworld_b200.config import MG2
+    for e in fp8_vs_bf16(MG2.replace(name="mg2_2l", layers=2, action_blocks=(1,)), "fp8_ffn"):
+        assert max(e.values()) <= 2e-2, e
+
+
+def test_engine_fp8_ffn_meets_2e2_full_depth():
+    from fastworld_b200.config import MG2
+    for e in fp8_vs_bf16(MG2, "fp8_ffn"):
+        assert max(e.values()) <= 2e-2, e
+
+
+def test_engine_fp8_all_linears_measured_bound():
+    from fastworld_b200.config import SMALL
+    for e in fp8_vs_bf16(SMALL, "fp8"):
+        assert e["out"] < 5e-2, e
+
+
+@pytest.mark.xfail(strict=True, reason="every block linear in e4m3: 3-4 % rounding noise per GEMM; the "
+                                      "latent differs from bf16 by 4-6.5e-2, above BASELINE's 2e-2")
+def test_engine_fp8_all_linears_2e2_target():
+    from fastworld_b200.config import MG2
+    for e in fp8_vs_bf16(MG2.replace(name="mg2_2l", layers=2, action_blocks=(1,)), "fp8"):
+        assert max(e.values()) <= 2e-2, e
