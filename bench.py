@@ -652,6 +652,26 @@ def ln(reps: int) -> None:
           f"(194 MB > L2): {nb / ms / 1e6:.0f} GB/s")
 
 
+def ln14(reps: int) -> None:
+    """norm1 / norm2 of the Wan-14B block: LayerNorm of the fp32 residual [4680, 5120] + adaLN
+    modulate into bf16 (four warps per row); algorithmic bytes 95.8 MB read + 47.9 MB written."""
+    from fastworld_b200 import ops
+    M, D = 4680, 5120
+    g = torch.Generator(device="cuda").manual_seed(0)
+    sets = _rows(2, lambda i: (torch.randn(M, D, device="cuda", generator=g),
+                               torch.empty(M, D, device="cuda", dtype=torch.bfloat16)))
+    shift, scale = torch.randn(D, device="cuda", generator=g) * 0.1, torch.randn(D, device="cuda", generator=g) * 0.1
+    fns = [lambda x=x, o=o: ops.layernorm(x, 1e-6, shift=shift, scale=scale, out=o) for x, o in sets]
+    for _ in range(reps):
+        for f in fns:
+            f()
+    torch.cuda.synchronize()
+    ms = _graph_ms(fns)
+    nb = M * D * 6
+    print(f"ln_wide_kernel 4680x5120: {ms * 1e3:.2f} us/launch, graph of back-to-back launches over 2 operand sets "
+          f"(288 MB > L2): {nb / ms / 1e6:.0f} GB/s")
+
+
 def rms(reps: int) -> None:
     """q and k RMSNorm + RoPE of the MG2 block ([2640, 1536] bf16 each, in place, as the engine
     runs them); algorithmic bytes 8.1 MB read + 8.1 MB written per tensor + the 1.35 MB RoPE table."""
@@ -686,7 +706,7 @@ def copy(reps: int) -> None:
 
 
 KERNELS = {"chunk": lambda a: chunk(a.chunks, a.config), "gemm": lambda a: gemm(a.reps),
-           "gemm_resid": lambda a: gemm_resid(a.reps), "attn": lambda a: attn(a.reps), "ln": lambda a: ln(a.reps),
+           "gemm_resid": lambda a: gemm_resid(a.reps), "attn": lambda a: attn(a.reps), "ln": lambda a: ln(a.reps), "ln14": lambda a: ln14(a.reps),
            "rms": lambda a: rms(a.reps), "copy": lambda a: copy(a.reps), "fp8_peak": lambda a: fp8_peak(a.reps)}
 
 

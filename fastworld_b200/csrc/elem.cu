@@ -174,28 +174,31 @@ __device__ __forceinline__ void load8(const __nv_bfloat16* p, float (&v)[8]) {
   }
 }
 
-// LayerNorm with eight consecutive elements per lane: fp32 rows are read as two 16-byte loads per
-// 256-column group and the bf16 row is written with one 16-byte store per group (each warp store
-// covers 512 contiguous bytes), half the memory instructions of ln_kernel.  A row is shared by
-// WPR warps (WPR > 1 for wide rows, so that no lane holds more than 48 values: D = 5120 uses 4
-// warps of 1280 columns), whose partial sums meet in shared memory.  D = 256 * NG8 * WPR.
-template <typename Tin, int NG8, int WPR>
-__global__ void __launch_bounds__(256, 3) ln8_kernel(const Tin* __restrict__ x, int ldx, int M, float eps,
-                                                  const float* __restrict__ shift, const float* __restrict__ scale,
-                                                  const __nv_bfloat16* __restrict__ w,
-                                                  const __nv_bfloat16* __restrict__ b, __nv_bfloat16* __restrict__ out,
-                                                  int ldo, uint8_t* __restrict__ out8, float* __restrict__ sa) {
+// LayerNorm of wide rows (D = 1024 * NG): a row is shared by four warps of D / 4 columns each,
+// so that no lane holds more than 40 values (one warp per row, as ln_kernel does, spills for
+// D = 5120); the four warps' partial sums meet in shared memory.  Lane l of a warp reads, in each
+// 256-column group of its part, the 16-byte chunks at columns l * 4 and 128 + l * 4 (two fully
+// coalesced 512-byte requests per warp) and writes its bf16 results at the same columns.  Same
+// arithmetic as ln_kernel.
+template <typename Tin, int NG>
+__global__ void __launch_bounds__(256, 3) ln_wide_kernel(const Tin* __restrict__ x, int ldx, int M, float eps,
+                                                      const float* __restrict__ shift, const float* __restrict__ scale,
+                                                      const __nv_bfloat16* __restrict__ w,
+                                                      const __nv_bfloat16* __restrict__ b,
+                                                      __nv_bfloat16* __restrict__ out, int ldo) {
   pdl_trigger();
   pdl_wait();
-  constexpr int ROWS = 8 / WPR, D = 256 * NG8 * WPR;
+  constexpr int WPR = 4, ROWS = 8 / WPR, D = 1024 * NG;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x * ROWS + warp / WPR, part = warp % WPR;
   const bool live = row < M;
-  const int c0 = part * 256 * NG8 + lane * 8;   // this lane's first column
-  float v[NG8][8];
+  const int base = part * 256 * NG + lane * 4;   // + g * 256 + h * 128
+  float v[NG][2][4];
   if (live) {
 #pragma unroll
-    for (int g = 0; g < NG8; ++g) load8(x + (size_t)row * ldx + c0 + g * 256, v[g]);
+    for (int g = 0; g < NG; ++g)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) load4(x + (size_t)row * ldx + base + g * 256 + h * 128, v[g][h]);
   }
   // per-column vectors staged in shared memory while the row loads are in flight
   const bool staged = (scale != nullptr) != (w != nullptr);
@@ -217,10 +220,8 @@ __global__ void __launch_bounds__(256, 3) ln8_kernel(const Tin* __restrict__ x, 
       s_b[i] = make_float4(b4[0], b4[1], b4[2], b4[3]);
     }
   }
-  // row statistics (rows shared by WPR warps combine their partial sums in shared memory)
-  auto row_sum = [&](float t, int k) {
+  auto row_sum = [&](float t, int k) {   // every thread of the block calls this
     t = warp_sum(t);
-    if (WPR == 1) return t;
     if (lane == 0) s_red[k][warp] = t;
     __syncthreads();
     float r = 0.f;
@@ -231,75 +232,55 @@ __global__ void __launch_bounds__(256, 3) ln8_kernel(const Tin* __restrict__ x, 
   float s = 0.f;
   if (live) {
 #pragma unroll
-    for (int g = 0; g < NG8; ++g)
+    for (int g = 0; g < NG; ++g)
 #pragma unroll
-      for (int i = 0; i < 8; ++i) s += v[g][i];
+      for (int i = 0; i < 8; ++i) s += v[g][i >> 2][i & 3];
   }
   const float mean = row_sum(s, 0) * (1.f / D);
   float q = 0.f;
   if (live) {
 #pragma unroll
-    for (int g = 0; g < NG8; ++g)
+    for (int g = 0; g < NG; ++g)
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        const float d = v[g][i] - mean;
+        const float d = v[g][i >> 2][i & 3] - mean;
         q += d * d;
       }
   }
   const float rstd = rsqrtf(row_sum(q, 1) * (1.f / D) + eps);
-  if (staged && WPR == 1) __syncthreads();   // (WPR > 1: the reductions above synchronised)
   if (!live) return;
-  float amax = 0.f;
 #pragma unroll
-  for (int g = 0; g < NG8; ++g) {
-    const int c = c0 + g * 256;
-    float* y = v[g];
+  for (int g = 0; g < NG; ++g)
 #pragma unroll
-    for (int i = 0; i < 8; ++i) y[i] = (y[i] - mean) * rstd;
-    if (staged) {   // y * (1 + scale) + shift, or y * w + b
+    for (int h = 0; h < 2; ++h) {
+      const int c = base + g * 256 + h * 128;
+      float(&y)[4] = v[g][h];
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const float4 A = s_a[c / 4 + h], B = s_b[c / 4 + h];
-        y[4 * h + 0] = y[4 * h + 0] * A.x + B.x;
-        y[4 * h + 1] = y[4 * h + 1] * A.y + B.y;
-        y[4 * h + 2] = y[4 * h + 2] * A.z + B.z;
-        y[4 * h + 3] = y[4 * h + 3] * A.w + B.w;
+      for (int i = 0; i < 4; ++i) y[i] = (y[i] - mean) * rstd;
+      if (staged) {   // y * (1 + scale) + shift, or y * w + b
+        const float4 A = s_a[c / 4], B = s_b[c / 4];
+        y[0] = y[0] * A.x + B.x;
+        y[1] = y[1] * A.y + B.y;
+        y[2] = y[2] * A.z + B.z;
+        y[3] = y[3] * A.w + B.w;
+      } else {
+        if (w) {
+          float wv[4], bv[4];
+          load4(w + c, wv);
+          load4(b + c, bv);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) y[i] = y[i] * wv[i] + bv[i];
+        }
+        if (scale) {
+          float sc[4], sh[4];
+          load4(scale + c, sc);
+          load4(shift + c, sh);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) y[i] = y[i] * (1.f + sc[i]) + sh[i];
+        }
       }
-    } else {
-      if (w) {
-        float wv[8], bv[8];
-        load8(w + c, wv);
-        load8(b + c, bv);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) y[i] = y[i] * wv[i] + bv[i];
-      }
-      if (scale) {
-        float sc[8], sh[8];
-        load8(scale + c, sc);
-        load8(shift + c, sh);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) y[i] = y[i] * (1.f + sc[i]) + sh[i];
-      }
+      store4(out + (size_t)row * ldo + c, y);
     }
-    if (out8) {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(y[i]));
-    } else {
-      *reinterpret_cast<uint4*>(out + (size_t)row * ldo + c) =
-          make_uint4(pack_bf16(y[0], y[1]), pack_bf16(y[2], y[3]), pack_bf16(y[4], y[5]), pack_bf16(y[6], y[7]));
-    }
-  }
-  if (out8) {   // e4m3 output with a per-row scale absmax / 448 (one warp per row only)
-    amax = warp_max(amax);
-    const float sc = amax > 0.f ? amax * (1.f / 448.f) : 1.f;
-    const float inv = 1.f / sc;
-#pragma unroll
-    for (int g = 0; g < NG8; ++g)
-      *reinterpret_cast<uint2*>(out8 + (size_t)row * ldo + c0 + g * 256) =
-          make_uint2(pack4_e4m3(v[g][0], v[g][1], v[g][2], v[g][3], inv),
-                     pack4_e4m3(v[g][4], v[g][5], v[g][6], v[g][7], inv));
-    if (lane == 0) sa[row] = sc;
-  }
 }
 
 template <typename Tin>
@@ -308,19 +289,15 @@ static int ln_dispatch(const Tin* x, int ldx, int M, int D, float eps, const flo
                        uint8_t* out8 = nullptr, float* sa = nullptr) {
   if (D % 128 || ldx % 4 || ldo % 4 || (out8 && !sa)) return FW_ESHAPE;
   const dim3 grid((M + 7) / 8), block(256);
-  const bool al16 = (reinterpret_cast<uintptr_t>(x) & 15u) == 0 && (out8 || (reinterpret_cast<uintptr_t>(out) & 15u) == 0) &&
-                    (!out8 || (reinterpret_cast<uintptr_t>(out8) & 7u) == 0);
-  if (D % 256 == 0 && ldx % 8 == 0 && ldo % 8 == 0 && al16) {
-    const int wpr = (!out8 && D > 256 * 6 && D % 1024 == 0) ? 4 : 1;   // wide rows: four warps per row
-    const dim3 grid8((M + 8 / wpr - 1) / (8 / wpr));
-    switch (wpr * 100 + D / (256 * wpr)) {
-#define FW_LN8_CASE(n, r)                                                                                        \
-  case r * 100 + n:                                                                                              \
-    launch_k(ln8_kernel<Tin, n, r>, grid8, block, 0, s, x, ldx, M, eps, shift, scale, w, b, out, ldo, out8, sa); \
+  if (!out8 && D % 1024 == 0 && D > 1536) {   // wide rows: four warps per row
+    switch (D / 1024) {
+#define FW_LNW_CASE(n)                                                                                   \
+  case n:                                                                                                \
+    launch_k(ln_wide_kernel<Tin, n>, dim3((M + 1) / 2), block, 0, s, x, ldx, M, eps, shift, scale, w, b, out, \
+             ldo);                                                                                       \
     return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
-      FW_LN8_CASE(1, 1) FW_LN8_CASE(2, 1) FW_LN8_CASE(3, 1) FW_LN8_CASE(4, 1) FW_LN8_CASE(5, 1) FW_LN8_CASE(6, 1)
-      FW_LN8_CASE(2, 4) FW_LN8_CASE(3, 4) FW_LN8_CASE(4, 4) FW_LN8_CASE(5, 4)
-#undef FW_LN8_CASE
+      FW_LNW_CASE(2) FW_LNW_CASE(3) FW_LNW_CASE(4) FW_LNW_CASE(5)
+#undef FW_LNW_CASE
       default: break;
     }
   }

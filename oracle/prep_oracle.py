@@ -10,7 +10,7 @@ library's generator.  The noise layout is the one ``fw_prep`` defines: key = the
 seed (``path_seed``, fastworld/models/mg2/model.py:25-26), counter = {group, tensor, 0, 0}
 with tensor 0 = the initial latent and tensor t = the renoising noise of step t - 1; group g's
 four words give elements 4g .. 4g + 3 by the Box-Muller transform with u = (word + 0.5) / 2^32
-(evaluated here in float64).
+(the uniforms formed in single precision as on the device, the transform in float64).
 """
 from __future__ import annotations
 
@@ -51,8 +51,11 @@ def normals(seed: int, tensor: int, n: int) -> np.ndarray:
     r = philox4x32_10(g, tensor, 0, 0, seed & 0xFFFFFFFF, seed >> 32)
     out = np.empty((n // 4, 4))
     for p in range(2):
-        u1 = (r[2 * p].astype(np.float64) + 0.5) / 2.0 ** 32
-        u2 = (r[2 * p + 1].astype(np.float64) + 0.5) / 2.0 ** 32
+        # the uniforms exactly as the device forms them: the 32-bit word rounded to single
+        # precision, + 0.5 and * 2^-32 in single precision; the transforms then in float64
+        u1 = ((r[2 * p].astype(np.uint32).astype(np.float32) + np.float32(0.5)) * np.float32(2.0 ** -32))
+        u2 = ((r[2 * p + 1].astype(np.uint32).astype(np.float32) + np.float32(0.5)) * np.float32(2.0 ** -32))
+        u1, u2 = u1.astype(np.float64), u2.astype(np.float64)
         rad = np.sqrt(-2.0 * np.log(u1))
         out[:, 2 * p] = rad * np.cos(2 * np.pi * u2)
         out[:, 2 * p + 1] = rad * np.sin(2 * np.pi * u2)
