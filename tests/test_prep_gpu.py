@@ -58,10 +58,12 @@ def test_noise_matches_the_cpu_generator():
             got = buf.float().cpu().numpy().reshape(-1)
             ref = normals(seed, t, got.size)
             ref_bf = torch.from_numpy(ref).float().bfloat16().float().numpy()
-            # equal after bf16 rounding except where fp32 math lands on the other side of a
-            # rounding boundary (at most one bf16 step)
-            step = np.abs(ref_bf) * 2.0 ** -7 + 1e-30
-            assert np.all(np.abs(got - ref_bf) <= step)
+            # equal after bf16 rounding except where the device's single-precision log / sincos
+            # land on the other side of a rounding boundary: within one bf16 step (2^-7
+            # relative) of the float64 value, or 1e-5 absolute near zero
+            err = np.abs(got - ref) - (np.abs(ref) * 2.0 ** -7 + 1e-5)
+            i = int(np.argmax(err))
+            assert err[i] <= 0, (t, i, float(got[i]), float(ref[i]))
             assert np.mean(got == ref_bf) > 0.995
             assert abs(got.mean()) < 0.02 and abs(got.std() - 1) < 0.02
         assert not torch.equal(D.x_in, D.noise[0])
