@@ -11,6 +11,8 @@
 // keyboard K/V of the action module (static.py:165-172) are computed once per chunk.
 #include <cmath>
 #include <cstring>
+#include <cstdio>
+#include <cstdlib>
 #include <string>
 #include <unordered_map>
 #include <vector>
@@ -33,6 +35,7 @@ struct Tensor {
 struct GemmOp {
   CUtensorMap a, b;
   CUtensorMap c;          // fp32 residual, for EPI_RESID_TMA
+  CUtensorMap o[3];       // bf16 output segments, for TMA-store epilogues (args.epi.tma_store)
   bool has_c = false;
   bool pair = false;      // 256 x 256 CTA-pair tiles (gemm2.cu)
   int bn = 256;
@@ -381,12 +384,13 @@ static int make_gemm(GemmOp& op, const void* A, int M, int K, int lda, const voi
   op.args.status = status;
   op.valid = true;
   rc = resid_to_tma(op);
+  if (!rc && !op.pair) rc = make_out_tmaps(op.args, op.o);
   if (rc) return rc;
   return gemm_check(op.args, bn);
 }
 static int run(const GemmOp& op, cudaStream_t s) {
   if (op.pair) return gemm_pair_launch(op.a, op.b, op.args, s, op.has_c ? &op.c : nullptr);
-  return gemm_bf16_launch(op.a, op.b, op.bn, op.args, s, 0, op.has_c ? &op.c : nullptr);
+  return gemm_bf16_launch(op.a, op.b, op.bn, op.args, s, 0, op.has_c ? &op.c : nullptr, op.o);
 }
 static int pick_bn(int N) { return N >= 256 ? 256 : (N >= 128 ? 128 : 64); }
 
@@ -440,10 +444,21 @@ static int make_attn(AttnOp& op, const void* q, int Lq, int heads, const void* k
 }
 static int run(const AttnOp& op, cudaStream_t s) { return attention_launch(op.q, op.k0, op.v0, op.k1, op.v1, op.args, s); }
 
-#define FW_TRY(x)         \
-  do {                    \
-    int _rc = (x);        \
-    if (_rc) return _rc;  \
+// With FW_TRACE_ERRORS=1 in the environment the engine names the first failing call on stderr.
+static bool trace_errors() {
+  static const bool on = [] {
+    const char* v = getenv("FW_TRACE_ERRORS");
+    return v && v[0] == '1';
+  }();
+  return on;
+}
+#define FW_TRY(x)                                                                        \
+  do {                                                                                   \
+    int _rc = (x);                                                                       \
+    if (_rc) {                                                                           \
+      if (trace_errors()) fprintf(stderr, "fastworld_b200: %s failed (%d) at engine.cu:%d\n", #x, _rc, __LINE__); \
+      return _rc;                                                                        \
+    }                                                                                    \
   } while (0)
 
 static int make_lin(fw_handle* h, GemmOp& op, const std::string& wname, const void* A, int lda, int M, int K, int N,
@@ -462,6 +477,7 @@ static int make_lin(fw_handle* h, GemmOp& op, const std::string& wname, const vo
   op.args.status = h->status;
   op.valid = true;
   FW_TRY(resid_to_tma(op));
+  FW_TRY(make_out_tmaps(op.args, op.o));
   return gemm_check(op.args, bn);
 }
 
@@ -679,6 +695,7 @@ static int finalize(fw_handle* h) {
       h->cakv_all = h->layers[0].cakv;
       GemmArgs& a = h->cakv_all.args;
       a.groups = nl;
+      a.epi.tma_store = false;   // grouped outputs are written by st.global (one tensor map per layer otherwise)
       a.tmB_grp = reinterpret_cast<const CUtensorMap*>(g);
       a.bias_grp = reinterpret_cast<const __nv_bfloat16* const*>(g + sizeof(CUtensorMap) * nl);
       a.out_grp_stride = (long long)2 * Ctx * Dl;
@@ -1114,6 +1131,7 @@ int fw_tp_peers(fw_handle* h, void* const* ws_bases, int n) {
         const int parity = (3 * i + k) & 1;
         if (e.mode != fw::EPI_BF16 || e.out[0] != h->part) return FW_ESTATE;
         e.mode = fw::EPI_BF16_PUSH;
+        e.tma_store = false;
         if (h->tp == 2) {
           e.peer_out = P.recv[1 - h->tpr] + (size_t)parity * LD;
         } else {

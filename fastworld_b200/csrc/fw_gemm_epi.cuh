@@ -199,6 +199,38 @@ __device__ __forceinline__ void epilogue_bf16_box(const GemmEpi& e, const __nv_b
   __syncwarp();
 }
 
+// The same bf16 box written by one TMA store (lane 0) through the output tensor map `om` of the
+// column segment: the TMA engine carries the global writes, so the warp is free as soon as the
+// store has read the box (an st.global epilogue is limited by the stores an SM keeps in flight:
+// about 13 GB/s per SM, 2 TB/s for the whole GPU, measured).  Rows >= M and columns past the
+// segment are clipped by TMA.  The box is reused only after the previous store read it.
+template <int NCH>
+__device__ __forceinline__ void epilogue_bf16_tma(const GemmEpi& e, const CUtensorMap* om, int row, int row0,
+                                                  int colb, int N, const uint32_t (*r)[32],
+                                                  const float* __restrict__ sa, const float* __restrict__ sw,
+                                                  uint8_t* box, int lane) {
+  const int frame = row / e.rows_per_frame;
+  if (lane == 0) bulk_wait_read0();   // this warp's previous store has read the box
+  __syncwarp();
+#pragma unroll
+  for (int cc = 0; cc < NCH; ++cc) {
+    float v[32];
+    epi_math_bf16(e, e.bias, row, frame, min(colb + cc * 32, N - 32), r[cc], sa, sw, v);
+#pragma unroll
+    for (int pc = 0; pc < 4; ++pc)
+      *reinterpret_cast<uint4*>(box + lane * 128 + (((cc * 4 + pc) ^ (lane & 7)) << 4)) =
+          make_uint4(pack_bf16(v[8 * pc + 0], v[8 * pc + 1]), pack_bf16(v[8 * pc + 2], v[8 * pc + 3]),
+                     pack_bf16(v[8 * pc + 4], v[8 * pc + 5]), pack_bf16(v[8 * pc + 6], v[8 * pc + 7]));
+  }
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    const int seg = colb / e.seg_w;
+    tma_store_2d(om, box, colb - seg * e.seg_w, row0);
+    bulk_commit();
+  }
+}
+
 // EPI_RESID_F32 (with or without a bf16 mirror): the warp's 32 rows x 32 columns of
 // gate * (acc + bias) go through a swizzled fp32 box; then each instruction updates four whole
 // 128-byte residual rows (8 lanes per row, 16 bytes each: coalesced read-modify-write, all eight

@@ -83,6 +83,9 @@ struct GemmEpi {
   int push_tp = 0, push_rank = 0, push_ls = 0;
   int ld_mirror = 0;
   int rows_per_frame = 1 << 30;
+  // bf16 output modes: store each warp's 32 x 64 box with a TMA store through the output tensor
+  // maps (one per column segment, box [32 rows, 64 cols], 128-byte swizzle) instead of st.global
+  bool tma_store = false;
 };
 
 struct GemmArgs {
@@ -106,8 +109,12 @@ struct GemmArgs {
 // bn in {64, 128, 256}.  `ctas` = 0 uses one CTA per SM (persistent).
 // tmC: the fp32 residual [M, ld_resid] with box [32 rows, 32 cols], 128-byte swizzle, for
 // EPI_RESID_TMA (ignored otherwise).
+// tmO: with epi.tma_store, the output tensor maps of the column segments (make_out_tmaps).
 int gemm_bf16_launch(const CUtensorMap& tmA, const CUtensorMap& tmB, int bn, const GemmArgs& a, cudaStream_t s,
-                     int ctas = 0, const CUtensorMap* tmC = nullptr);
+                     int ctas = 0, const CUtensorMap* tmC = nullptr, const CUtensorMap* tmO = nullptr);
+// Output tensor maps for a bf16-output GEMM (one per column segment of a.epi) and sets
+// a.epi.tma_store; leaves the st.global path (returns 0, tma_store false) for grouped launches.
+int make_out_tmaps(GemmArgs& a, CUtensorMap (&o)[3]);
 int gemm_check(const GemmArgs& a, int bn);
 // CTA-pair variant (gemm2.cu): 256 x 256 tiles; tmA box [128 rows, 64 cols] as above, tmB box
 // [128 rows, 64 cols] (half a tile of output columns per CTA).

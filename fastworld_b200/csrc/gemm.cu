@@ -43,7 +43,9 @@ struct GemmCfg {
 template <int BN, bool F8>
 __global__ void __launch_bounds__(320, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                     const __grid_constant__ CUtensorMap tmC, const GemmArgs args) {
+                     const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmO0,
+                     const __grid_constant__ CUtensorMap tmO1, const __grid_constant__ CUtensorMap tmO2,
+                     const GemmArgs args) {
   using C = GemmCfg<BN>;
   constexpr int KE = F8 ? 128 : 64;   // K elements per stage
   pdl_trigger();
@@ -193,7 +195,9 @@ __global__ void __launch_bounds__(320, 1)
       if (args.epi.mode == EPI_BF16_PUSH ||
           (NC >= 2 && (args.epi.mode == EPI_BF16 || args.epi.mode == EPI_GELU_BF16 ||
                        args.epi.mode == EPI_GELU_ERF_BF16))) {   // 64 columns per box
-#pragma unroll
+        // not unrolled: one box's code is already long, and warps that miss in the instruction
+        // cache stall the epilogue (the main stall of an epilogue-bound GEMM, measured)
+#pragma unroll 1
         for (int b = 0; b < NC / 2; ++b) {
           uint32_t r[2][32];
           tmem_ld32(tb + (uint32_t)(b * 64), r[0]);
@@ -201,9 +205,13 @@ __global__ void __launch_bounds__(320, 1)
           tmem_ld_wait();
           const int colb = colh + b * 64;
           if (colb < N) {
-            if (args.epi.mode == EPI_BF16_PUSH)
+            if (args.epi.mode == EPI_BF16_PUSH) {
               epilogue_push64(args.epi, rowc, row0, colb, M, N, r[0], r[1], box, lane);
-            else
+            } else if (args.epi.tma_store) {
+              const int seg = colb / args.epi.seg_w;
+              epilogue_bf16_tma<2>(args.epi, seg == 0 ? &tmO0 : (seg == 1 ? &tmO1 : &tmO2), rowc, row0, colb, N, r,
+                                   sa, args.sw, box, lane);
+            } else
               epilogue_bf16_box<2>(args.epi, args.groups > 1 ? args.bias_grp[g] : args.epi.bias,
                                    (size_t)g * (size_t)args.out_grp_stride, rowc, row0, colb, M, N, r, sa,
                                    args.sw, box, lane);
@@ -215,7 +223,7 @@ __global__ void __launch_bounds__(320, 1)
         // (NC boxes in flight, one wait at the end).  Earlier tiles overlap the next tile's main
         // loop and reuse the warp's one box.
         const bool last = args.epi.mode == EPI_RESID_TMA && t + (int)gridDim.x >= num_tiles;
-#pragma unroll
+#pragma unroll 1
         for (int c = 0; c < NC; ++c) {
           uint32_t r[32];
           tmem_ld32(tb + (uint32_t)(c * 32), r);
@@ -236,7 +244,8 @@ __global__ void __launch_bounds__(320, 1)
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
-    if (args.epi.mode == EPI_RESID_TMA && lane == 0) bulk_wait0();   // residual adds performed before exit
+    if ((args.epi.mode == EPI_RESID_TMA || args.epi.tma_store) && lane == 0)
+      bulk_wait0();   // residual adds / output stores performed before exit
   }
   __syncthreads();
   if (warp == 1) {
@@ -303,30 +312,53 @@ int gemm_check(const GemmArgs& a, int bn) {
 }
 
 template <int BN, bool F8>
-static int launch_bn(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmC, const GemmArgs& a,
-                     cudaStream_t s, int grid) {
+static int launch_bn(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmC, const CUtensorMap* o,
+                     const GemmArgs& a, cudaStream_t s, int grid) {
   using C = GemmCfg<BN>;
   cudaError_t err =
       cudaFuncSetAttribute(gemm_bf16_kernel<BN, F8>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (err != cudaSuccess) return FW_ECUDA;
-  launch_k(gemm_bf16_kernel<BN, F8>, grid, 320, C::SMEM, s, tmA, tmB, tmC, a);
+  launch_k(gemm_bf16_kernel<BN, F8>, grid, 320, C::SMEM, s, tmA, tmB, tmC, o[0], o[1], o[2], a);
   return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
 }
 
+int make_out_tmaps(GemmArgs& a, CUtensorMap (&o)[3]) {
+  GemmEpi& e = a.epi;
+  e.tma_store = false;
+  if (a.groups != 1 || (e.mode != EPI_BF16 && e.mode != EPI_GELU_BF16 && e.mode != EPI_GELU_ERF_BF16)) return 0;
+  if (e.seg_w <= 0 || e.ld_out % 8) return FW_ESHAPE;
+  const int nseg = (a.N + e.seg_w - 1) / e.seg_w;
+  if (nseg > 3) return FW_ESHAPE;
+  for (int i = 0; i < nseg; ++i) {
+    const int cols = a.N - i * e.seg_w < e.seg_w ? a.N - i * e.seg_w : e.seg_w;
+    const int rc = make_tmap_2d(&o[i], e.out[i], 2, a.M, cols, e.ld_out, 32, 64, true);
+    if (rc) return rc;
+  }
+  for (int i = nseg; i < 3; ++i) o[i] = o[0];
+  e.tma_store = true;
+  return 0;
+}
+
 int gemm_bf16_launch(const CUtensorMap& tmA, const CUtensorMap& tmB, int bn, const GemmArgs& a, cudaStream_t s,
-                     int ctas, const CUtensorMap* tmC) {
+                     int ctas, const CUtensorMap* tmC, const CUtensorMap* tmO) {
   int rc = gemm_check(a, bn);
   if (rc) return rc;
   if (a.epi.mode == EPI_RESID_TMA && !tmC) return FW_EINVAL;
+  if (a.epi.tma_store && (!tmO || a.groups != 1)) return FW_EINVAL;
   const CUtensorMap& mc = tmC ? *tmC : tmA;   // unused unless EPI_RESID_TMA
+  const CUtensorMap none[3] = {tmA, tmA, tmA};   // unused unless epi.tma_store
+  const CUtensorMap* o = a.epi.tma_store ? tmO : none;
   const int tiles = ((a.M + 127) / 128) * ((a.N + bn - 1) / bn) * a.groups;
   int grid = ctas > 0 ? ctas : num_sms();
   if (grid > tiles) grid = tiles;
   GemmArgs b = a;
   switch (bn) {
-    case 256: return a.sa ? launch_bn<256, true>(tmA, tmB, mc, b, s, grid) : launch_bn<256, false>(tmA, tmB, mc, b, s, grid);
-    case 128: return a.sa ? launch_bn<128, true>(tmA, tmB, mc, b, s, grid) : launch_bn<128, false>(tmA, tmB, mc, b, s, grid);
-    default: return a.sa ? launch_bn<64, true>(tmA, tmB, mc, b, s, grid) : launch_bn<64, false>(tmA, tmB, mc, b, s, grid);
+    case 256:
+      return a.sa ? launch_bn<256, true>(tmA, tmB, mc, o, b, s, grid) : launch_bn<256, false>(tmA, tmB, mc, o, b, s, grid);
+    case 128:
+      return a.sa ? launch_bn<128, true>(tmA, tmB, mc, o, b, s, grid) : launch_bn<128, false>(tmA, tmB, mc, o, b, s, grid);
+    default:
+      return a.sa ? launch_bn<64, true>(tmA, tmB, mc, o, b, s, grid) : launch_bn<64, false>(tmA, tmB, mc, o, b, s, grid);
   }
 }
 

@@ -105,7 +105,10 @@ int fw_gemm_bf16(const void* A, const void* B, const void* bias, void* out, int 
   a.epi.seg_w = 1 << 30;
   a.epi.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
   if (bn == 512) return gemm_pair_launch(ta, tb, a, reinterpret_cast<cudaStream_t>(stream));
-  return gemm_bf16_launch(ta, tb, bn, a, reinterpret_cast<cudaStream_t>(stream));
+  CUtensorMap to[3];
+  rc = make_out_tmaps(a, to);
+  if (rc) return rc;
+  return gemm_bf16_launch(ta, tb, bn, a, reinterpret_cast<cudaStream_t>(stream), 0, nullptr, to);
 }
 
 int fw_gemm_e4m3(const void* A8, const float* sa, const void* B8, const float* sw, const void* bias, void* out,
@@ -132,7 +135,10 @@ int fw_gemm_e4m3(const void* A8, const float* sa, const void* B8, const float* s
   a.epi.seg_w = 1 << 30;
   a.epi.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
   if (bn == 512) return gemm_pair_launch(ta, tb, a, reinterpret_cast<cudaStream_t>(stream));
-  return gemm_bf16_launch(ta, tb, bn, a, reinterpret_cast<cudaStream_t>(stream));
+  CUtensorMap to[3];
+  rc = make_out_tmaps(a, to);
+  if (rc) return rc;
+  return gemm_bf16_launch(ta, tb, bn, a, reinterpret_cast<cudaStream_t>(stream), 0, nullptr, to);
 }
 
 int fw_ipc_get_handle(const void* ptr, void* handle, size_t* offset) {
