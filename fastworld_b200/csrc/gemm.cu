@@ -40,7 +40,17 @@ struct GemmCfg {
 // F8 = false: bf16 operands, kind::f16, 64 elements (128 bytes) of K per stage.
 // F8 = true:  e4m3 operands, kind::f8f6f4, 128 elements (128 bytes) of K per stage; the same
 //             128-byte-swizzled smem tiles and descriptors, 32 bytes of K per MMA instruction.
-template <int BN, bool F8>
+// Epilogue kinds, one kernel instantiation each, so that a launch carries only the code of its
+// own epilogue (the in-chunk GEMMs are sensitive to instruction-cache misses):
+enum : int {
+  EK_BOX = 0,     // bf16 output modes, 64 columns per box (TMA store or st.global)
+  EK_RTMA = 1,    // EPI_RESID_TMA
+  EK_RF32 = 2,    // EPI_RESID_F32
+  EK_CHUNK = 3,   // EPI_F32, and the bf16 modes of 64-column tiles (epilogue_chunk)
+  EK_PUSH = 4,    // EPI_BF16_PUSH
+};
+
+template <int BN, bool F8, int EK>
 __global__ void __launch_bounds__(320, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmO0,
@@ -177,7 +187,7 @@ __global__ void __launch_bounds__(320, 1)
       const int g = t / tpg, mb = (t - g * tpg) % num_m, nb = (t - g * tpg) / num_m;
       const int row = mb * 128 + q * 32 + lane;
       const int colh = nb * BN + h * (BN / 2);
-      if (args.epi.mode == EPI_RESID_F32 && row < M && colh < N) {   // warm L2 with this thread's residual row part
+      if (EK == EK_RF32 && row < M && colh < N) {   // warm L2 with this thread's residual row part
         const char* p = reinterpret_cast<const char*>(args.epi.resid + (size_t)row * args.epi.ld_resid + colh);
 #pragma unroll
         for (int b = 0; b < BN * 2; b += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(p + b));
@@ -192,9 +202,7 @@ __global__ void __launch_bounds__(320, 1)
       uint8_t* box = smem + C::EPI_OFF + (warp - 2) * C::EPI_BOX;
       const int rowc = min(row, M - 1), row0 = mb * 128 + q * 32;
       const float* sa = F8 ? args.sa : nullptr;
-      if (args.epi.mode == EPI_BF16_PUSH ||
-          (NC >= 2 && (args.epi.mode == EPI_BF16 || args.epi.mode == EPI_GELU_BF16 ||
-                       args.epi.mode == EPI_GELU_ERF_BF16))) {   // 64 columns per box
+      if constexpr (EK == EK_PUSH || EK == EK_BOX) {   // 64 columns per box
         // not unrolled: one box's code is already long, and warps that miss in the instruction
         // cache stall the epilogue (the main stall of an epilogue-bound GEMM, measured)
 #pragma unroll 1
@@ -205,7 +213,7 @@ __global__ void __launch_bounds__(320, 1)
           tmem_ld_wait();
           const int colb = colh + b * 64;
           if (colb < N) {
-            if (args.epi.mode == EPI_BF16_PUSH) {
+            if constexpr (EK == EK_PUSH) {
               epilogue_push64(args.epi, rowc, row0, colb, M, N, r[0], r[1], box, lane);
             } else if (args.epi.tma_store) {
               const int seg = colb / args.epi.seg_w;
@@ -222,7 +230,7 @@ __global__ void __launch_bounds__(320, 1)
         // pending, so the pipeline stages are idle and each warp stages all its chunks at once
         // (NC boxes in flight, one wait at the end).  Earlier tiles overlap the next tile's main
         // loop and reuse the warp's one box.
-        const bool last = args.epi.mode == EPI_RESID_TMA && t + (int)gridDim.x >= num_tiles;
+        const bool last = EK == EK_RTMA && t + (int)gridDim.x >= num_tiles;
 #pragma unroll 1
         for (int c = 0; c < NC; ++c) {
           uint32_t r[32];
@@ -230,10 +238,10 @@ __global__ void __launch_bounds__(320, 1)
           tmem_ld_wait();
           const int col0 = colh + c * 32;
           if (col0 >= N) continue;
-          if (args.epi.mode == EPI_RESID_TMA)
+          if constexpr (EK == EK_RTMA)
             epilogue_chunk_tma(args.epi, &tmC, rowc, row0, col0, r, sa, args.sw,
                                last ? smem + ((warp - 2) * NC + c) * C::EPI_BOX : box, lane, !last);
-          else if (args.epi.mode == EPI_RESID_F32)
+          else if constexpr (EK == EK_RF32)
             epilogue_resid_box(args.epi, rowc, row0, col0, M, r, sa, args.sw, box, lane);
           else if (row < M)
             epilogue_chunk(args.epi, row, col0, r, sa, args.sw);
@@ -244,7 +252,7 @@ __global__ void __launch_bounds__(320, 1)
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
-    if ((args.epi.mode == EPI_RESID_TMA || args.epi.tma_store) && lane == 0)
+    if ((EK == EK_RTMA || (EK == EK_BOX && args.epi.tma_store)) && lane == 0)
       bulk_wait0();   // residual adds / output stores performed before exit
   }
   __syncthreads();
@@ -311,15 +319,43 @@ int gemm_check(const GemmArgs& a, int bn) {
   return 0;
 }
 
-template <int BN, bool F8>
+template <int BN, bool F8, int EK>
 static int launch_bn(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmC, const CUtensorMap* o,
                      const GemmArgs& a, cudaStream_t s, int grid) {
   using C = GemmCfg<BN>;
   cudaError_t err =
-      cudaFuncSetAttribute(gemm_bf16_kernel<BN, F8>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+      cudaFuncSetAttribute(gemm_bf16_kernel<BN, F8, EK>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (err != cudaSuccess) return FW_ECUDA;
-  launch_k(gemm_bf16_kernel<BN, F8>, grid, 320, C::SMEM, s, tmA, tmB, tmC, o[0], o[1], o[2], a);
+  launch_k(gemm_bf16_kernel<BN, F8, EK>, grid, 320, C::SMEM, s, tmA, tmB, tmC, o[0], o[1], o[2], a);
   return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
+}
+
+static int epi_kind(const GemmEpi& e, int bn) {
+  switch (e.mode) {
+    case EPI_BF16_PUSH: return EK_PUSH;
+    case EPI_BF16:
+    case EPI_GELU_BF16:
+    case EPI_GELU_ERF_BF16: return bn >= 128 ? EK_BOX : EK_CHUNK;
+    case EPI_RESID_TMA: return EK_RTMA;
+    case EPI_RESID_F32: return EK_RF32;
+    default: return EK_CHUNK;
+  }
+}
+
+template <int BN, bool F8>
+static int launch_kind(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmC, const CUtensorMap* o,
+                       const GemmArgs& a, cudaStream_t s, int grid) {
+  switch (epi_kind(a.epi, BN)) {
+    case EK_RTMA: return launch_bn<BN, F8, EK_RTMA>(tmA, tmB, tmC, o, a, s, grid);
+    case EK_RF32: return launch_bn<BN, F8, EK_RF32>(tmA, tmB, tmC, o, a, s, grid);
+    case EK_CHUNK: return launch_bn<BN, F8, EK_CHUNK>(tmA, tmB, tmC, o, a, s, grid);
+    default: break;
+  }
+  if constexpr (BN >= 128) {   // the box kinds need two 32-column chunks per thread
+    if (epi_kind(a.epi, BN) == EK_BOX) return launch_bn<BN, F8, EK_BOX>(tmA, tmB, tmC, o, a, s, grid);
+    if constexpr (!F8) return launch_bn<BN, false, EK_PUSH>(tmA, tmB, tmC, o, a, s, grid);
+  }
+  return FW_EINVAL;
 }
 
 int make_out_tmaps(GemmArgs& a, CUtensorMap (&o)[3]) {
@@ -354,11 +390,11 @@ int gemm_bf16_launch(const CUtensorMap& tmA, const CUtensorMap& tmB, int bn, con
   GemmArgs b = a;
   switch (bn) {
     case 256:
-      return a.sa ? launch_bn<256, true>(tmA, tmB, mc, o, b, s, grid) : launch_bn<256, false>(tmA, tmB, mc, o, b, s, grid);
+      return a.sa ? launch_kind<256, true>(tmA, tmB, mc, o, b, s, grid) : launch_kind<256, false>(tmA, tmB, mc, o, b, s, grid);
     case 128:
-      return a.sa ? launch_bn<128, true>(tmA, tmB, mc, o, b, s, grid) : launch_bn<128, false>(tmA, tmB, mc, o, b, s, grid);
+      return a.sa ? launch_kind<128, true>(tmA, tmB, mc, o, b, s, grid) : launch_kind<128, false>(tmA, tmB, mc, o, b, s, grid);
     default:
-      return a.sa ? launch_bn<64, true>(tmA, tmB, mc, o, b, s, grid) : launch_bn<64, false>(tmA, tmB, mc, o, b, s, grid);
+      return a.sa ? launch_kind<64, true>(tmA, tmB, mc, o, b, s, grid) : launch_kind<64, false>(tmA, tmB, mc, o, b, s, grid);
   }
 }
 
