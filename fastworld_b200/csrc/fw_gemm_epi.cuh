@@ -134,10 +134,14 @@ __device__ __forceinline__ void epilogue_chunk_tma(const GemmEpi& e, const CUten
 }
 
 // Bias / activation / e4m3 scales of one 32-column accumulator chunk (bf16 output modes).
+// ACT: the activation fixed at compile time (EPI_BF16 / EPI_GELU_BF16 / EPI_GELU_ERF_BF16), or
+// -1 to read it from e.mode.
+template <int ACT = -1>
 __device__ __forceinline__ void epi_math_bf16(const GemmEpi& e, const __nv_bfloat16* bias, int row, int frame,
                                               int col0, const uint32_t (&r)[32],
                                               const float* __restrict__ sa, const float* __restrict__ sw,
                                               float (&v)[32]) {
+  const int act = ACT >= 0 ? ACT : e.mode;
 #pragma unroll
   for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
   if (sa) {
@@ -150,10 +154,10 @@ __device__ __forceinline__ void epi_math_bf16(const GemmEpi& e, const __nv_bfloa
     }
   }
   add_bias(e, bias, frame, col0, v);
-  if (e.mode == EPI_GELU_BF16) {
+  if (act == EPI_GELU_BF16) {
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
-  } else if (e.mode == EPI_GELU_ERF_BF16) {
+  } else if (act == EPI_GELU_ERF_BF16) {
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = 0.5f * v[j] * (1.f + erff(v[j] * 0.7071067811865476f));
   }
@@ -204,7 +208,7 @@ __device__ __forceinline__ void epilogue_bf16_box(const GemmEpi& e, const __nv_b
 // store has read the box (an st.global epilogue is limited by the stores an SM keeps in flight:
 // about 13 GB/s per SM, 2 TB/s for the whole GPU, measured).  Rows >= M and columns past the
 // segment are clipped by TMA.  The box is reused only after the previous store read it.
-template <int NCH>
+template <int NCH, int ACT>
 __device__ __forceinline__ void epilogue_bf16_tma(const GemmEpi& e, const CUtensorMap* om, int row, int row0,
                                                   int colb, int N, const uint32_t (*r)[32],
                                                   const float* __restrict__ sa, const float* __restrict__ sw,
@@ -215,7 +219,7 @@ __device__ __forceinline__ void epilogue_bf16_tma(const GemmEpi& e, const CUtens
 #pragma unroll
   for (int cc = 0; cc < NCH; ++cc) {
     float v[32];
-    epi_math_bf16(e, e.bias, row, frame, min(colb + cc * 32, N - 32), r[cc], sa, sw, v);
+    epi_math_bf16<ACT>(e, e.bias, row, frame, min(colb + cc * 32, N - 32), r[cc], sa, sw, v);
 #pragma unroll
     for (int pc = 0; pc < 4; ++pc)
       *reinterpret_cast<uint4*>(box + lane * 128 + (((cc * 4 + pc) ^ (lane & 7)) << 4)) =

@@ -43,11 +43,13 @@ struct GemmCfg {
 // Epilogue kinds, one kernel instantiation each, so that a launch carries only the code of its
 // own epilogue (the in-chunk GEMMs are sensitive to instruction-cache misses):
 enum : int {
-  EK_BOX = 0,     // bf16 output modes, 64 columns per box (TMA store or st.global)
+  EK_BOX = 0,     // bf16 output modes, 64 columns per box stored with st.global (grouped launches)
   EK_RTMA = 1,    // EPI_RESID_TMA
   EK_RF32 = 2,    // EPI_RESID_F32
   EK_CHUNK = 3,   // EPI_F32, and the bf16 modes of 64-column tiles (epilogue_chunk)
   EK_PUSH = 4,    // EPI_BF16_PUSH
+  EK_TMA = 8,     // bf16 output modes, 64 columns per box, TMA store; + the activation:
+                  // EK_TMA + EPI_BF16, EK_TMA + EPI_GELU_BF16, EK_TMA + EPI_GELU_ERF_BF16
 };
 
 template <int BN, bool F8, int EK>
@@ -202,7 +204,7 @@ __global__ void __launch_bounds__(320, 1)
       uint8_t* box = smem + C::EPI_OFF + (warp - 2) * C::EPI_BOX;
       const int rowc = min(row, M - 1), row0 = mb * 128 + q * 32;
       const float* sa = F8 ? args.sa : nullptr;
-      if constexpr (EK == EK_PUSH || EK == EK_BOX) {   // 64 columns per box
+      if constexpr (EK == EK_PUSH || EK == EK_BOX || EK >= EK_TMA) {   // 64 columns per box
         // not unrolled: one box's code is already long, and warps that miss in the instruction
         // cache stall the epilogue (the main stall of an epilogue-bound GEMM, measured)
 #pragma unroll 1
@@ -215,10 +217,10 @@ __global__ void __launch_bounds__(320, 1)
           if (colb < N) {
             if constexpr (EK == EK_PUSH) {
               epilogue_push64(args.epi, rowc, row0, colb, M, N, r[0], r[1], box, lane);
-            } else if (args.epi.tma_store) {
+            } else if constexpr (EK >= EK_TMA) {
               const int seg = colb / args.epi.seg_w;
-              epilogue_bf16_tma<2>(args.epi, seg == 0 ? &tmO0 : (seg == 1 ? &tmO1 : &tmO2), rowc, row0, colb, N, r,
-                                   sa, args.sw, box, lane);
+              epilogue_bf16_tma<2, EK - EK_TMA>(args.epi, seg == 0 ? &tmO0 : (seg == 1 ? &tmO1 : &tmO2), rowc, row0,
+                                                colb, N, r, sa, args.sw, box, lane);
             } else
               epilogue_bf16_box<2>(args.epi, args.groups > 1 ? args.bias_grp[g] : args.epi.bias,
                                    (size_t)g * (size_t)args.out_grp_stride, rowc, row0, colb, M, N, r, sa,
@@ -252,7 +254,7 @@ __global__ void __launch_bounds__(320, 1)
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
-    if ((EK == EK_RTMA || (EK == EK_BOX && args.epi.tma_store)) && lane == 0)
+    if ((EK == EK_RTMA || EK >= EK_TMA) && lane == 0)
       bulk_wait0();   // residual adds / output stores performed before exit
   }
   __syncthreads();
@@ -335,7 +337,7 @@ static int epi_kind(const GemmEpi& e, int bn) {
     case EPI_BF16_PUSH: return EK_PUSH;
     case EPI_BF16:
     case EPI_GELU_BF16:
-    case EPI_GELU_ERF_BF16: return bn >= 128 ? EK_BOX : EK_CHUNK;
+    case EPI_GELU_ERF_BF16: return bn < 128 ? EK_CHUNK : (e.tma_store ? EK_TMA + e.mode : EK_BOX);
     case EPI_RESID_TMA: return EK_RTMA;
     case EPI_RESID_F32: return EK_RF32;
     default: return EK_CHUNK;
@@ -352,8 +354,17 @@ static int launch_kind(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUt
     default: break;
   }
   if constexpr (BN >= 128) {   // the box kinds need two 32-column chunks per thread
-    if (epi_kind(a.epi, BN) == EK_BOX) return launch_bn<BN, F8, EK_BOX>(tmA, tmB, tmC, o, a, s, grid);
-    if constexpr (!F8) return launch_bn<BN, false, EK_PUSH>(tmA, tmB, tmC, o, a, s, grid);
+    switch (epi_kind(a.epi, BN)) {
+      case EK_BOX: return launch_bn<BN, F8, EK_BOX>(tmA, tmB, tmC, o, a, s, grid);
+      case EK_TMA + EPI_BF16: return launch_bn<BN, F8, EK_TMA + EPI_BF16>(tmA, tmB, tmC, o, a, s, grid);
+      case EK_TMA + EPI_GELU_BF16: return launch_bn<BN, F8, EK_TMA + EPI_GELU_BF16>(tmA, tmB, tmC, o, a, s, grid);
+      case EK_TMA + EPI_GELU_ERF_BF16:
+        return launch_bn<BN, F8, EK_TMA + EPI_GELU_ERF_BF16>(tmA, tmB, tmC, o, a, s, grid);
+      case EK_PUSH:
+        if constexpr (!F8) return launch_bn<BN, false, EK_PUSH>(tmA, tmB, tmC, o, a, s, grid);
+        break;
+      default: break;
+    }
   }
   return FW_EINVAL;
 }
