@@ -556,15 +556,24 @@ def gemm_resid(reps: int) -> None:
 
 
 def attn(reps: int) -> None:
+    """Steady self-attention (12 heads, 2640 queries over 2640 history + 2640 current keys) and
+    cross-attention (2640 queries over 257 context keys), MG2 shape; timed through recorded
+    graphs of back-to-back launches."""
     from fastworld_b200 import ops
     g = torch.Generator(device="cuda").manual_seed(0)
-    r = lambda n: torch.randn(n, 12, 128, device="cuda", generator=g).to(torch.bfloat16)
+    r = lambda n: torch.randn(n, 12, 128, device="cuda", generator=g).to(torch.bfloat16)  # noqa: E731
     q, k0, v0, k1, v1 = r(2640), r(2640), r(2640), r(2640), r(2640)
+    kc, vc = r(257), r(257)
     meta = torch.tensor([2640, 2640], dtype=torch.int32, device="cuda")
+    meta_x = torch.tensor([257, 0], dtype=torch.int32, device="cuda")
     for _ in range(reps):
         ops.attention(q, k0, v0, k1, v1, meta)
     torch.cuda.synchronize()
-    print("attn ok")
+    ms = _graph_ms([lambda: ops.attention(q, k0, v0, k1, v1, meta)] * 4)
+    msx = _graph_ms([lambda: ops.attention(q, kc, vc, kc, vc, meta_x)] * 4)
+    fl, flx = 4.0 * 2640 * 5280 * 128 * 12, 4.0 * 2640 * 257 * 128 * 12
+    print(f"attention self {ms * 1e3:.1f} us ({fl / ms / 1e9:.0f} TFLOP/s), cross {msx * 1e3:.1f} us "
+          f"({flx / msx / 1e9:.0f} TFLOP/s)")
 
 
 def fp8_peak(reps: int) -> None:

@@ -56,10 +56,14 @@ __device__ __forceinline__ float max3f(float a, float b, float c) {
   return d;
 }
 
+// TMA_OUT: O leaves through the tile's (then idle) P buffer with two TMA stores per tile instead
+// of each softmax thread storing its own row (32 rows per warp store instruction).
+template <bool TMA_OUT>
 __global__ void __launch_bounds__(attn::THREADS, 1)
     attention_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK0,
                      const __grid_constant__ CUtensorMap tmV0, const __grid_constant__ CUtensorMap tmK1,
-                     const __grid_constant__ CUtensorMap tmV1, const AttnArgs args) {
+                     const __grid_constant__ CUtensorMap tmV1, const __grid_constant__ CUtensorMap tmO,
+                     const AttnArgs args) {
   using namespace attn;
   pdl_trigger();
   pdl_wait();
@@ -314,17 +318,41 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
         for (int c = 0; c < 4; ++c) {
           tmem_ld32(tmem + lane_off + o_col(t) + (uint32_t)(c * 32), r);
           tmem_ld_wait();
-          if (grow < args.Lq) {
+          uint4 u[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            u[i] = make_uint4(pack_bf16(__uint_as_float(r[8 * i + 0]) * inv, __uint_as_float(r[8 * i + 1]) * inv),
+                              pack_bf16(__uint_as_float(r[8 * i + 2]) * inv, __uint_as_float(r[8 * i + 3]) * inv),
+                              pack_bf16(__uint_as_float(r[8 * i + 4]) * inv, __uint_as_float(r[8 * i + 5]) * inv),
+                              pack_bf16(__uint_as_float(r[8 * i + 6]) * inv, __uint_as_float(r[8 * i + 7]) * inv));
+          if constexpr (TMA_OUT) {   // into the P buffer (its last reader, the final P V, completed)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int chunk = c * 4 + i, sub = chunk >> 3, ch = chunk & 7;
+              *reinterpret_cast<uint4*>(sP + sub * TILE + row * 128 + ((ch ^ (row & 7)) << 4)) = u[i];
+            }
+          } else if (grow < args.Lq) {
             uint4* dst = reinterpret_cast<uint4*>(args.out + (size_t)grow * args.ld_out + col + c * 32);
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
-              dst[i] = make_uint4(pack_bf16(__uint_as_float(r[8 * i + 0]) * inv, __uint_as_float(r[8 * i + 1]) * inv),
-                                  pack_bf16(__uint_as_float(r[8 * i + 2]) * inv, __uint_as_float(r[8 * i + 3]) * inv),
-                                  pack_bf16(__uint_as_float(r[8 * i + 4]) * inv, __uint_as_float(r[8 * i + 5]) * inv),
-                                  pack_bf16(__uint_as_float(r[8 * i + 6]) * inv, __uint_as_float(r[8 * i + 7]) * inv));
+            for (int i = 0; i < 4; ++i) dst[i] = u[i];
           }
         }
+        if constexpr (TMA_OUT) fence_proxy_async_smem();
         tc_fence_before();
+      }
+    }
+    if constexpr (TMA_OUT) {
+      // the tile's 128 softmax threads meet (named barrier 1 + t), then one stores the tile: rows
+      // past Lq are clipped by the tensor map
+      if (t == 0)
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+      else
+        asm volatile("bar.sync 2, 128;" ::: "memory");
+      if (q == 0 && lane == 0 && ok && nblk > 0) {
+        tma_store_2d(&tmO, sP, col, q0 + t * BQ);
+        tma_store_2d(&tmO, sP + TILE, col + 64, q0 + t * BQ);
+        bulk_commit();
+        bulk_wait0();
       }
     }
   }
@@ -336,17 +364,18 @@ __global__ void __launch_bounds__(attn::THREADS, 1)
 }
 
 int attention_launch(const CUtensorMap& tmQ, const CUtensorMap& tmK0, const CUtensorMap& tmV0,
-                     const CUtensorMap& tmK1, const CUtensorMap& tmV1, const AttnArgs& a, cudaStream_t s) {
+                     const CUtensorMap& tmK1, const CUtensorMap& tmV1, const AttnArgs& a, cudaStream_t s,
+                     const CUtensorMap* tmO) {
   if (a.Lq <= 0 || a.heads <= 0 || !a.meta || !a.out) return FW_EINVAL;
   if (a.ld_out % 8 || (reinterpret_cast<uintptr_t>(a.out) & 15u)) return FW_EALIGN;
   dim3 grid((a.Lq + 2 * attn::BQ - 1) / (2 * attn::BQ), a.heads);
-  auto go = [&](auto kern) {
+  auto go = [&](auto kern, const CUtensorMap& o) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, attn::SMEM) != cudaSuccess)
       return FW_ECUDA;
-    launch_k(kern, grid, attn::THREADS, attn::SMEM, s, tmQ, tmK0, tmV0, tmK1, tmV1, a);
+    launch_k(kern, grid, attn::THREADS, attn::SMEM, s, tmQ, tmK0, tmV0, tmK1, tmV1, o, a);
     return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
   };
-  return go(attention_kernel);
+  return tmO ? go(attention_kernel<true>, *tmO) : go(attention_kernel<false>, tmQ);
 }
 
 }  // namespace fw

@@ -44,7 +44,7 @@ struct GemmOp {
 };
 
 struct AttnOp {
-  CUtensorMap q, k0, v0, k1, v1;
+  CUtensorMap q, k0, v0, k1, v1, o;
   AttnArgs args;
 };
 
@@ -430,6 +430,7 @@ static int make_attn(AttnOp& op, const void* q, int Lq, int heads, const void* k
   if (!rc) rc = make_tmap_2d(&op.v0, v0, 2, cap0, cols, cols, 128, 64, true);
   if (!rc) rc = make_tmap_2d(&op.k1, k1, 2, cap1, cols, cols, 128, 64, true);
   if (!rc) rc = make_tmap_2d(&op.v1, v1, 2, cap1, cols, cols, 128, 64, true);
+  if (!rc) rc = make_tmap_2d(&op.o, out, 2, Lq, cols, cols, 128, 64, true);
   if (rc) return rc;
   op.args.Lq = Lq;
   op.args.heads = heads;
@@ -442,7 +443,9 @@ static int make_attn(AttnOp& op, const void* q, int Lq, int heads, const void* k
   op.args.status = status;
   return 0;
 }
-static int run(const AttnOp& op, cudaStream_t s) { return attention_launch(op.q, op.k0, op.v0, op.k1, op.v1, op.args, s); }
+static int run(const AttnOp& op, cudaStream_t s) {
+  return attention_launch(op.q, op.k0, op.v0, op.k1, op.v1, op.args, s, &op.o);
+}
 
 // With FW_TRACE_ERRORS=1 in the environment the engine names the first failing call on stderr.
 static bool trace_errors() {

@@ -137,7 +137,10 @@ struct AttnArgs {
   int* status = nullptr;
 };
 // Q [Lq, heads*128] (tmQ box [128, 64]); K/V segments [keys, heads*128] (box [128, 64]).
+// tmO (optional): the output [Lq, heads*128] with box [128, 64], 128-byte swizzle; O is then
+// written by TMA stores.
 int attention_launch(const CUtensorMap& tmQ, const CUtensorMap& tmK0, const CUtensorMap& tmV0,
-                     const CUtensorMap& tmK1, const CUtensorMap& tmV1, const AttnArgs& a, cudaStream_t s);
+                     const CUtensorMap& tmK1, const CUtensorMap& tmV1, const AttnArgs& a, cudaStream_t s,
+                     const CUtensorMap* tmO = nullptr);
 
 }  // namespace fw

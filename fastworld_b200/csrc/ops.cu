@@ -238,6 +238,8 @@ int fw_attention(const void* q, int Lq, int heads, const void* k0, const void* v
   if (!rc) rc = make_tmap_2d(&tv0, v0, 2, max_keys0, cols, cols, 128, 64, true);
   if (!rc) rc = make_tmap_2d(&tk1, k1, 2, max_keys1, cols, cols, 128, 64, true);
   if (!rc) rc = make_tmap_2d(&tv1, v1, 2, max_keys1, cols, cols, 128, 64, true);
+  CUtensorMap to;
+  if (!rc) rc = make_tmap_2d(&to, out, 2, Lq, cols, cols, 128, 64, true);
   if (rc) return rc;
   AttnArgs a;
   a.Lq = Lq;
@@ -249,7 +251,7 @@ int fw_attention(const void* q, int Lq, int heads, const void* k0, const void* v
   a.ld_out = cols;
   a.scale_log2 = (float)(1.4426950408889634 / std::sqrt(128.0));
   a.status = status;
-  return attention_launch(tq, tk0, tv0, tk1, tv1, a, reinterpret_cast<cudaStream_t>(stream));
+  return attention_launch(tq, tk0, tv0, tk1, tv1, a, reinterpret_cast<cudaStream_t>(stream), &to);
 }
 
 }  // extern "C"
