@@ -3,8 +3,8 @@ drift over 16 chunks must be reported").
 
 Two steps, so the slow CPU side can run on any host:
 
-    python tests/drift_report.py run --config mg2 --chunks 16 --out gpurun_out/drift_mg2.pt   # GPU
-    python tests/drift_report.py compare gpurun_out/drift_mg2.pt [--threads N]                # CPU
+    python tests/drift_report.py run --config mg2 --chunks 16 --out drift_mg2.pt   # GPU
+    python tests/drift_report.py compare drift_mg2.pt [--threads N]                # CPU
 
 ``run`` plays chunks 0..N-1 of one seeded path through ``B200StaticMG`` (each chunk on the
 engine's own state) and saves, per chunk, the inputs drawn on the device (x_in, noise), the
@@ -103,7 +103,7 @@ if __name__ == "__main__":
     r = sub.add_parser("run")
     r.add_argument("--config", default="mg2")
     r.add_argument("--chunks", type=int, default=16)
-    r.add_argument("--out", default="gpurun_out/drift_mg2.pt")
+    r.add_argument("--out", default="drift_mg2.pt")
     c = sub.add_parser("compare")
     c.add_argument("file")
     c.add_argument("--threads", type=int, default=0)
