@@ -511,7 +511,7 @@ def tp_parity_variant(rank, world, local, ctl):
 
 # ---------------------------------------------------------------- single-kernel workloads
 # Small, self-terminating runs of one kernel for ncu captures and CUDA-event timing:
-#   python bench.py --kernel gemm|gemm_resid|attn|ln|rms|copy|fp8_peak [--reps 3]
+#   python bench.py --kernel gemm|gemm_resid|attn|ln|ln14|rms|copy|fp8_peak [--reps 3]
 #   python bench.py --kernel chunk [--chunks 2] [--config mg2|mg2_fp8]   (eager chunks)
 
 def chunk(n: int, config: str = "mg2") -> None:
@@ -715,8 +715,9 @@ def copy(reps: int) -> None:
 
 
 KERNELS = {"chunk": lambda a: chunk(a.chunks, a.config), "gemm": lambda a: gemm(a.reps),
-           "gemm_resid": lambda a: gemm_resid(a.reps), "attn": lambda a: attn(a.reps), "ln": lambda a: ln(a.reps), "ln14": lambda a: ln14(a.reps),
-           "rms": lambda a: rms(a.reps), "copy": lambda a: copy(a.reps), "fp8_peak": lambda a: fp8_peak(a.reps)}
+           "gemm_resid": lambda a: gemm_resid(a.reps), "attn": lambda a: attn(a.reps), "ln": lambda a: ln(a.reps),
+           "ln14": lambda a: ln14(a.reps), "rms": lambda a: rms(a.reps), "copy": lambda a: copy(a.reps),
+           "fp8_peak": lambda a: fp8_peak(a.reps)}
 
 
 def main():
