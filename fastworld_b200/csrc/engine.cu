@@ -382,6 +382,7 @@ static int make_gemm(GemmOp& op, const void* A, int M, int K, int lda, const voi
   op.args.K = K;
   op.args.epi = epi;
   op.args.status = status;
+  op.args.b_static = true;   // B is always a weight (or a derived weight) in the engine
   op.valid = true;
   rc = resid_to_tma(op);
   if (!rc && !op.pair) rc = make_out_tmaps(op.args, op.o);
@@ -478,6 +479,7 @@ static int make_lin(fw_handle* h, GemmOp& op, const std::string& wname, const vo
   op.args.sa = h->sa;
   op.args.sw = P<float>(h, wname + ".sw");
   op.args.status = h->status;
+  op.args.b_static = true;
   op.valid = true;
   FW_TRY(resid_to_tma(op));
   FW_TRY(make_out_tmaps(op.args, op.o));

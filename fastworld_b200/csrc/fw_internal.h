@@ -100,6 +100,9 @@ struct GemmArgs {
   // same A by B_g (tensor map tmB_grp[g], in device memory, 64-byte aligned), adds bias_grp[g]
   // and writes the out[] segments shifted by g * out_grp_stride elements.
   int groups = 1;
+  // B is not written by any kernel of the stream (the engine's weights): its first loads may be
+  // issued before the programmatic-dependent-launch wait
+  bool b_static = false;
   const CUtensorMap* tmB_grp = nullptr;
   const __nv_bfloat16* const* bias_grp = nullptr;
   long long out_grp_stride = 0;

@@ -104,6 +104,18 @@ __global__ void __launch_bounds__(320, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Weights that no kernel of the stream writes (args.b_static) are fetched for the CTA's first
+  // tile before the dependency wait: their loads overlap the previous kernel's tail.  The stages
+  // are still free at this point (first pass over the ring), so no empty-barrier wait is needed.
+  const int pre = (args.b_static && args.groups == 1 && blockIdx.x < num_tiles)
+                      ? (num_kb < C::STAGES ? num_kb : C::STAGES) : 0;
+  if (warp == 0 && lane == 0 && pre > 0) {
+    const int nb0 = (blockIdx.x % tpg) / num_m;
+    for (int kb = 0; kb < pre; ++kb) {
+      mbar_arrive_expect_tx(full + kb, C::STAGE);   // both halves of the stage: B now, A after the wait
+      tma_load_2d(sB + kb * C::B_BYTES, &tmB, full + kb, kb * KE, nb0 * BN);
+    }
+  }
   pdl_wait();   // everything below reads or writes data of earlier kernels
 
   if (warp == 0) {
@@ -115,13 +127,17 @@ __global__ void __launch_bounds__(320, 1)
         const int g = t / tpg, mb = (t - g * tpg) % num_m, nb = (t - g * tpg) / num_m;
         const CUtensorMap* mB = args.groups > 1 ? args.tmB_grp + g : &tmB;
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait(empty + stage, phase ^ 1u, abort_flag, args.status, DEV_TIMEOUT_PRODUCER)) {
-            ok = false;
-            break;
+          if (t == (int)blockIdx.x && kb < pre) {   // B already in flight; only A is left
+            tma_load_2d(sA + stage * C::A_BYTES, &tmA, full + stage, kb * KE, mb * 128);
+          } else {
+            if (!mbar_wait(empty + stage, phase ^ 1u, abort_flag, args.status, DEV_TIMEOUT_PRODUCER)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(full + stage, C::STAGE);
+            tma_load_2d(sA + stage * C::A_BYTES, &tmA, full + stage, kb * KE, mb * 128);
+            tma_load_2d(sB + stage * C::B_BYTES, mB, full + stage, kb * KE, nb * BN);
           }
-          mbar_arrive_expect_tx(full + stage, C::STAGE);
-          tma_load_2d(sA + stage * C::A_BYTES, &tmA, full + stage, kb * KE, mb * 128);
-          tma_load_2d(sB + stage * C::B_BYTES, mB, full + stage, kb * KE, nb * BN);
           used |= 1u << stage;
           last_par = (last_par & ~(1u << stage)) | (phase << stage);
           if (++stage == C::STAGES) {
