@@ -26,7 +26,8 @@ weights and inputs.  Metric: frames per second (12 pixel frames per chunk), whol
   tensor-parallel over the N ranks, every N); for N > 1 also ``explore`` (configs[3]: 64 sessions
   from one image, prefix-cache branching, cross-GPU checkpoint restores over NVLink) and
   ``tp_parity`` (a tensor-parallel test model over the N ranks: ranks bit-identical, latents
-  against the CPU oracle).
+  against the CPU oracle); ``taehv`` (every N: the TAEHV decoder on one chunk's latent, ms per
+  chunk, TFLOP/s, and the served frame rate of DiT chunk + decoder).
 
 Multi-GPU (torchrun): every rank runs its own session; there is no collective on the data path
 of ``value`` (sessions are independent).  Timing is bracketed by a barrier and synchronize; the
@@ -369,6 +370,8 @@ def run_ours(args):
         variants["tp14b"] = guarded(lambda: tp14b_variant(rank, world, local, ctl), world, ctl)
     if world > 1 and not args.no_tp and agree(time.time() - t_start < args.variant_budget, world, ctl):
         variants["tp_parity"] = guarded(lambda: tp_parity_variant(rank, world, local, ctl), world, ctl)
+    if not args.no_taehv and agree(time.time() - t_start < args.variant_budget, world, ctl):
+        variants["taehv"] = guarded(lambda: taehv_variant(ms, rank, world, ctl), world, ctl)
     line = None
     if rank == 0:
         fps = world * FRAMES_PER_CHUNK / (ms / 1e3)
@@ -434,6 +437,28 @@ def explore_variant(S, rank, world, ctl):
     allres = [None] * world
     torch.distributed.all_gather_object(allres, res, group=ctl)
     return explore.summarize(allres, world, 64, 16, 6, 2, "mg2") if rank == 0 else None
+
+
+def taehv_variant(chunk_ms, rank, world, ctl):
+    """The decoder after the DiT (the reference's TinyVAE, TAEHV taew2_1): every rank decodes its
+    own session's chunks; decode time is the max over ranks."""
+    from fastworld_b200.vae import TAEW2_1
+    dms, vae = taehv_decode_ms(10)
+    del vae
+    torch.cuda.empty_cache()
+    if world > 1:
+        got = [None] * world
+        torch.distributed.all_gather_object(got, dms, group=ctl)
+        dms = max(got)
+    peak_tf, _, peak_kind = peaks()
+    tf = TAEW2_1.flops() / 1e12 / (dms / 1e3)
+    fr = TAEW2_1.frames_out
+    return {"workload": "TinyVAE (TAEHV taew2_1) streaming decode of one MG2 latent chunk: [1, 16, 3, 44, 80] -> "
+                        "12 frames of 352 x 640 (fp16 activations, fp32 accumulate; one library-held graph)",
+            "ms_per_chunk": dms, "frames_per_s": world * fr / (dms / 1e3), "algorithmic_gflop": TAEW2_1.flops() / 1e9,
+            "tflops": tf, "frac_of_peak": tf / peak_tf, "peak_kind": f"{peak_kind} bf16 burst",
+            "dit_plus_decoder_fps": world * fr / ((chunk_ms + dms) / 1e3),
+            "reference_ms_per_chunk_published": 10.4}
 
 
 def tp14b_variant(rank, world, local, ctl):
@@ -714,7 +739,33 @@ def copy(reps: int) -> None:
     print(f"copy_kernel 649 MB: {ms * 1e3:.1f} us, {2 * nb / ms / 1e6:.0f} GB/s (read + write)")
 
 
-KERNELS = {"chunk": lambda a: chunk(a.chunks, a.config), "gemm": lambda a: gemm(a.reps),
+def taehv_decode_ms(replays: int = 10):
+    """TinyVAE (taew2_1) on one MG2 latent chunk: warm graph replays timed with CUDA events.
+    Returns (ms per chunk, the decoder) after checking the device status."""
+    from fastworld_b200.vae import TAEW2_1, TinyVAE
+    cfg = TAEW2_1
+    vae = TinyVAE("cuda", cfg=cfg, seed=0)
+    g = torch.Generator(device="cuda").manual_seed(0)
+    lat = torch.randn(1, 16, cfg.lat_frames, cfg.lat_h, cfg.lat_w, device="cuda", generator=g).bfloat16()
+    for _ in range(3):
+        vae.decode(lat)
+    ms = _events_ms(vae.graph.replay, replays)
+    if vae.device_status() != 0:
+        raise RuntimeError(f"taehv device status {vae.device_status()}")
+    return ms, vae
+
+
+def taehv(reps: int) -> None:
+    """The TAEHV decoder on one MG2 latent chunk (12 frames of 352 x 640): graph replays."""
+    from fastworld_b200.vae import TAEW2_1
+    ms, vae = taehv_decode_ms(max(reps, 3))
+    n = vae.graph.num_nodes()
+    tf = TAEW2_1.flops() / 1e12 / (ms / 1e3)
+    print(f"taehv decode: {ms:.3f} ms per chunk ({n} graph nodes), {TAEW2_1.frames_out / (ms / 1e3):.0f} frames/s, "
+          f"{TAEW2_1.flops() / 1e9:.1f} GFLOP algorithmic = {tf:.0f} TFLOP/s")
+
+
+KERNELS = {"chunk": lambda a: chunk(a.chunks, a.config), "gemm": lambda a: gemm(a.reps), "taehv": lambda a: taehv(a.reps),
            "gemm_resid": lambda a: gemm_resid(a.reps), "attn": lambda a: attn(a.reps), "ln": lambda a: ln(a.reps),
            "ln14": lambda a: ln14(a.reps), "rms": lambda a: rms(a.reps), "copy": lambda a: copy(a.reps),
            "fp8_peak": lambda a: fp8_peak(a.reps)}
@@ -734,6 +785,7 @@ def main():
     ap.add_argument("--no-fp8", action="store_true", help="skip the e4m3 variant (configs[2])")
     ap.add_argument("--no-tp", action="store_true", help="skip the 14B tensor-parallel variants (configs[4])")
     ap.add_argument("--no-explore", action="store_true", help="skip the explore variant (configs[3], N > 1)")
+    ap.add_argument("--no-taehv", action="store_true", help="skip the decoder variant")
     ap.add_argument("--variant-budget", type=float, default=600.0,
                     help="start no further variant once this many seconds have passed")
     args = ap.parse_args()

@@ -14,7 +14,7 @@ LIB_PATH = os.path.join(HERE, "libfastworld_b200.so")
 FW_MAX_ACTION_BLOCKS = 64
 FW_MAX_STEPS = 16
 KIND_WEIGHT, KIND_STATE, KIND_INPUT, KIND_OUTPUT, KIND_WORKSPACE, KIND_STATUS, KIND_DERIVED = range(7)
-DT_BF16, DT_F32, DT_I32, DT_U8 = range(4)
+DT_BF16, DT_F32, DT_I32, DT_U8, DT_F16 = range(5)
 EPI_BF16, EPI_GELU_BF16, EPI_RESID_F32, EPI_F32, EPI_GELU_ERF_BF16 = range(5)
 
 
@@ -48,6 +48,11 @@ class FwPrepArgs(ctypes.Structure):
     _fields_ = [("chunk", ctypes.c_int), ("seed", ctypes.c_ulonglong), ("draw_noise", ctypes.c_int),
                 ("cond", ctypes.c_void_p), ("cond_frames", ctypes.c_int), ("j_lo", ctypes.c_int),
                 ("n_act", ctypes.c_int), ("actions", ctypes.c_float * (FW_PREP_MAX_ACT * 8))]
+
+
+class FwTaehvConfig(ctypes.Structure):
+    _fields_ = [("lat_ch", ctypes.c_int), ("lat_frames", ctypes.c_int), ("lat_h", ctypes.c_int),
+                ("lat_w", ctypes.c_int), ("channels", ctypes.c_int * 4), ("time_up", ctypes.c_int * 3)]
 
 
 _SIGS = {
@@ -93,6 +98,14 @@ _SIGS = {
                                        ctypes.c_void_p]),
     "fw_graph_begin": (ctypes.c_int, [ctypes.c_void_p]),
     "fw_graph_end": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)]),
+    "fw_taehv_create": (ctypes.c_int, [ctypes.POINTER(FwTaehvConfig), ctypes.POINTER(ctypes.c_void_p)]),
+    "fw_taehv_tensor_count": (ctypes.c_int, [ctypes.c_void_p]),
+    "fw_taehv_tensor_info_at": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(FwTensorInfo)]),
+    "fw_taehv_bind": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_char_p, ctypes.c_void_p, ctypes.c_size_t]),
+    "fw_taehv_finalize": (ctypes.c_int, [ctypes.c_void_p]),
+    "fw_taehv_decode": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
+    "fw_taehv_status": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int)]),
+    "fw_taehv_destroy": (None, [ctypes.c_void_p]),
     "fw_graph_launch": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
     "fw_graph_nodes": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_size_t)]),
     "fw_graph_destroy": (None, [ctypes.c_void_p]),

@@ -60,6 +60,7 @@ extern "C" {
 #define FW_F32 1
 #define FW_I32 2
 #define FW_U8 3
+#define FW_F16 4
 
 #define FW_MAX_ACTION_BLOCKS 64
 #define FW_MAX_STEPS 16
@@ -213,6 +214,36 @@ void fw_graph_destroy(fw_graph* g);
 /* Let kernels on the current device read and write `peer`'s memory (checkpoints placed on
  * another GPU; fastworld/prefix_cache.py:85-87 keeps every checkpoint on the GPU that made it). */
 int fw_peer_access(int peer);
+
+/* ---- TAEHV streaming video decoder (TinyVAE, fastworld/models/mg2/vae.py:95-124) ----
+ * Decodes one latent chunk "lat" [16, lat_frames, lat_h, lat_w] (fp16, as the reference casts it) into
+ * lat_frames * prod(time_up) RGB frames [frames, 3, 8 lat_h, 8 lat_w] fp32 in [-1, 1], carrying
+ * the streaming state (each MemBlock's last input frame, tensor "mem") from chunk to chunk.
+ * Tensors are registered and bound like the session engine's (fw_taehv_tensor_info_at /
+ * fw_taehv_bind): weights fp16 [Cout, taps * Cin] with K ordered (tap, input channel), biases
+ * fp32; "conv_in.w" is [C0, 192]: 9 taps x 16 latent channels, then 48 zero columns;
+ * "conv_out.w" / "conv_out.b" are padded to 32 output rows (3 used).  fw_taehv_finalize
+ * allocates the activation buffers (one cudaMalloc) and builds the TMA descriptors;
+ * fw_taehv_decode launches the whole decoder (no host synchronisation; graph-capturable).
+ * A zeroed "mem" is the state of a new stream; the caller drops the first
+ * prod(time_up) - 1 frames of a stream's first chunk (TAEHV's frames_to_trim). */
+typedef struct fw_taehv_config {
+  int lat_ch;          /* 16 */
+  int lat_frames;      /* latent frames per chunk (MG2: 3) */
+  int lat_h, lat_w;    /* latent size (MG2: 44 x 80); lat_w a multiple of 16 */
+  int channels[4];     /* stage widths (taew2_1: 256, 128, 64, 64), multiples of 64, <= 256 */
+  int time_up[3];      /* frames per input frame at the three upsampling steps (1, 2, 2) */
+} fw_taehv_config;
+typedef struct fw_taehv fw_taehv;
+int fw_taehv_create(const fw_taehv_config* cfg, fw_taehv** out);
+int fw_taehv_tensor_count(const fw_taehv* h);
+int fw_taehv_tensor_info_at(const fw_taehv* h, int index, fw_tensor_info* info);
+int fw_taehv_bind(fw_taehv* h, const char* name, void* ptr, size_t bytes);
+int fw_taehv_finalize(fw_taehv* h);
+int fw_taehv_decode(fw_taehv* h, void* stream);
+/* Device status word (0 = every bounded wait completed); synchronous. */
+int fw_taehv_status(fw_taehv* h, int* out);
+void fw_taehv_destroy(fw_taehv* h);
 
 /* ---- failure-path self-tests (no counterpart in the reference, which has no device-side
  * failure detection) ----
