@@ -471,7 +471,7 @@ struct fw_taehv {
   };
   std::vector<Tensor> tensors;
   bool finalized = false;
-  void* work = nullptr;   // activations, one allocation
+  void* work = nullptr;   // activations (the bound "work" tensor)
   int* status = nullptr;
   // plan
   int T0 = 0, h = 0, w = 0;
@@ -485,6 +485,25 @@ struct fw_taehv {
 namespace {
 
 using fw::taehv::Conv;
+
+// Activation buffers, in order: the first conv's neighbourhood tensor, per stage 3 block inputs,
+// 2 temporaries and the stage output, the three upsampled TGrow outputs, the last conv's input.
+std::vector<size_t> work_layout(const fw_taehv* h, size_t* total) {
+  std::vector<size_t> sizes, off;
+  sizes.push_back((size_t)h->T0 * h->h * h->w * 192 * 2);
+  auto stage_bytes = [&](int s, int Cc) { return (size_t)h->F[s] * (h->h << s) * (h->w << s) * Cc * 2; };
+  for (int s = 0; s < 3; ++s)
+    for (int k = 0; k < 6; ++k) sizes.push_back(stage_bytes(s, h->C[s]));
+  for (int s = 0; s < 3; ++s) sizes.push_back(stage_bytes(s + 1, h->C[s]));
+  sizes.push_back(stage_bytes(3, h->C[3]));
+  size_t t = 0;
+  for (size_t b : sizes) {
+    off.push_back(t);
+    t += (b + 1023) & ~(size_t)1023;
+  }
+  *total = t;
+  return off;
+}
 
 int find(const fw_taehv* h, const char* name) {
   for (size_t i = 0; i < h->tensors.size(); ++i)
@@ -505,7 +524,7 @@ void add(fw_taehv* h, const std::string& name, int kind, int dtype, std::initial
     n *= (size_t)d;
   }
   for (; i < 5; ++i) t.shape[i] = 0;
-  t.bytes = n * (dtype == FW_F32 ? 4 : 2);
+  t.bytes = n * (dtype == FW_F32 || dtype == FW_I32 ? 4 : (dtype == FW_U8 ? 1 : 2));
   h->tensors.push_back(t);
 }
 
@@ -559,6 +578,10 @@ int fw_taehv_create(const fw_taehv_config* cfg, fw_taehv** out) {
   int64_t mem = 0;
   for (int s = 0; s < 3; ++s) mem += 3LL * h->C[s] * ((int64_t)h->h << s) * ((int64_t)h->w << s);
   add(h, "mem", FW_KIND_STATE, FW_F16, {mem});
+  size_t work = 0;
+  work_layout(h, &work);
+  add(h, "work", FW_KIND_WORKSPACE, FW_U8, {(int64_t)work});
+  add(h, "status", FW_KIND_STATUS, FW_I32, {4});
   *out = h;
   return FW_OK;
 }
@@ -592,25 +615,11 @@ int fw_taehv_finalize(fw_taehv* h) {
   if (!h || h->finalized) return FW_EINVAL;
   for (const auto& t : h->tensors)
     if (!t.ptr) return FW_ENOTBOUND;
-  // work buffers: im2col of the first conv, then per stage 3 block inputs, 2 temporaries and
-  // the stage output, the three upsampled tensors and the last conv's input
-  const int T0 = h->T0;
-  std::vector<size_t> sizes;
-  sizes.push_back((size_t)T0 * h->h * h->w * 192 * 2);
-  auto stage_bytes = [&](int s, int Cc) { return (size_t)h->F[s] * (h->h << s) * (h->w << s) * Cc * 2; };
-  for (int s = 0; s < 3; ++s)
-    for (int k = 0; k < 6; ++k) sizes.push_back(stage_bytes(s, h->C[s]));
-  for (int s = 0; s < 3; ++s) sizes.push_back(stage_bytes(s + 1, h->C[s]));   // upsampled TGrow outputs
-  sizes.push_back(stage_bytes(3, h->C[3]));
   size_t total = 0;
-  std::vector<size_t> off;
-  for (size_t b : sizes) {
-    off.push_back(total);
-    total += (b + 1023) & ~(size_t)1023;
-  }
-  if (cudaMalloc(&h->work, total + 256) != cudaSuccess) return FW_ECUDA;
-  h->status = reinterpret_cast<int*>(static_cast<char*>(h->work) + total);
-  cudaMemset(h->status, 0, 256);
+  const std::vector<size_t> off = work_layout(h, &total);
+  const int T0 = h->T0;
+  h->work = ptr(h, "work");
+  h->status = static_cast<int*>(ptr(h, "status"));
   auto buf = [&](int i) { return static_cast<char*>(h->work) + off[i]; };
   h->im = reinterpret_cast<__half*>(buf(0));
   // buffers of stage s: in[k] = buf(1 + 6 s + k) (k < 3), tmp a / b = + 3 / + 4, out = + 5
@@ -763,10 +772,6 @@ int fw_taehv_status(fw_taehv* h, int* out) {
   return cudaMemcpy(out, h->status, sizeof(int), cudaMemcpyDeviceToHost) == cudaSuccess ? FW_OK : FW_ECUDA;
 }
 
-void fw_taehv_destroy(fw_taehv* h) {
-  if (!h) return;
-  if (h->work) cudaFree(h->work);
-  delete h;
-}
+void fw_taehv_destroy(fw_taehv* h) { delete h; }
 
 }  // extern "C"

@@ -181,7 +181,8 @@ def make_config(cfg: TaehvConfig) -> _lib.FwTaehvConfig:
     return c
 
 
-_DT = {_lib.DT_BF16: torch.bfloat16, _lib.DT_F32: torch.float32, _lib.DT_F16: torch.float16}
+_DT = {_lib.DT_BF16: torch.bfloat16, _lib.DT_F32: torch.float32, _lib.DT_F16: torch.float16, _lib.DT_I32: torch.int32,
+       _lib.DT_U8: torch.uint8}
 
 
 class TinyVAE:

@@ -222,9 +222,10 @@ int fw_peer_access(int peer);
  * Tensors are registered and bound like the session engine's (fw_taehv_tensor_info_at /
  * fw_taehv_bind): weights fp16 [Cout, taps * Cin] with K ordered (tap, input channel), biases
  * fp32; "conv_in.w" is [C0, 192]: 9 taps x 16 latent channels, then 48 zero columns;
- * "conv_out.w" / "conv_out.b" are padded to 32 output rows (3 used).  fw_taehv_finalize
- * allocates the activation buffers (one cudaMalloc) and builds the TMA descriptors;
- * fw_taehv_decode launches the whole decoder (no host synchronisation; graph-capturable).
+ * "conv_out.w" / "conv_out.b" are padded to 32 output rows (3 used); "work" is the activation
+ * workspace and "status" the int32[4] device status word (zeroed).  fw_taehv_finalize builds the
+ * TMA descriptors; fw_taehv_decode launches the whole decoder (no host synchronisation;
+ * graph-capturable).
  * A zeroed "mem" is the state of a new stream; the caller drops the first
  * prod(time_up) - 1 frames of a stream's first chunk (TAEHV's frames_to_trim). */
 typedef struct fw_taehv_config {

@@ -128,6 +128,7 @@ def test_capi_tensor_table():
             infos[inf.name.decode()] = (inf.kind, tuple(inf.shape[j] for j in range(inf.ndim)), inf.bytes)
         assert infos["mem"][2] == TAEW2_1.state_bytes()
         assert infos["lat"][1] == (16, 3, 44, 80) and infos["rgb"][1] == (12, 3, 352, 640)
+        assert 1.0e9 < infos["work"][2] < 1.3e9 and infos["work"][0] == _lib.KIND_WORKSPACE
         pk = pack_weights(TAEW2_1, synthetic_state_dict(TAEW2_1, 0))
         weights = {k for k, v in infos.items() if v[0] == _lib.KIND_WEIGHT}
         assert weights == set(pk)
