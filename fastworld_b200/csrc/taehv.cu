@@ -54,22 +54,37 @@ enum : int { EK_STORE = 0, EK_UP = 1, EK_RGB = 2 };
 
 constexpr int kSmemLimit = 232448;   // opt-in dynamic shared memory per CTA
 
-template <int BN, int EK>
+// How the A operand (and B) reach shared memory:
+//   LM_TAP    one pipeline unit per (tap, 64-channel block): A = the 128 pixels at the tap's
+//             offset (4-D box {64, 16, 8, 1}), B = the tap's weight block; a 3 x 3 conv reads
+//             every input byte 9 times from L2
+//   LM_HALO   one unit per (64-channel block, dx): A = the tile's 10 input rows (8 + halo) at
+//             x offset dx (box {64, 16, 10, 1}, 20 KB), from which the three taps dy = -1, 0, 1
+//             are the 1024-byte-aligned windows at rows 0, 1, 2 (2048 bytes apart); B = those
+//             three taps' weight blocks.  Input bytes are read 3 times (x halo copies).
+//   LM_HALO_RES  LM_HALO with all weights resident in shared memory (loaded once per CTA)
+enum : int { LM_TAP = 0, LM_HALO = 1, LM_HALO_RES = 2 };
+
+template <int BN, int EK, int LM>
 struct Cfg {
-  static constexpr int A_BYTES = 128 * 64 * 2;
-  static constexpr int B_BYTES = BN * 64 * 2;
+  static constexpr int A_BYTES = LM == LM_TAP ? 128 * 128 : 160 * 128;
+  static constexpr int B_BYTES = LM == LM_TAP ? BN * 128 : (LM == LM_HALO ? 3 * BN * 128 : 0);
   static constexpr int STAGE = A_BYTES + B_BYTES;
+  // resident weights: 9 taps x one 64-channel block
+  static constexpr int RES = LM == LM_HALO_RES ? 9 * BN * 128 : 0;
   // per epilogue warp: EK_STORE one [32 pixels x 128 B] box; EK_UP two upsampled rows
   static constexpr int BOX = EK == EK_STORE ? 4096 : (EK == EK_UP ? 8192 : 0);
   static constexpr int EPI = 8 * BOX;
-  static constexpr int FIT = (kSmemLimit - 2048 - EPI) / STAGE;
+  static constexpr int FIT = (kSmemLimit - 2048 - EPI - RES) / STAGE;
   static constexpr int STAGES = FIT > 8 ? 8 : FIT;
-  static constexpr int BAR_OFF = STAGES * STAGE;
+  static constexpr int RES_OFF = STAGES * STAGE;
+  static constexpr int BAR_OFF = RES_OFF + RES;
   static constexpr int EPI_OFF = BAR_OFF + 1024;
   static constexpr int SMEM = EPI_OFF + EPI + 1024;
   static constexpr uint32_t TMEM_COLS = 2 * BN;
   static_assert(STAGES >= 3, "pipeline too shallow");
   static_assert(SMEM <= kSmemLimit, "shared memory");
+  static_assert(STAGE % 1024 == 0 && RES % 1024 == 0, "1024-byte aligned operands");
 };
 
 struct ConvArgs {
@@ -91,29 +106,34 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-template <int BN, int EK>
+template <int BN, int EK, int LM>
 __global__ void __launch_bounds__(320, 1)
     conv_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmM,
                 const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmY, const ConvArgs a) {
-  using C = Cfg<BN, EK>;
+  using C = Cfg<BN, EK, LM>;
+  constexpr bool HALO = LM != LM_TAP;
   pdl_trigger();
   extern __shared__ uint8_t smem_raw[];
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
   uint8_t* smem = smem_raw + pad;
   uint8_t* sA = smem;
   uint8_t* sB = smem + C::STAGES * C::A_BYTES;
+  uint8_t* sR = smem + C::RES_OFF;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
   uint64_t* empty = full + C::STAGES;
   uint64_t* tfull = empty + C::STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* res_full = drain + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(res_full + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nxb = a.W >> 4, nyb = (a.H + 7) >> 3;
   const int num_m = a.T * nyb * nxb, num_n = (a.N + BN - 1) / BN;
   const int num_tiles = num_m * num_n;
-  const int cpt = a.ch0 + a.ch1, num_kb = a.taps * cpt;
+  const int cpt = a.ch0 + a.ch1;
+  // pipeline units per tile: (tap, block) or (block, dx)
+  const int num_kb = HALO ? 3 * cpt : a.taps * cpt;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
@@ -125,6 +145,7 @@ __global__ void __launch_bounds__(320, 1)
       mbar_init(tempty + b, 128);   // the four warps of epilogue group b
     }
     mbar_init(drain, 1);
+    mbar_init(res_full, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -140,14 +161,20 @@ __global__ void __launch_bounds__(320, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  // The weights are static: the first tile's weight blocks are requested before the wait on
-  // the previous kernel (the stages are still free on the first pass over the ring).
-  const int pre = blockIdx.x < num_tiles ? (num_kb < C::STAGES ? num_kb : C::STAGES) : 0;
-  if (warp == 0 && lane == 0) {
-    const int nb0 = blockIdx.x / num_m;
-    for (int kb = 0; kb < pre; ++kb) {
-      mbar_arrive_expect_tx(full + kb, C::STAGE);
-      tma_load_2d(sB + kb * C::B_BYTES, &tmW, full + kb, kb * 64, nb0 * BN);
+  // The weights are static: they are requested before the wait on the previous kernel (the
+  // resident copy, or the first tile's blocks while the ring's stages are still free).
+  int pre = 0;
+  if (warp == 0 && lane == 0 && blockIdx.x < num_tiles) {
+    if constexpr (LM == LM_HALO_RES) {
+      mbar_arrive_expect_tx(res_full, C::RES);
+      for (int p = 0; p < 9; ++p) tma_load_2d(sR + p * BN * 128, &tmW, res_full, p * 64, 0);
+    } else if constexpr (LM == LM_TAP) {
+      pre = num_kb < C::STAGES ? num_kb : C::STAGES;
+      const int nb0 = blockIdx.x / num_m;
+      for (int kb = 0; kb < pre; ++kb) {
+        mbar_arrive_expect_tx(full + kb, C::STAGE);
+        tma_load_2d(sB + kb * C::B_BYTES, &tmW, full + kb, kb * 64, nb0 * BN);
+      }
     }
   }
   pdl_wait();
@@ -162,15 +189,23 @@ __global__ void __launch_bounds__(320, 1)
         const int xb = m % nxb, r = m / nxb, yb = r % nyb, f = r / nyb;
         const int x0 = xb * 16, y0 = yb * 8;
         for (int kb = 0; kb < num_kb; ++kb) {
-          const int p = kb / cpt, j = kb - p * cpt;
-          const int dy = a.taps == 9 ? p / 3 - 1 : 0, dx = a.taps == 9 ? p % 3 - 1 : 0;
+          // unit kb: LM_TAP (tap p, block j); halo modes (block j, x offset dx)
+          const int p = HALO ? 0 : kb / cpt, j = HALO ? kb / 3 : kb - p * cpt;
+          const int dy = HALO ? -1 : (a.taps == 9 ? p / 3 - 1 : 0);
+          const int dx = HALO ? kb % 3 - 1 : (a.taps == 9 ? p % 3 - 1 : 0);
           if (!(t == (int)blockIdx.x && kb < pre)) {
             if (!mbar_wait(empty + stage, phase ^ 1u, abort_flag, a.status, DEV_TIMEOUT_PRODUCER)) {
               ok = false;
               break;
             }
             mbar_arrive_expect_tx(full + stage, C::STAGE);
-            tma_load_2d(sB + stage * C::B_BYTES, &tmW, full + stage, kb * 64, nb * BN);
+            if constexpr (LM == LM_TAP) {
+              tma_load_2d(sB + stage * C::B_BYTES, &tmW, full + stage, kb * 64, nb * BN);
+            } else if constexpr (LM == LM_HALO) {   // weight blocks of taps (dy, dx), dy = -1, 0, 1
+              for (int d = 0; d < 3; ++d)
+                tma_load_2d(sB + stage * C::B_BYTES + d * BN * 128, &tmW, full + stage,
+                            ((d * 3 + dx + 1) * cpt + j) * 64, nb * BN);
+            }
           }
           uint8_t* dst = sA + stage * C::A_BYTES;
           if (j < a.ch0)
@@ -190,6 +225,8 @@ __global__ void __launch_bounds__(320, 1)
       volatile int no_abort = 0;
       for (int s = 0; s < C::STAGES; ++s)
         if (used >> s & 1u) mbar_wait(full + s, last_par >> s & 1u, &no_abort, a.status, DEV_TIMEOUT_DRAIN);
+      if (LM == LM_HALO_RES && blockIdx.x < num_tiles)
+        mbar_wait(res_full, 0, &no_abort, a.status, DEV_TIMEOUT_DRAIN);
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -198,6 +235,8 @@ __global__ void __launch_bounds__(320, 1)
       uint32_t phase = 0;
       bool ok = true;
       int i = 0;
+      if (LM == LM_HALO_RES && blockIdx.x < num_tiles)
+        ok = mbar_wait(res_full, 0, abort_flag, a.status, DEV_TIMEOUT_MMA);
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++i) {
         const int acc = i & 1;
         const uint32_t acc_phase = (uint32_t)(i >> 1) & 1u;
@@ -211,10 +250,26 @@ __global__ void __launch_bounds__(320, 1)
           }
           tc_fence_after();
           const uint32_t a0 = smem_u32(sA + stage * C::A_BYTES), b0 = smem_u32(sB + stage * C::B_BYTES);
+          // kind::f16; the instruction descriptor selects fp16 operands
+          if constexpr (LM == LM_TAP) {
 #pragma unroll
-          for (int k = 0; k < 4; ++k)   // kind::f16; the instruction descriptor selects fp16 operands
-            umma_bf16(d, sdesc_sw128(a0 + k * 32, 16, 1024), sdesc_sw128(b0 + k * 32, 16, 1024), idesc,
-                      (kb | k) != 0);
+            for (int k = 0; k < 4; ++k)
+              umma_bf16(d, sdesc_sw128(a0 + k * 32, 16, 1024), sdesc_sw128(b0 + k * 32, 16, 1024), idesc,
+                        (kb | k) != 0);
+          } else {
+            const int dxi = kb % 3;
+#pragma unroll
+            for (int dyi = 0; dyi < 3; ++dyi) {
+              // tap (dy, dx): the window at input row dyi of the unit's 10 rows
+              const uint32_t aw = a0 + (uint32_t)(dyi * 2048);
+              const uint32_t bw = LM == LM_HALO ? b0 + (uint32_t)(dyi * BN * 128)
+                                                : smem_u32(sR) + (uint32_t)((dyi * 3 + dxi) * BN * 128);
+#pragma unroll
+              for (int k = 0; k < 4; ++k)
+                umma_bf16(d, sdesc_sw128(aw + k * 32, 16, 1024), sdesc_sw128(bw + k * 32, 16, 1024), idesc,
+                          (kb | dyi | k) != 0);
+            }
+          }
           umma_commit(empty + stage);
           if (++stage == C::STAGES) {
             stage = 0;
@@ -435,21 +490,22 @@ int make_map_w(CUtensorMap* out, const void* base, int rows, int K, int box_rows
   return r == CUDA_SUCCESS ? 0 : FW_EINVAL;
 }
 
-template <int BN, int EK>
+template <int BN, int EK, int LM>
 int launch_conv(const CUtensorMap& x, const CUtensorMap& m, const CUtensorMap& w, const CUtensorMap& y,
                 const ConvArgs& a, cudaStream_t s) {
-  using C = Cfg<BN, EK>;
-  if (cudaFuncSetAttribute(conv_kernel<BN, EK>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
+  using C = Cfg<BN, EK, LM>;
+  if (cudaFuncSetAttribute(conv_kernel<BN, EK, LM>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) !=
+      cudaSuccess)
     return FW_ECUDA;
   const int tiles = a.T * ((a.H + 7) / 8) * (a.W / 16) * ((a.N + BN - 1) / BN);
   const int grid = tiles < num_sms() ? tiles : num_sms();
-  launch_k(conv_kernel<BN, EK>, grid, 320, C::SMEM, s, x, m, w, y, a);
+  launch_k(conv_kernel<BN, EK, LM>, grid, 320, C::SMEM, s, x, m, w, y, a);
   return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
 }
 
 // One launch of the decoder's plan.
 struct Conv {
-  int bn = 0, ek = EK_STORE;
+  int bn = 0, ek = EK_STORE, lm = LM_TAP;
   CUtensorMap x{}, m{}, w{}, y{};
   ConvArgs a{};
 };
@@ -631,9 +687,13 @@ int fw_taehv_finalize(fw_taehv* h) {
   auto wmap = [&](CUtensorMap* m, const std::string& name, int rows, int K, int bn) {
     if (!rc) rc = make_map_w(m, ptr(h, name), rows, K, bn);
   };
-  auto amap = [&](CUtensorMap* m, const void* p, int s, int Cc, int frames) {
-    if (!rc) rc = make_map_nhwc(m, p, frames, h->h << s, h->w << s, Cc, 16, 8);
+  // input maps: 8-row boxes for per-tap loads, 10-row boxes (tile + halo) for the halo modes
+  auto amap = [&](CUtensorMap* m, const void* p, int s, int Cc, int frames, int lm = LM_TAP) {
+    if (!rc) rc = make_map_nhwc(m, p, frames, h->h << s, h->w << s, Cc, 16, lm == LM_TAP ? 8 : 10);
   };
+  // 3 x 3 convs with at most 64 output channels are bound by operand traffic from L2: halo
+  // loads, and resident weights when they fit (one 64-channel input block)
+  auto lm_for = [](int bn, int cpt) { return bn <= 64 ? (cpt == 1 ? LM_HALO_RES : LM_HALO) : LM_TAP; };
   auto omap = [&](CUtensorMap* m, const void* p, int s, int Cc, int frames) {
     if (!rc) rc = make_map_nhwc(m, p, frames, h->h << s, h->w << s, Cc, 16, 2);
   };
@@ -667,21 +727,24 @@ int fw_taehv_finalize(fw_taehv* h) {
       Conv c0, c1, c2;
       // conv over cat[x, past]
       c0.bn = bn;
-      amap(&c0.x, xin, s, Cs, Fs);
-      if (!rc) rc = make_map_nhwc(&c0.m, mem + mem_off, 1, Hs, Ws, Cs, 16, 8);
+      c0.lm = lm_for(bn, 2 * Cs / 64);
+      amap(&c0.x, xin, s, Cs, Fs, c0.lm);
+      if (!rc) rc = make_map_nhwc(&c0.m, mem + mem_off, 1, Hs, Ws, Cs, 16, c0.lm == LM_TAP ? 8 : 10);
       wmap(&c0.w, p + ".w0", Cs, 9 * 2 * Cs, bn);
       omap(&c0.y, ta, s, Cs, Fs);
       c0.a = ConvArgs{Fs, Hs, Ws, 9, Cs / 64, Cs / 64, Cs, (const float*)ptr(h, p + ".b0"), nullptr, 1, 0, 0,
                       nullptr, h->status};
       c1.bn = bn;
-      amap(&c1.x, ta, s, Cs, Fs);
+      c1.lm = lm_for(bn, Cs / 64);
+      amap(&c1.x, ta, s, Cs, Fs, c1.lm);
       c1.m = c1.x;
       wmap(&c1.w, p + ".w1", Cs, 9 * Cs, bn);
       omap(&c1.y, tbuf, s, Cs, Fs);
       c1.a = ConvArgs{Fs, Hs, Ws, 9, Cs / 64, 0, Cs, (const float*)ptr(h, p + ".b1"), nullptr, 1, 0, 0, nullptr,
                       h->status};
       c2.bn = bn;
-      amap(&c2.x, tbuf, s, Cs, Fs);
+      c2.lm = lm_for(bn, Cs / 64);
+      amap(&c2.x, tbuf, s, Cs, Fs, c2.lm);
       c2.m = c2.x;
       wmap(&c2.w, p + ".w2", Cs, 9 * Cs, bn);
       omap(&c2.y, yout, s, Cs, Fs);
@@ -714,7 +777,8 @@ int fw_taehv_finalize(fw_taehv* h) {
       const int Cn = h->C[s + 1], Fn = h->F[s + 1];
       Conv c;
       c.bn = bn_for(Cn);
-      amap(&c.x, up(s), s + 1, Cs, Fn);
+      c.lm = lm_for(c.bn, Cs / 64);
+      amap(&c.x, up(s), s + 1, Cs, Fn, c.lm);
       c.m = c.x;
       wmap(&c.w, "conv" + std::to_string(s) + ".w", Cn, 9 * Cs, c.bn);
       __half* dst = s < 2 ? sb(s + 1, 0) : z;
@@ -728,7 +792,9 @@ int fw_taehv_finalize(fw_taehv* h) {
     Conv c;
     c.bn = 32;
     c.ek = EK_RGB;
-    amap(&c.x, z, 3, h->C[3], h->F[3]);
+    c.lm = LM_HALO_RES;
+    if (h->C[3] != 64) return FW_ESHAPE;   // resident weights: one 64-channel input block
+    amap(&c.x, z, 3, h->C[3], h->F[3], c.lm);
     c.m = c.x;
     wmap(&c.w, "conv_out.w", 32, 9 * h->C[3], 32);
     c.y = c.x;
@@ -752,15 +818,19 @@ int fw_taehv_decode(fw_taehv* h, void* stream) {
   for (const Conv& c : h->convs) {
     int rc;
     if (c.ek == EK_UP)
-      rc = c.bn == 256 ? launch_conv<256, EK_UP>(c.x, c.m, c.w, c.y, c.a, s)
-           : c.bn == 128 ? launch_conv<128, EK_UP>(c.x, c.m, c.w, c.y, c.a, s)
-                         : launch_conv<64, EK_UP>(c.x, c.m, c.w, c.y, c.a, s);
+      rc = c.bn == 256 ? launch_conv<256, EK_UP, LM_TAP>(c.x, c.m, c.w, c.y, c.a, s)
+           : c.bn == 128 ? launch_conv<128, EK_UP, LM_TAP>(c.x, c.m, c.w, c.y, c.a, s)
+                         : launch_conv<64, EK_UP, LM_TAP>(c.x, c.m, c.w, c.y, c.a, s);
     else if (c.ek == EK_RGB)
-      rc = launch_conv<32, EK_RGB>(c.x, c.m, c.w, c.y, c.a, s);
+      rc = launch_conv<32, EK_RGB, LM_HALO_RES>(c.x, c.m, c.w, c.y, c.a, s);
+    else if (c.lm == LM_HALO_RES)
+      rc = launch_conv<64, EK_STORE, LM_HALO_RES>(c.x, c.m, c.w, c.y, c.a, s);
+    else if (c.lm == LM_HALO)
+      rc = launch_conv<64, EK_STORE, LM_HALO>(c.x, c.m, c.w, c.y, c.a, s);
     else
-      rc = c.bn == 256 ? launch_conv<256, EK_STORE>(c.x, c.m, c.w, c.y, c.a, s)
-           : c.bn == 128 ? launch_conv<128, EK_STORE>(c.x, c.m, c.w, c.y, c.a, s)
-                         : launch_conv<64, EK_STORE>(c.x, c.m, c.w, c.y, c.a, s);
+      rc = c.bn == 256 ? launch_conv<256, EK_STORE, LM_TAP>(c.x, c.m, c.w, c.y, c.a, s)
+           : c.bn == 128 ? launch_conv<128, EK_STORE, LM_TAP>(c.x, c.m, c.w, c.y, c.a, s)
+                         : launch_conv<64, EK_STORE, LM_TAP>(c.x, c.m, c.w, c.y, c.a, s);
     if (rc) return rc;
   }
   fw::launch_k(seg_copy_kernel, 2 * fw::num_sms(), 256, 0, s, h->mem_update);
