@@ -249,25 +249,26 @@ __global__ void __launch_bounds__(320, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t a0 = smem_u32(sA + stage * C::A_BYTES), b0 = smem_u32(sB + stage * C::B_BYTES);
-          // kind::f16; the instruction descriptor selects fp16 operands
+          // Descriptors are built once per unit; operand offsets are added to their 14-bit
+          // start-address field (byte offset / 16; every offset stays inside shared memory).
+          // kind::f16; the instruction descriptor selects fp16 operands.
+          const uint64_t ad = sdesc_sw128(smem_u32(sA + stage * C::A_BYTES), 16, 1024);
           if constexpr (LM == LM_TAP) {
+            const uint64_t bd = sdesc_sw128(smem_u32(sB + stage * C::B_BYTES), 16, 1024);
 #pragma unroll
-            for (int k = 0; k < 4; ++k)
-              umma_bf16(d, sdesc_sw128(a0 + k * 32, 16, 1024), sdesc_sw128(b0 + k * 32, 16, 1024), idesc,
-                        (kb | k) != 0);
+            for (int k = 0; k < 4; ++k) umma_bf16(d, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
           } else {
             const int dxi = kb % 3;
+            const uint64_t bd = LM == LM_HALO ? sdesc_sw128(smem_u32(sB + stage * C::B_BYTES), 16, 1024)
+                                              : sdesc_sw128(smem_u32(sR) + (uint32_t)(dxi * BN * 128), 16, 1024);
 #pragma unroll
             for (int dyi = 0; dyi < 3; ++dyi) {
-              // tap (dy, dx): the window at input row dyi of the unit's 10 rows
-              const uint32_t aw = a0 + (uint32_t)(dyi * 2048);
-              const uint32_t bw = LM == LM_HALO ? b0 + (uint32_t)(dyi * BN * 128)
-                                                : smem_u32(sR) + (uint32_t)((dyi * 3 + dxi) * BN * 128);
+              // tap (dy, dx): the window at input row dyi of the unit's 10 rows (2048 bytes apart);
+              // its weight block: dyi-th of the unit's three, or tap dyi * 3 + dxi of the resident copy
+              const uint64_t aw = ad + (uint64_t)(dyi * 128);
+              const uint64_t bw = bd + (uint64_t)(dyi * (LM == LM_HALO ? BN * 8 : 3 * BN * 8));
 #pragma unroll
-              for (int k = 0; k < 4; ++k)
-                umma_bf16(d, sdesc_sw128(aw + k * 32, 16, 1024), sdesc_sw128(bw + k * 32, 16, 1024), idesc,
-                          (kb | dyi | k) != 0);
+              for (int k = 0; k < 4; ++k) umma_bf16(d, aw + 2 * k, bw + 2 * k, idesc, (kb | dyi | k) != 0);
             }
           }
           umma_commit(empty + stage);

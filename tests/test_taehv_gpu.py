@@ -75,3 +75,37 @@ def test_graph_replay_equals_eager_and_state_restores():
     vae.reset()
     first = vae.decode(_lat(cfg, 1))
     assert first.shape[0] == cfg.frames_out - cfg.trim
+
+
+def test_prefix_cache_with_tinyvae_matches_serving_from_scratch():
+    """PrefixCache over a session with the real decoder: the frames served with checkpoint
+    sharing (a bounded pool, so restores, evictions and latent replays through the decoder all
+    happen) equal serving every request from scratch, bit for bit."""
+    from fastworld_b200.config import SMALL
+    from fastworld_b200.prefix_cache import PrefixCache
+    from fastworld_b200.static import B200StaticMG
+    from fastworld_b200.vae import TAEW2_1, TinyVAE
+    from fastworld_b200.weights import synthetic_state_dict
+    S = B200StaticMG(SMALL, synthetic_state_dict(SMALL, 0))
+    S.add_image("img0", seed=5, max_chunks=8)
+    S.capture(warmup=1)
+    vae = TinyVAE("cuda:0", cfg=TAEW2_1, seed=1)
+    trunk = [("img0", (k, c)) for k, c in zip("wwsadw", "uijkli")]
+    paths = [trunk, trunk[:4] + [("img0", ("q", "u"))] * 2, trunk[:2] + [("img0", ("d", "j"))], trunk[:5]]
+    served = []
+    for every, bound in ((None, None), (2, 1)):
+        cache = PrefixCache(S, vae, every=every, max_checkpoints=bound)
+        got = []
+        for p in paths:
+            frames, _ = cache.serve(p)
+            got.append(frames)
+        served.append(got)
+        if every:
+            assert cache.n_evicted > 0
+    for a, b in zip(*served):
+        assert len(a) == len(b)
+        for fa, fb in zip(a, b):
+            assert torch.equal(fa, fb)
+    assert served[0][0][0].shape[0] == TAEW2_1.frames_out - TAEW2_1.trim
+    assert vae.device_status() == 0
+    S.graphs = {}
