@@ -33,9 +33,10 @@
 //                EK_UP     TGrow + nearest 2x upsample: each 64-channel box is written to
 //                          both output rows of its pixel row pair, each pixel twice along x,
 //                          by TMA stores of [32 pixels x 64 channels] rows
-//                EK_RGB    (+bias) -> fp16 -> clamp [0, 1] -> x 2 - 1 -> fp32 planar frames
 // The first conv's input has 16 channels: a prep kernel applies the clamp and writes its
 // 3 x 3 neighbourhoods as 144 (padded to 192) channels, and that conv runs as a 1-tap conv.
+// The last conv (64 -> 3) runs in `rgb_kernel`, transposed (all taps' products per input pixel,
+// then a 3 x 3 gather), with the bias, fp16 rounding, clamp and x 2 - 1 in its epilogue.
 #include <cuda_fp16.h>
 
 #include <cstring>
@@ -50,7 +51,7 @@ namespace fw {
 
 namespace taehv {
 
-enum : int { EK_STORE = 0, EK_UP = 1, EK_RGB = 2 };
+enum : int { EK_STORE = 0, EK_UP = 1 };
 
 constexpr int kSmemLimit = 232448;   // opt-in dynamic shared memory per CTA
 
@@ -73,7 +74,7 @@ struct Cfg {
   // resident weights: 9 taps x one 64-channel block
   static constexpr int RES = LM == LM_HALO_RES ? 9 * BN * 128 : 0;
   // per epilogue warp: EK_STORE one [32 pixels x 128 B] box; EK_UP two upsampled rows
-  static constexpr int BOX = EK == EK_STORE ? 4096 : (EK == EK_UP ? 8192 : 0);
+  static constexpr int BOX = EK == EK_STORE ? 4096 : 8192;
   static constexpr int EPI = 8 * BOX;
   static constexpr int FIT = (kSmemLimit - 2048 - EPI - RES) / STAGE;
   static constexpr int STAGES = FIT > 8 ? 8 : FIT;
@@ -96,7 +97,7 @@ struct ConvArgs {
   const __half* resid;   // [T, H, W, N] or null (EK_STORE)
   int relu;
   int up_stride, up_C;   // EK_UP: output frames per input frame, channels per output frame
-  float* rgb;            // EK_RGB: [T, 3, H, W]
+  float* rgb;            // rgb_kernel: [T, 3, H, W]
   int* status;
 };
 
@@ -104,6 +105,19 @@ __device__ __forceinline__ float round_h(float v) { return __half2float(__float2
 __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
   __half2 h = __floats2half2_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);
+}
+// AND of `pred` over the 128 threads that use named barrier `id` (a barrier for all of them).
+__device__ __forceinline__ bool bar_and128(int id, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "barrier.red.and.pred q, %2, 128, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}\n"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "r"(id)
+      : "memory");
+  return r != 0;
 }
 
 template <int BN, int EK, int LM>
@@ -302,21 +316,7 @@ __global__ void __launch_bounds__(320, 1)
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
       const uint32_t tb = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(g * BN);
-      if constexpr (EK == EK_RGB) {
-        uint32_t v[32];
-        tmem_ld32(tb, v);
-        tmem_ld_wait();
-        if (inside) {
-          const size_t plane = (size_t)a.H * a.W;
-          float* o = a.rgb + (size_t)f * 3 * plane + (size_t)y * a.W + x;
-#pragma unroll
-          for (int c = 0; c < 3; ++c) {
-            float u = round_h(__uint_as_float(v[c]) + (a.bias ? __ldg(a.bias + c) : 0.f));
-            u = fminf(fmaxf(u, 0.f), 1.f);
-            o[c * plane] = u * 2.f - 1.f;
-          }
-        }
-      } else {
+      {
 #pragma unroll 1
         for (int b = 0; b < BN / 64; ++b) {
           uint32_t v[2][32];
@@ -404,7 +404,7 @@ __global__ void __launch_bounds__(320, 1)
       tc_fence_before();
       mbar_arrive(tempty + g);
     }
-    if (lane == 0 && EK != EK_RGB) bulk_wait0();
+    if (lane == 0) bulk_wait0();
   }
   tc_fence_before();
   __syncthreads();
@@ -504,7 +504,188 @@ int launch_conv(const CUtensorMap& x, const CUtensorMap& m, const CUtensorMap& w
   return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
 }
 
+// The last conv (64 -> 3 channels) in the transposed arrangement: a 3-channel conv on the
+// per-tap form would spend 36 tensor-core MMAs per 128 pixels (each MMA of M = 128 costs about
+// as much at N = 32 as at N = 64, and only 3 of the columns are used).  Instead, per tile of
+// 8 x 16 output pixels, the input region with its halo (10 rows x 18 columns = 180 pixels, one
+// TMA box) is multiplied by all 27 (tap, channel) weight rows at once: D[r, t * 3 + c] =
+// in[r] . W[c, t] for every region pixel r (two M = 128 blocks, K = 64: 8 MMAs).  The epilogue
+// writes D to shared memory and each output pixel sums its 9 neighbours' entries:
+// out[y, x, c] = sum_t D[(y + dy_t + 1) * 18 + x + dx_t + 1, t * 3 + c], then bias, fp16
+// rounding, clamp to [0, 1], x 2 - 1.
+namespace rgbk {
+constexpr int REGION = 180, A_BYTES = 256 * 128, BOX_BYTES = REGION * 128;
+constexpr int STAGES = 4;
+constexpr int W_OFF = STAGES * A_BYTES;          // resident weights [32 rows (t * 3 + c), 64]
+constexpr int T_OFF = W_OFF + 32 * 128;          // per epilogue group: D table [256][27] fp32
+constexpr int T_BYTES = 256 * 27 * 4;
+constexpr int BAR_OFF = T_OFF + 2 * T_BYTES;
+constexpr int SMEM = BAR_OFF + 1024 + 1024;
+static_assert(SMEM <= kSmemLimit, "shared memory");
+}  // namespace rgbk
+
+__global__ void __launch_bounds__(320, 1)
+    rgb_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW, const ConvArgs a) {
+  using namespace rgbk;
+  pdl_trigger();
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
+  uint8_t* smem = smem_raw + pad;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + BAR_OFF);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint64_t* res_full = drain + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(res_full + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nxb = a.W >> 4, nyb = (a.H + 7) >> 3;
+  const int num_tiles = a.T * nyb * nxb;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(tfull + b, 1);
+      mbar_init(tempty + b, 128);
+    }
+    mbar_init(drain, 1);
+    mbar_init(res_full, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 128);   // 2 buffers x (2 region blocks x 32 columns)
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  if (warp == 0 && lane == 0 && blockIdx.x < num_tiles) {   // static weights: before the wait
+    mbar_arrive_expect_tx(res_full, 32 * 128);
+    tma_load_2d(smem + W_OFF, &tmW, res_full, 0, 0);
+  }
+  pdl_wait();
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0, used = 0, last_par = 0;
+      for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+        const int xb = t % nxb, r = t / nxb, yb = r % nyb, f = r / nyb;
+        if (!mbar_wait(empty + stage, phase ^ 1u, abort_flag, a.status, DEV_TIMEOUT_PRODUCER)) break;
+        mbar_arrive_expect_tx(full + stage, BOX_BYTES);
+        tma_load_4d(smem + stage * A_BYTES, &tmX, full + stage, 0, xb * 16 - 1, yb * 8 - 1, f);
+        used |= 1u << stage;
+        last_par = (last_par & ~(1u << stage)) | (phase << stage);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      volatile int no_abort = 0;
+      for (int s = 0; s < STAGES; ++s)
+        if (used >> s & 1u) mbar_wait(full + s, last_par >> s & 1u, &no_abort, a.status, DEV_TIMEOUT_DRAIN);
+      if (blockIdx.x < num_tiles) mbar_wait(res_full, 0, &no_abort, a.status, DEV_TIMEOUT_DRAIN);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16(128, 32);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = blockIdx.x >= num_tiles || mbar_wait(res_full, 0, abort_flag, a.status, DEV_TIMEOUT_MMA);
+      const uint64_t bd = sdesc_sw128(smem_u32(smem + W_OFF), 16, 1024);
+      int i = 0;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++i) {
+        const int acc = i & 1;
+        if (!mbar_wait(tempty + acc, ((uint32_t)(i >> 1) & 1u) ^ 1u, abort_flag, a.status, DEV_TIMEOUT_MMA)) break;
+        if (!mbar_wait(full + stage, phase, abort_flag, a.status, DEV_TIMEOUT_MMA)) break;
+        tc_fence_after();
+        const uint64_t ad = sdesc_sw128(smem_u32(smem + stage * A_BYTES), 16, 1024);
+#pragma unroll
+        for (int blk = 0; blk < 2; ++blk)   // region pixels 0-127 and 128-255 (180-255 unused)
+#pragma unroll
+          for (int k = 0; k < 4; ++k)       // kind::f16, fp16 operands
+            umma_bf16(tmem_base + (uint32_t)(acc * 64 + blk * 32), ad + (uint64_t)(blk * 1024) + 2 * k, bd + 2 * k,
+                      idesc, k != 0);
+        umma_commit(empty + stage);
+        umma_commit(tfull + acc);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      umma_commit(drain);
+      volatile int no_abort = 0;
+      mbar_wait(drain, 0, &no_abort, a.status, DEV_TIMEOUT_DRAIN);
+    }
+  } else {
+    const int g = (warp - 2) >> 2, q = warp & 3;
+    float* tab = reinterpret_cast<float*>(smem + T_OFF + g * T_BYTES);
+    const int bar_id = 1 + g;
+    const int p = q * 32 + lane, yl = p >> 4, xl = p & 15;
+    const size_t plane = (size_t)a.H * a.W;
+    float bias[3];
+#pragma unroll
+    for (int c = 0; c < 3; ++c) bias[c] = a.bias ? __ldg(a.bias + c) : 0.f;
+    int i = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++i) {
+      if ((i & 1) != g) continue;
+      const int xb = t % nxb, r = t / nxb, yb = r % nyb, f = r / nyb;
+      const bool ok = mbar_wait(tfull + g, (uint32_t)(i >> 1) & 1u, abort_flag, a.status, DEV_TIMEOUT_EPILOGUE);
+      // the group's four warps leave together (they meet at named barriers below); this is also
+      // the point after which the group's previous tile has finished reading the table
+      if (!bar_and128(bar_id, ok)) break;
+      tc_fence_after();
+      uint32_t v0[32], v1[32];
+      const uint32_t tb = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(g * 64);
+      tmem_ld32(tb, v0);
+      tmem_ld32(tb + 32, v1);
+      tmem_ld_wait();
+      tc_fence_before();
+      mbar_arrive(tempty + g);
+#pragma unroll
+      for (int j = 0; j < 27; ++j) tab[p * 27 + j] = __uint_as_float(v0[j]);
+      if (p + 128 < REGION) {
+#pragma unroll
+        for (int j = 0; j < 27; ++j) tab[(p + 128) * 27 + j] = __uint_as_float(v1[j]);
+      }
+      asm volatile("bar.sync %0, 128;" ::"r"(bar_id) : "memory");
+      const int y = yb * 8 + yl, x = xb * 16 + xl;
+      if (y < a.H) {
+        float o[3] = {0.f, 0.f, 0.f};
+#pragma unroll
+        for (int tap = 0; tap < 9; ++tap) {
+          const int rr = (yl + tap / 3) * 18 + xl + tap % 3;
+#pragma unroll
+          for (int c = 0; c < 3; ++c) o[c] += tab[rr * 27 + tap * 3 + c];
+        }
+        float* out = a.rgb + (size_t)f * 3 * plane + (size_t)y * a.W + x;
+#pragma unroll
+        for (int c = 0; c < 3; ++c) {
+          const float u = fminf(fmaxf(round_h(o[c] + bias[c]), 0.f), 1.f);
+          out[c * plane] = u * 2.f - 1.f;
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tmem_base, 128);
+}
+
+int launch_rgb(const CUtensorMap& x, const CUtensorMap& w, const ConvArgs& a, cudaStream_t s) {
+  if (cudaFuncSetAttribute(rgb_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, rgbk::SMEM) != cudaSuccess)
+    return FW_ECUDA;
+  const int tiles = a.T * ((a.H + 7) / 8) * (a.W / 16);
+  launch_k(rgb_kernel, tiles < num_sms() ? tiles : num_sms(), 320, rgbk::SMEM, s, x, w, a);
+  return cudaGetLastError() == cudaSuccess ? 0 : FW_ECUDA;
+}
+
 // One launch of the decoder's plan.
+constexpr int EK_RGB = 2;   // the plan's last conv: rgb_kernel
 struct Conv {
   int bn = 0, ek = EK_STORE, lm = LM_TAP;
   CUtensorMap x{}, m{}, w{}, y{};
@@ -628,7 +809,7 @@ int fw_taehv_create(const fw_taehv_config* cfg, fw_taehv** out) {
     add(h, "tgrow" + std::to_string(s) + ".w", FW_KIND_WEIGHT, FW_F16, {(int64_t)Cs * c.time_up[s], Cs});
     add(h, "conv" + std::to_string(s) + ".w", FW_KIND_WEIGHT, FW_F16, {h->C[s + 1], 9 * Cs});
   }
-  add(h, "conv_out.w", FW_KIND_WEIGHT, FW_F16, {32, 9 * h->C[3]});
+  add(h, "conv_out.wt", FW_KIND_WEIGHT, FW_F16, {32, h->C[3]});
   add(h, "conv_out.b", FW_KIND_WEIGHT, FW_F32, {32});
   add(h, "lat", FW_KIND_INPUT, FW_F16, {16, h->T0, h->h, h->w});
   add(h, "rgb", FW_KIND_OUTPUT, FW_F32, {h->F[3], 3, (int64_t)h->h * 8, (int64_t)h->w * 8});
@@ -793,14 +974,13 @@ int fw_taehv_finalize(fw_taehv* h) {
     Conv c;
     c.bn = 32;
     c.ek = EK_RGB;
-    c.lm = LM_HALO_RES;
-    if (h->C[3] != 64) return FW_ESHAPE;   // resident weights: one 64-channel input block
-    amap(&c.x, z, 3, h->C[3], h->F[3], c.lm);
+    if (h->C[3] != 64) return FW_ESHAPE;   // one 64-channel block of K
+    if (!rc) rc = make_map_nhwc(&c.x, z, h->F[3], h->h << 3, h->w << 3, h->C[3], 18, 10);
     c.m = c.x;
-    wmap(&c.w, "conv_out.w", 32, 9 * h->C[3], 32);
+    wmap(&c.w, "conv_out.wt", 32, 64, 32);
     c.y = c.x;
-    c.a = ConvArgs{h->F[3], h->h << 3, h->w << 3, 9, h->C[3] / 64, 0, 3, (const float*)ptr(h, "conv_out.b"),
-                   nullptr, 0, 0, 0, (float*)ptr(h, "rgb"), h->status};
+    c.a = ConvArgs{h->F[3], h->h << 3, h->w << 3, 9, 1, 0, 3, (const float*)ptr(h, "conv_out.b"), nullptr, 0, 0, 0,
+                   (float*)ptr(h, "rgb"), h->status};
     h->convs.push_back(c);
   }
   if (rc) return rc;
@@ -823,7 +1003,7 @@ int fw_taehv_decode(fw_taehv* h, void* stream) {
            : c.bn == 128 ? launch_conv<128, EK_UP, LM_TAP>(c.x, c.m, c.w, c.y, c.a, s)
                          : launch_conv<64, EK_UP, LM_TAP>(c.x, c.m, c.w, c.y, c.a, s);
     else if (c.ek == EK_RGB)
-      rc = launch_conv<32, EK_RGB, LM_HALO_RES>(c.x, c.m, c.w, c.y, c.a, s);
+      rc = launch_rgb(c.x, c.w, c.a, s);
     else if (c.lm == LM_HALO_RES)
       rc = launch_conv<64, EK_STORE, LM_HALO_RES>(c.x, c.m, c.w, c.y, c.a, s);
     else if (c.lm == LM_HALO)

@@ -165,8 +165,9 @@ def pack_weights(cfg: TaehvConfig, sd: Dict[str, torch.Tensor]) -> Dict[str, tor
                 out[f"{q}.b{j}"] = f(sd[f"{p}.{i}.bias"])
         out[f"tgrow{s}.w"] = _conv_k(h(sd[f"decoder.{b + 4}.conv.weight"]))
         out[f"conv{s}.w"] = _conv_k(h(sd[f"decoder.{b + 5}.weight"]))
-    w = _conv_k(h(sd["decoder.22.weight"]))
-    out["conv_out.w"] = torch.cat([w, torch.zeros(32 - w.shape[0], w.shape[1], dtype=w.dtype)], 0)
+    # the last conv, transposed: row (ky * 3 + kx) * 3 + c holds W[c, :, ky, kx]
+    w = h(sd["decoder.22.weight"]).permute(2, 3, 0, 1).reshape(27, -1)
+    out["conv_out.wt"] = torch.cat([w, torch.zeros(32 - w.shape[0], w.shape[1], dtype=w.dtype)], 0)
     out["conv_out.b"] = torch.cat([f(sd["decoder.22.bias"]), torch.zeros(29)])
     return out
 

@@ -222,7 +222,8 @@ int fw_peer_access(int peer);
  * Tensors are registered and bound like the session engine's (fw_taehv_tensor_info_at /
  * fw_taehv_bind): weights fp16 [Cout, taps * Cin] with K ordered (tap, input channel), biases
  * fp32; "conv_in.w" is [C0, 192]: 9 taps x 16 latent channels, then 48 zero columns;
- * "conv_out.w" / "conv_out.b" are padded to 32 output rows (3 used); "work" is the activation
+ * "conv_out.wt" is the last conv transposed, [32, C3] with row (ky * 3 + kx) * 3 + c (27 used),
+ * "conv_out.b" fp32 [32] (3 used); "work" is the activation
  * workspace and "status" the int32[4] device status word (zeroed).  fw_taehv_finalize builds the
  * TMA descriptors; fw_taehv_decode launches the whole decoder (no host synchronisation;
  * graph-capturable).

@@ -91,7 +91,10 @@ def test_packed_weight_layout():
     assert pk["conv_in.w"].shape == (64, 192) and torch.all(pk["conv_in.w"][:, 144:] == 0)
     ref = F.conv2d(x16, sd["decoder.1.weight"].float(), padding=1)
     assert torch.allclose(_im2col_conv(x16, pk["conv_in.w"], 9, 16), ref, atol=1e-3)
-    assert pk["conv_out.w"].shape == (32, 9 * 64) and torch.all(pk["conv_out.w"][3:] == 0)
+    # the transposed last conv: row (ky * 3 + kx) * 3 + c
+    w22 = sd["decoder.22.weight"]
+    assert pk["conv_out.wt"].shape == (32, 64) and torch.all(pk["conv_out.wt"][27:] == 0)
+    assert torch.equal(pk["conv_out.wt"][(2 * 3 + 1) * 3 + 2], w22[2, :, 2, 1])
     assert pk["tgrow1.w"].shape == (128, 64)
 
 
