@@ -27,7 +27,8 @@ weights and inputs.  Metric: frames per second (12 pixel frames per chunk), whol
   from one image, prefix-cache branching, cross-GPU checkpoint restores over NVLink) and
   ``tp_parity`` (a tensor-parallel test model over the N ranks: ranks bit-identical, latents
   against the CPU oracle); ``taehv`` (every N: the TAEHV decoder on one chunk's latent, ms per
-  chunk, TFLOP/s, and the served frame rate of DiT chunk + decoder).
+  chunk, TFLOP/s, and the served frame rate of DiT chunk + decoder); ``lingbot`` (every N: the
+  LingBot-World-v2 runtime's steady chunk at its own shape).
 
 Multi-GPU (torchrun): every rank runs its own session; there is no collective on the data path
 of ``value`` (sessions are independent).  Timing is bracketed by a barrier and synchronize; the
@@ -372,6 +373,8 @@ def run_ours(args):
         variants["tp_parity"] = guarded(lambda: tp_parity_variant(rank, world, local, ctl), world, ctl)
     if not args.no_taehv and agree(time.time() - t_start < args.variant_budget, world, ctl):
         variants["taehv"] = guarded(lambda: taehv_variant(ms, rank, world, ctl), world, ctl)
+    if not args.no_lingbot and agree(time.time() - t_start < args.variant_budget, world, ctl):
+        variants["lingbot"] = guarded(lambda: lingbot_variant(rank, world, ctl), world, ctl)
     line = None
     if rank == 0:
         fps = world * FRAMES_PER_CHUNK / (ms / 1e3)
@@ -459,6 +462,47 @@ def taehv_variant(chunk_ms, rank, world, ctl):
             "tflops": tf, "frac_of_peak": tf / peak_tf, "peak_kind": f"{peak_kind} bf16 burst",
             "dit_plus_decoder_fps": world * fr / ((chunk_ms + dms) / 1e3),
             "reference_ms_per_chunk_published": 10.4}
+
+
+def lingbot_variant(rank, world, ctl):
+    """The LingBot-World-v2 runtime at its shape (Wan-1.3B, 4 latent frames = 6032 tokens per
+    chunk, an 18-frame window = 27144 keys with a 6-frame sink): steady chunks (plan (14, 18),
+    roll [10:18] -> [6:14]) replayed from the captured graph; every rank runs its own session."""
+    from fastworld_b200.lingbot import LINGBOT, B200StaticLingbot, synthetic_inputs
+    cfg = LINGBOT
+    I = synthetic_inputs(cfg, 9, seed=0, text_tokens=120)
+    S = B200StaticLingbot(cfg, device=f"cuda:{torch.cuda.current_device()}", seed=0)
+    S.set_session(I)
+    S.capture()
+    for k in range(5):                     # chunks 0-4: fill the window, reach the steady plan
+        S.gen_chunk(k)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    times = []
+    for k in range(5, 9):
+        S._prep(k)
+        e0.record()
+        S.graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+    status = S.device_status()
+    del S
+    torch.cuda.empty_cache()
+    ms = sorted(times)[len(times) // 2]
+    if world > 1:
+        got = [None] * world
+        torch.distributed.all_gather_object(got, ms, group=ctl)
+        ms = max(got)
+    fl = cfg.flops()
+    peak_tf, _, peak_kind = peaks()
+    return {"workload": "LingBot-World-v2 causal chunk (Wan-1.3B I2V + camera injector + text cross-attention), "
+                        "6032 tokens over a 27144-key window with a 6-frame sink, 4 steps + the key refresh",
+            "ms_per_chunk": ms, "frames_per_s": world * 4 * cfg.chunk / (ms / 1e3),
+            "chunk_tflop": fl["total"] / 1e12, "tflops": fl["total"] / 1e12 / (ms / 1e3),
+            "frac_of_peak": fl["total"] / 1e12 / (ms / 1e3) / peak_tf, "peak_kind": f"{peak_kind} bf16 burst",
+            "attention_share_of_flops": fl["attention"] / fl["total"], "graphs": 1, "status_ok": status == 0,
+            "reference_ms_per_chunk_published_h100": 843}
 
 
 def tp14b_variant(rank, world, local, ctl):
@@ -765,7 +809,14 @@ def taehv(reps: int) -> None:
           f"{TAEW2_1.flops() / 1e9:.1f} GFLOP algorithmic = {tf:.0f} TFLOP/s")
 
 
+def lingbot(reps: int) -> None:
+    """The LingBot runtime at its shape: steady chunk time from graph replays."""
+    out = lingbot_variant(0, 1, None)
+    print(json.dumps(out))
+
+
 KERNELS = {"chunk": lambda a: chunk(a.chunks, a.config), "gemm": lambda a: gemm(a.reps), "taehv": lambda a: taehv(a.reps),
+           "lingbot": lambda a: lingbot(a.reps),
            "gemm_resid": lambda a: gemm_resid(a.reps), "attn": lambda a: attn(a.reps), "ln": lambda a: ln(a.reps),
            "ln14": lambda a: ln14(a.reps), "rms": lambda a: rms(a.reps), "copy": lambda a: copy(a.reps),
            "fp8_peak": lambda a: fp8_peak(a.reps)}
@@ -786,6 +837,7 @@ def main():
     ap.add_argument("--no-tp", action="store_true", help="skip the 14B tensor-parallel variants (configs[4])")
     ap.add_argument("--no-explore", action="store_true", help="skip the explore variant (configs[3], N > 1)")
     ap.add_argument("--no-taehv", action="store_true", help="skip the decoder variant")
+    ap.add_argument("--no-lingbot", action="store_true", help="skip the LingBot runtime variant")
     ap.add_argument("--variant-budget", type=float, default=600.0,
                     help="start no further variant once this many seconds have passed")
     args = ap.parse_args()

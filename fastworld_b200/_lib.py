@@ -55,6 +55,16 @@ class FwTaehvConfig(ctypes.Structure):
                 ("lat_w", ctypes.c_int), ("channels", ctypes.c_int * 4), ("time_up", ctypes.c_int * 3)]
 
 
+class FwLbConfig(ctypes.Structure):
+    _fields_ = [("dim", ctypes.c_int), ("heads", ctypes.c_int), ("head_dim", ctypes.c_int), ("ffn", ctypes.c_int),
+                ("layers", ctypes.c_int), ("freq_dim", ctypes.c_int), ("text_len", ctypes.c_int),
+                ("text_dim", ctypes.c_int), ("lat_ch", ctypes.c_int), ("y_ch", ctypes.c_int), ("cam_ch", ctypes.c_int),
+                ("chunk", ctypes.c_int), ("lat_h", ctypes.c_int), ("lat_w", ctypes.c_int), ("kv_frames", ctypes.c_int),
+                ("sink_frames", ctypes.c_int), ("n_steps", ctypes.c_int), ("eps", ctypes.c_float),
+                ("timesteps", ctypes.c_float * 8), ("sig_x0", ctypes.c_double * 8), ("an_alpha", ctypes.c_float * 8),
+                ("an_sigma", ctypes.c_float * 8)]
+
+
 _SIGS = {
     "fw_abi_version": (ctypes.c_int, []),
     "fw_launch_count": (ctypes.c_ulonglong, []),
@@ -98,6 +108,15 @@ _SIGS = {
                                        ctypes.c_void_p]),
     "fw_graph_begin": (ctypes.c_int, [ctypes.c_void_p]),
     "fw_graph_end": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)]),
+    "fw_lb_create": (ctypes.c_int, [ctypes.POINTER(FwLbConfig), ctypes.POINTER(ctypes.c_void_p)]),
+    "fw_lb_tensor_count": (ctypes.c_int, [ctypes.c_void_p]),
+    "fw_lb_tensor_info_at": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(FwTensorInfo)]),
+    "fw_lb_bind": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_char_p, ctypes.c_void_p, ctypes.c_size_t]),
+    "fw_lb_finalize": (ctypes.c_int, [ctypes.c_void_p]),
+    "fw_lb_set_prompt": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
+    "fw_lb_chunk": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
+    "fw_lb_roll_pieces": (ctypes.c_int, [ctypes.c_void_p]),
+    "fw_lb_destroy": (None, [ctypes.c_void_p]),
     "fw_taehv_create": (ctypes.c_int, [ctypes.POINTER(FwTaehvConfig), ctypes.POINTER(ctypes.c_void_p)]),
     "fw_taehv_tensor_count": (ctypes.c_int, [ctypes.c_void_p]),
     "fw_taehv_tensor_info_at": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(FwTensorInfo)]),

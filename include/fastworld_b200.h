@@ -247,6 +247,42 @@ int fw_taehv_decode(fw_taehv* h, void* stream);
 int fw_taehv_status(fw_taehv* h, int* out);
 void fw_taehv_destroy(fw_taehv* h);
 
+/* ---- LingBot-World-v2 causal runtime (StaticLingbot, fastworld/models/lingbot_v2/static.py:49-320) ----
+ * A Wan-1.3B I2V DiT with a camera injector, text cross-attention and a KV window of kv_frames
+ * frames with a sink of sink_frames, served chunk by chunk.  Tensors are registered and bound
+ * like the session engine's (fw_lb_tensor_info_at / fw_lb_bind): packed bf16 weights
+ * (b<i>.sa.qkv = q | k | v rows, b<i>.ca.kv = k | v rows), state
+ * K.<i> / V.<i> [kv_frames * tokens per frame, dim], fp32 latents (x_in, noise.<i>, y_in, out),
+ * bf16 Plücker features pl_in, the padded prompt ctx_in, and per chunk the device plan
+ * int32[8] = {write offset, key length, 0, roll src, roll dst, roll rows, roll piece rows, 0}
+ * (rows = tokens) and chunk int32[4] = {k, chunk * k, 0, 0} (RoPE frame offset).
+ * fw_lb_set_prompt: text embedding and every block's cross-attention K/V (derived tensors
+ * xk, xv) from ctx_in; fw_lb_chunk: one chunk (camera branch, n_steps forwards, the t = 0 key
+ * refresh, the roll); both graph-capturable, no host synchronisation. */
+typedef struct fw_lb_config {
+  int dim, heads, head_dim, ffn, layers, freq_dim;
+  int text_len, text_dim;
+  int lat_ch, y_ch, cam_ch, chunk, lat_h, lat_w;
+  int kv_frames, sink_frames;
+  int n_steps;
+  float eps;
+  float timesteps[8];
+  double sig_x0[8];      /* fp64 sigma of each step's x0 conversion */
+  float an_alpha[8];     /* renoising to step i + 1: alpha * x0 + sigma * noise */
+  float an_sigma[8];
+} fw_lb_config;
+typedef struct fw_lb fw_lb;
+int fw_lb_create(const fw_lb_config* cfg, fw_lb** out);
+int fw_lb_tensor_count(const fw_lb* h);
+int fw_lb_tensor_info_at(const fw_lb* h, int index, fw_tensor_info* info);
+int fw_lb_bind(fw_lb* h, const char* name, void* ptr, size_t bytes);
+int fw_lb_finalize(fw_lb* h);
+int fw_lb_set_prompt(fw_lb* h, void* stream);
+int fw_lb_chunk(fw_lb* h, void* stream);
+/* Roll launches per chunk (the most pieces any plan of this window needs). */
+int fw_lb_roll_pieces(const fw_lb* h);
+void fw_lb_destroy(fw_lb* h);
+
 /* ---- failure-path self-tests (no counterpart in the reference, which has no device-side
  * failure detection) ----
  * Runs a bounded wait that nothing satisfies, so that it runs out after `limit_ns`
