@@ -1,17 +1,17 @@
 // The LingBot-World-v2 causal chunk runtime (the reference's StaticLingbot,
 // fastworld/models/lingbot_v2/static.py:49-320) on the library's sm_100a kernels.
 //
-// One chunk = the camera branch (static.py:186-204, hoisted: once per chunk), 4 denoising
-// forwards with x0 = x - sigma * flow in fp64 and renoising (254-265), a forward at t = 0 over
-// x0 that refreshes the chunk's keys (266), and the end-of-chunk roll of the KV window (267-268,
-// 245-252).  A forward (206-243) writes its RoPE'd keys and values into the per-layer KV buffer at
+// One chunk = the camera branch (static.py:188-207, hoisted: once per chunk), 4 denoising
+// forwards with x0 = x - sigma * flow in fp64 and renoising (266-277), a forward at t = 0 over
+// x0 that refreshes the chunk's keys (278-279), and the end-of-chunk roll of the KV window (280-281,
+// 257-264).  A forward (209-255) writes its RoPE'd keys and values into the per-layer KV buffer at
 // the plan's write offset, then attends to the buffer's first key_len frames; the self-attention
 // residual update is followed by the camera affine xs = (1 + scale) * xs + shift; cross-attention
-// reads the prompt's K/V (fw_lb_set_prompt, 127-137).
+// reads the prompt's K/V (fw_lb_set_prompt, 128-137).
 //
 // The chunk's plan (write offset, key length, roll) and chunk index live in device memory
 // (tensors "plan", "chunk"), so one captured graph serves every chunk; the roll is a sequence
-// of non-overlapping piece copies, as the eager runtime's (static.py:245-252), whose count the
+// of non-overlapping piece copies, as the eager runtime's (static.py:257-264), whose count the
 // plan sets on the device.
 //
 // GEMMs, attention, LayerNorm, RMSNorm + RoPE, the time embedding, patchify and the RoPE table
@@ -385,7 +385,7 @@ int forward(fw_lb* h, int step, const float* x, float* x0, const float* noise, f
     LB_TRY(ln_f32(xs, D, L, D, c.eps, e6, e6 + D, nullptr, nullptr, y, D, s));
     LB_TRY(run(ly.qkv, s));
     LB_TRY(rms_rope2(q, W(h, p + "sa.nq.w"), q, kc, W(h, p + "sa.nk.w"), kc, D, L, D, c.eps, rope, c.head_dim, D, s));
-    // keys and values enter the window before the attention reads it (static.py:216-219)
+    // keys and values enter the window before the attention reads it (static.py:228-231)
     launch_k(kv_write_kernel, blocks(n / 8, 256), 256, 0, s, P<__nv_bfloat16>(h, "K." + std::to_string(i)),
              P<__nv_bfloat16>(h, "V." + std::to_string(i)), (const __nv_bfloat16*)kc, (const __nv_bfloat16*)vc, plan, L,
              D, h->cap);
@@ -428,7 +428,7 @@ int chunk(fw_lb* h, cudaStream_t s) {
                    last ? nullptr : bufs[i & 1], true, s));
     x = bufs[i & 1];
   }
-  // the t = 0 forward over the denoised latent refreshes the chunk's keys (static.py:266)
+  // the t = 0 forward over the denoised latent refreshes the chunk's keys (static.py:278-279)
   LB_TRY(forward(h, c.n_steps, P<const float>(h, "out"), nullptr, nullptr, nullptr, false, s));
   RollPtrs rp{};
   for (int i = 0; i < c.layers; ++i) {

@@ -2,7 +2,7 @@
 camera injector, text cross-attention and a sink + rolling KV window, served chunk by chunk
 (the reference's ``StaticLingbot``, ``fastworld/models/lingbot_v2/static.py:49-320``).
 
-What a chunk computes (``static.py:209-262``): 4 denoising forwards of the DiT over the chunk's
+What a chunk computes (``static.py:209-281``): 4 denoising forwards of the DiT over the chunk's
 C = 4 latent frames (x0 = x - sigma * flow in fp64, then renoising with the session generator's
 noise), then a forward at t = 0 over the denoised latent that refreshes the chunk's keys, and the
 end-of-chunk roll of the KV window.  Every forward writes its RoPE'd keys and values into the
@@ -65,8 +65,8 @@ def flow_schedule(steps_index=(0, 250, 500, 750), n_train: int = 1000, shift: fl
     Shifted flow-matching sigmas s' = shift s / (1 + (shift - 1) s) over s = 1 .. 1/n_train
     (n_train points, then a final 0), timesteps = 1000 s'; the chunk loop uses
     timesteps[steps_index].  Per step i: ``sig_x0[i]`` (fp64) = the sigma whose timestep is
-    nearest to t_i (``static.py:105-111``); renoising to t_{i+1} uses alpha = 1 - sigma,
-    sigma = the fp32 sigma of t_{i+1} (``static.py:112-121``).  The scheduler itself belongs to
+    nearest to t_i (``static.py:110-115``); renoising to t_{i+1} uses alpha = 1 - sigma,
+    sigma = the fp32 sigma of t_{i+1} (``static.py:116-125``).  The scheduler itself belongs to
     the un-vendored Wan package: these constants are this build's restatement, shared by the
     engine and the oracle."""
     s = np.linspace(1.0, 1.0 / n_train, n_train)

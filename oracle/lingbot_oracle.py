@@ -8,18 +8,18 @@ missing.
 It restates, op for op and in PyTorch fp32 on the CPU, the reference's ``StaticLingbot``
 (``fastworld/models/lingbot_v2/static.py``):
 
-* ``_consts``     per-step time embeddings and scheduler constants (``static.py:89-121``)
+* ``_consts``     per-step time embeddings and scheduler constants (``static.py:91-126``)
                   -> :meth:`LingbotOracle.time_embed` (constants from ``lingbot.flow_schedule``)
-* ``set_prompt``  text embedding and every block's cross-attention K/V (``static.py:127-137``)
+* ``set_prompt``  text embedding and every block's cross-attention K/V (``static.py:128-137``)
                   -> :meth:`LingbotOracle.set_prompt`
 * ``_prep``       chunk slices of noise / condition / Plücker features, the RoPE table at the
-                  chunk's absolute frame offset, the 3 renoising draws (``static.py:152-168``)
-* ``_cam_emb`` / ``_cam_block`` / ``_hoist_cam``  camera branch (``static.py:186-204``)
+                  chunk's absolute frame offset, the 3 renoising draws (``static.py:154-169``)
+* ``_cam_emb`` / ``_cam_block`` / ``_hoist_cam``  camera branch (``static.py:188-207``)
 * ``_net``        the DiT forward with the KV write at the plan's offset before attention over
-                  the buffer's first ``key_len`` frames (``static.py:206-243``)
-* ``_roll``       the end-of-chunk KV shift (``static.py:245-252``)
+                  the buffer's first ``key_len`` frames (``static.py:209-255``)
+* ``_roll``       the end-of-chunk KV shift (``static.py:257-264``)
 * ``_chunk``      4 forwards, x0 in fp64, renoising, the t = 0 KV refresh, the roll
-                  (``static.py:254-268``)
+                  (``static.py:266-281``)
 
 The block internals of the un-vendored Wan model (LayerNorm eps 1e-6, RMSNorm over the full
 width, GELU-tanh FFN, ``text_embedding`` = Linear, GELU-tanh, Linear; ``time_embedding`` =
