@@ -815,8 +815,25 @@ def lingbot(reps: int) -> None:
     print(json.dumps(out))
 
 
+def lingbot_chunk(reps: int) -> None:
+    """One steady LingBot chunk launched eagerly inside the NVTX range "lb_chunk" (for a launch
+    list: ncu --nvtx --nvtx-include "lb_chunk/"), after 6 chunks that reach the steady plan."""
+    from fastworld_b200.lingbot import LINGBOT, B200StaticLingbot, synthetic_inputs
+    I = synthetic_inputs(LINGBOT, 8, seed=0, text_tokens=120)
+    S = B200StaticLingbot(LINGBOT, device="cuda", seed=0)
+    S.set_session(I)
+    for k in range(6):
+        S.gen_chunk(k)
+    torch.cuda.synchronize()
+    torch.cuda.nvtx.range_push("lb_chunk")
+    S.gen_chunk(6, graph=False)
+    torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize()
+    print(f"lingbot chunk 6 (eager) done, device status {S.device_status()}")
+
+
 KERNELS = {"chunk": lambda a: chunk(a.chunks, a.config), "gemm": lambda a: gemm(a.reps), "taehv": lambda a: taehv(a.reps),
-           "lingbot": lambda a: lingbot(a.reps),
+           "lingbot": lambda a: lingbot(a.reps), "lingbot_chunk": lambda a: lingbot_chunk(a.reps),
            "gemm_resid": lambda a: gemm_resid(a.reps), "attn": lambda a: attn(a.reps), "ln": lambda a: ln(a.reps),
            "ln14": lambda a: ln14(a.reps), "rms": lambda a: rms(a.reps), "copy": lambda a: copy(a.reps),
            "fp8_peak": lambda a: fp8_peak(a.reps)}
