@@ -69,20 +69,26 @@ def flow_schedule(steps_index=(0, 250, 500, 750), n_train: int = 1000, shift: fl
     sigma = the fp32 sigma of t_{i+1} (``static.py:116-125``).  The scheduler itself belongs to
     the un-vendored Wan package: these constants are this build's restatement, shared by the
     engine and the oracle."""
-    s = np.linspace(1.0, 1.0 / n_train, n_train)
-    sig = shift * s / (1 + (shift - 1) * s)
-    sigmas64 = np.concatenate([sig, [0.0]])
-    ts64 = sig * 1000.0
-    t = [float(ts64[i]) for i in steps_index]
-    sig_x0 = [float(sigmas64[int(np.argmin(np.abs(ts64 - ti)))]) for ti in t]
-    sigmas32 = sigmas64.astype(np.float32)
+    sigmas32, ts32 = scheduler_tables(n_train, shift)
+    t = [float(ts32[i]) for i in steps_index]
+    sig_x0 = [float(sigmas32[int(np.argmin(np.abs(ts32.astype(np.float64) - ti)))]) for ti in t]
     an_alpha, an_sigma = [], []
     for ti in t[1:]:
-        idx = int(np.argmin(np.abs(ts64.astype(np.float32) - np.float32(ti))))
-        sg = float(sigmas32[idx])
-        an_alpha.append(float(np.float32(1.0) - np.float32(sg)))
-        an_sigma.append(sg)
+        idx = int(np.nonzero(ts32 == np.float32(ti))[0][0])
+        sg = sigmas32[idx]
+        an_alpha.append(float(np.float32(1.0) - sg))
+        an_sigma.append(float(sg))
     return t, sig_x0, an_alpha, an_sigma
+
+
+def scheduler_tables(n_train: int = 1000, shift: float = 3.0):
+    """The scheduler's stored tables (fp32): sigmas [n_train + 1] ending in 0, timesteps
+    [n_train] = 1000 sigma."""
+    s = np.linspace(1.0, 1.0 / n_train, n_train)
+    sig = shift * s / (1 + (shift - 1) * s)
+    sigmas32 = np.concatenate([sig, [0.0]]).astype(np.float32)
+    ts32 = (sigmas32[:-1].astype(np.float64) * 1000.0).astype(np.float32)
+    return sigmas32, ts32
 
 
 @dataclass(frozen=True)

@@ -38,8 +38,12 @@ from oracle.mg2_oracle import apply_rope, attention, bf16, gelu_tanh, layer_norm
 
 
 class LingbotOracle:
-    def __init__(self, cfg, sd: Dict[str, torch.Tensor]):
+    """``round_bf16=False`` keeps every tensor fp32 (the form the golden run of the reference's
+    own code takes, with its bf16 buffers switched to fp32)."""
+
+    def __init__(self, cfg, sd: Dict[str, torch.Tensor], round_bf16: bool = True):
         self.cfg = cfg
+        self.rb = bf16 if round_bf16 else (lambda x: x)
         self.w = {k: v.float() for k, v in sd.items()}
         self.freqs = rope_freqs(cfg.head_dim)
         t, self.sig_x0, self.an_alpha, self.an_sigma = cfg.schedule()
@@ -73,7 +77,7 @@ class LingbotOracle:
             p = f"blocks.{i}.cross_attn."
             k = rms_norm(self.lin(emb, p + "k"), self.w[p + "norm_k.weight"], c.eps)
             v = self.lin(emb, p + "v")
-            kv.append((bf16(k).view(c.text_len, c.heads, c.head_dim), bf16(v).view(c.text_len, c.heads, c.head_dim)))
+            kv.append((self.rb(k).view(c.text_len, c.heads, c.head_dim), self.rb(v).view(c.text_len, c.heads, c.head_dim)))
         self.xkv = kv
 
     # ------------------------------------------------------------------ chunk inputs
@@ -105,7 +109,7 @@ class LingbotOracle:
             h = self.lin(torch.nn.functional.silu(self.lin(emb, p + "cam_injector_layer1")),
                          p + "cam_injector_layer2") + emb
             # the eager module adds 1 to the bf16 scale tensor (static.py:207): bf16(1 + bf16(scale))
-            out.append((bf16(1.0 + bf16(self.lin(h, p + "cam_scale_layer"))), bf16(self.lin(h, p + "cam_shift_layer"))))
+            out.append((self.rb(1.0 + self.rb(self.lin(h, p + "cam_scale_layer"))), self.rb(self.lin(h, p + "cam_shift_layer"))))
         return out
 
     # ------------------------------------------------------------------ network
@@ -114,7 +118,7 @@ class LingbotOracle:
         L, D, H, Dh, Ft = c.tokens, c.dim, c.heads, c.head_dim, c.frame_tokens
         t = self.timesteps[step] if step < len(self.timesteps) else 0.0
         e, e0 = self.time_embed(t)
-        xs = self.lin(self.patches(torch.cat([bf16(x), bf16(y)], 0)), "patch_embedding")
+        xs = self.lin(self.patches(torch.cat([self.rb(x), self.rb(y)], 0)), "patch_embedding")
         for i in range(c.layers):
             p = f"blocks.{i}."
             ee = self.w[p + "modulation"][0] + e0
@@ -123,10 +127,10 @@ class LingbotOracle:
             q = rms_norm(self.lin(yin, sa + "q"), self.w[sa + "norm_q.weight"], c.eps).view(L, H, Dh)
             k = rms_norm(self.lin(yin, sa + "k"), self.w[sa + "norm_k.weight"], c.eps).view(L, H, Dh)
             v = self.lin(yin, sa + "v").view(L, H, Dh)
-            rq, rk = apply_rope(bf16(q), fi), apply_rope(bf16(k), fi)
+            rq, rk = apply_rope(self.rb(q), fi), apply_rope(self.rb(k), fi)
             K, V = st["K"][i], st["V"][i]
-            K[woff * Ft:woff * Ft + L] = bf16(rk)
-            V[woff * Ft:woff * Ft + L] = bf16(v)
+            K[woff * Ft:woff * Ft + L] = self.rb(rk)
+            V[woff * Ft:woff * Ft + L] = self.rb(v)
             a = attention(rq, K[:klen * Ft], V[:klen * Ft]).reshape(L, D)
             xs = xs + self.lin(a, sa + "o") * ee[2]
             cam1, camb = cam[i]
