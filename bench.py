@@ -27,7 +27,7 @@ weights and inputs.  Metric: frames per second (12 pixel frames per chunk), whol
   from one image, prefix-cache branching, cross-GPU checkpoint restores over NVLink) and
   ``tp_parity`` (a tensor-parallel test model over the N ranks: ranks bit-identical, latents
   against the CPU oracle); ``taehv`` (every N: the TAEHV decoder on one chunk's latent, ms per
-  chunk, TFLOP/s, and the served frame rate of DiT chunk + decoder); ``lingbot`` (every N: the
+  chunk, TFLOP/s, and the served frame rate of DiT chunk + decoder); ``lingbot`` (N = 1: the
   LingBot-World-v2 runtime's steady chunk at its own shape).
 
 Multi-GPU (torchrun): every rank runs its own session; there is no collective on the data path
@@ -373,7 +373,7 @@ def run_ours(args):
         variants["tp_parity"] = guarded(lambda: tp_parity_variant(rank, world, local, ctl), world, ctl)
     if not args.no_taehv and agree(time.time() - t_start < args.variant_budget, world, ctl):
         variants["taehv"] = guarded(lambda: taehv_variant(ms, rank, world, ctl), world, ctl)
-    if not args.no_lingbot and agree(time.time() - t_start < args.variant_budget, world, ctl):
+    if world == 1 and not args.no_lingbot and time.time() - t_start < args.variant_budget:
         variants["lingbot"] = guarded(lambda: lingbot_variant(rank, world, ctl), world, ctl)
     line = None
     if rank == 0:
