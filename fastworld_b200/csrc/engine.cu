@@ -469,6 +469,7 @@ static int make_lin(fw_handle* h, GemmOp& op, const std::string& wname, const vo
                     int ldb, int bn, const GemmEpi& epi) {
   if (!h->fp8 || !ptr_of(h, wname + ".q8")) return make_gemm(op, A, M, K, lda, W(h, wname + ".w"), N, ldb, bn, epi,
                                                             h->status);
+  if (bn == 224) bn = 256;   // the e4m3 GEMM has no 224-wide tile
   op.bn = bn;
   FW_TRY(make_tmap_2d(&op.a, h->a8, 1, M, K, K, 128, 128, true));
   FW_TRY(make_tmap_2d(&op.b, P<uint8_t>(h, wname + ".q8"), 1, N, K, K, bn, 128, true));
@@ -620,7 +621,10 @@ static int finalize(fw_handle* h) {
     auto row_par = [&](const char* name, const float* gate, __nv_bfloat16* mirror) {
       return tp ? epi_bf16(h->part, D, nullptr) : epi_resid(h->xs, D, W(h, p + name + ".b"), gate, mirror);
     };
-    FW_TRY(make_lin(h, ly.o, p + "sa.o", h->ao, Dl, L, Dl, D, Dl, 256, row_par("sa.o", ee + 2 * D, nullptr)));
+    // the gated-residual linears take 224-wide tiles where that fills the SMs better (bf16 only;
+    // the tensor-parallel partial-sum epilogue and the e4m3 linears keep 256)
+    const int bnr = tp ? 256 : gemm_resid_bn(L, D);
+    FW_TRY(make_lin(h, ly.o, p + "sa.o", h->ao, Dl, L, Dl, D, Dl, bnr, row_par("sa.o", ee + 2 * D, nullptr)));
     FW_TRY(make_lin(h, ly.caq, p + "ca.q", h->y, D, L, D, Dl, D, bnl, epi_bf16(h->q, Dl, W(h, p + "ca.q.b"))));
     {
       __nv_bfloat16* ck = h->ckv + (size_t)i * 2 * Ctx * Dl;
@@ -629,11 +633,11 @@ static int finalize(fw_handle* h) {
       e.seg_w = Dl;
       FW_TRY(make_gemm(ly.cakv, h->ctx, Ctx, D, D, W(h, p + "ca.kv.w"), 2 * Dl, D, bnl, e, st));
     }
-    FW_TRY(make_lin(h, ly.cao, p + "ca.o", h->ao, Dl, L, Dl, D, Dl, 256,
+    FW_TRY(make_lin(h, ly.cao, p + "ca.o", h->ao, Dl, L, Dl, D, Dl, bnr,
                     row_par("ca.o", nullptr, ly.act >= 0 ? h->xbf : nullptr)));
     FW_TRY(make_lin(h, ly.ff0, p + "ffn.0", h->y, D, L, D, h->FFl, D, 256,
                     epi_bf16(h->hb, h->FFl, W(h, p + "ffn.0.b"), EPI_GELU_BF16)));
-    FW_TRY(make_lin(h, ly.ff2, p + "ffn.2", h->hb, h->FFl, L, h->FFl, D, h->FFl, 256,
+    FW_TRY(make_lin(h, ly.ff2, p + "ffn.2", h->hb, h->FFl, L, h->FFl, D, h->FFl, bnr,
                     row_par("ffn.2", ee + 5 * D, nullptr)));
     const void* hk = ptr_of(h, "hk." + std::to_string(i));
     const void* hv = ptr_of(h, "hv." + std::to_string(i));

@@ -119,6 +119,10 @@ int gemm_bf16_launch(const CUtensorMap& tmA, const CUtensorMap& tmB, int bn, con
 // a.epi.tma_store; leaves the st.global path (returns 0, tma_store false) for grouped launches.
 int make_out_tmaps(GemmArgs& a, CUtensorMap (&o)[3]);
 int gemm_check(const GemmArgs& a, int bn);
+// Tile width for a bf16 GEMM with a 32-column epilogue (residual, fp32 output): 224 where it
+// needs no more waves of the GPU's SMs than 256 and so gives each SM less work, else 256
+// (64 / 128 for narrow outputs).
+int gemm_resid_bn(int M, int N);
 // CTA-pair variant (gemm2.cu): 256 x 256 tiles; tmA box [128 rows, 64 cols] as above, tmB box
 // [128 rows, 64 cols] (half a tile of output columns per CTA).
 int gemm_pair_launch(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmArgs& a, cudaStream_t s,

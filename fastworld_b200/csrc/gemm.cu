@@ -22,14 +22,23 @@
 
 namespace fw {
 
+// BN = 224 (7 chunks of 32 columns) exists for the N = 1536 residual linears of 2640-row chunks:
+// 21 x 7 = 147 tiles fill one wave of 148 SMs, where 256-wide tiles leave 22 SMs idle (126
+// tiles).  Measured on B200 it gains only 1-2 % (2640 x 1536 x 1536: 15.35 -> 15.1 us; K = 8960:
+// 62.1 -> 61.4 us): a tile's time barely follows its width, so the one-CTA main loop is not
+// bound by the MMA's N (the extra SMs also re-read A: 7 column tiles instead of 6).  Its two
+// accumulators sit 256 columns apart.
 template <int BN>
 struct GemmCfg {
   static constexpr int BM = 128, BK = 64;
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE = A_BYTES + B_BYTES;
-  static constexpr int STAGES = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
-  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int STAGES = BN > 128 ? 4 : (BN == 128 ? 6 : 8);
+  static constexpr int ACC = BN == 224 ? 256 : BN;   // TMEM column stride of the two accumulators
+  static constexpr int TMEM_COLS = 2 * ACC;
+  // epilogue: 32-column chunks per tile, and the first warp of a lane quarter takes the first H0
+  static constexpr int NCT = BN / 32, H0 = (NCT + 1) / 2;
   // staging for EPI_RESID_TMA: one [32 rows x 32 fp32] 128-byte-swizzled box per epilogue warp,
   // 1024-aligned after the barrier block
   static constexpr int EPI_OFF = STAGES * STAGE + 1024;
@@ -160,7 +169,7 @@ __global__ void __launch_bounds__(320, 1)
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
         if (!mbar_wait(tempty + acc, acc_phase ^ 1u, abort_flag, args.status, DEV_TIMEOUT_MMA)) break;
         tc_fence_after();
-        const uint32_t d = tmem_base + (uint32_t)(acc * BN);
+        const uint32_t d = tmem_base + (uint32_t)(acc * C::ACC);
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(full + stage, phase, abort_flag, args.status, DEV_TIMEOUT_MMA)) {
             ok = false;
@@ -194,26 +203,29 @@ __global__ void __launch_bounds__(320, 1)
     }
   } else {
     // 8 epilogue warps: warp w reads TMEM lane quarter (w % 4) and column half (w - 2) / 4 of
-    // the tile.  All of a thread's accumulator columns are loaded at once, the TMEM buffer is
-    // released, and the bias / activation / residual math and the stores run from registers.
-    constexpr int NC = BN / 64;                   // 32-column chunks per thread
-    static_assert(8 * NC * C::EPI_BOX <= C::STAGES * C::STAGE, "last-tile staging must fit in the pipeline stages");
+    // the tile (chunks [0, H0) or [H0, NCT) of 32 columns; the halves are equal except for
+    // BN = 224, 4 + 3 chunks).  All of a thread's accumulator columns are loaded at once, the
+    // TMEM buffer is released, and the bias / activation / residual math and the stores run from
+    // registers.
+    constexpr int NC = BN / 64;                   // 64-column boxes per thread are NC / 2
+    static_assert(8 * C::H0 * C::EPI_BOX <= C::STAGES * C::STAGE, "last-tile staging must fit in the pipeline stages");
     const int q = warp & 3, h = (warp - 2) >> 2;
+    const int c_lo = h ? C::H0 : 0, n_ch = h ? C::NCT - C::H0 : C::H0;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
       const int g = t / tpg, mb = (t - g * tpg) % num_m, nb = (t - g * tpg) / num_m;
       const int row = mb * 128 + q * 32 + lane;
-      const int colh = nb * BN + h * (BN / 2);
+      const int colh = nb * BN + c_lo * 32;
       if (EK == EK_RF32 && row < M && colh < N) {   // warm L2 with this thread's residual row part
         const char* p = reinterpret_cast<const char*>(args.epi.resid + (size_t)row * args.epi.ld_resid + colh);
 #pragma unroll
-        for (int b = 0; b < BN * 2; b += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(p + b));
+        for (int b = 0; b < n_ch * 128; b += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(p + b));
       }
       const bool ok = mbar_wait(tfull + acc, acc_phase, abort_flag, args.status, DEV_TIMEOUT_EPILOGUE);
       if (!__all_sync(0xffffffffu, ok)) break;   // keep the warp converged for tcgen05.ld
       tc_fence_after();
-      const uint32_t tb = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + h * (BN / 2));
+      const uint32_t tb = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * C::ACC + c_lo * 32);
       // Accumulator chunks are read from TMEM as each is needed (tcgen05.ld is warp-collective:
       // every lane executes it) and the buffer is released after the last one: the next tile's
       // main loop outlasts this epilogue, so holding TMEM costs nothing and frees the registers.
@@ -250,7 +262,7 @@ __global__ void __launch_bounds__(320, 1)
         // loop and reuse the warp's one box.
         const bool last = EK == EK_RTMA && t + (int)gridDim.x >= num_tiles;
 #pragma unroll 1
-        for (int c = 0; c < NC; ++c) {
+        for (int c = 0; c < n_ch; ++c) {
           uint32_t r[32];
           tmem_ld32(tb + (uint32_t)(c * 32), r);
           tmem_ld_wait();
@@ -258,7 +270,7 @@ __global__ void __launch_bounds__(320, 1)
           if (col0 >= N) continue;
           if constexpr (EK == EK_RTMA)
             epilogue_chunk_tma(args.epi, &tmC, rowc, row0, col0, r, sa, args.sw,
-                               last ? smem + ((warp - 2) * NC + c) * C::EPI_BOX : box, lane, !last);
+                               last ? smem + ((warp - 2) * C::H0 + c) * C::EPI_BOX : box, lane, !last);
           else if constexpr (EK == EK_RF32)
             epilogue_resid_box(args.epi, rowc, row0, col0, M, r, sa, args.sw, box, lane);
           else if (row < M)
@@ -289,7 +301,10 @@ int gemm_check(const GemmArgs& a, int bn) {
       return FW_EINVAL;
     if (e.mode != EPI_BF16 && e.mode != EPI_GELU_BF16 && e.mode != EPI_GELU_ERF_BF16) return FW_EINVAL;
   }
-  if (bn != 64 && bn != 128 && bn != 256) return FW_EINVAL;
+  if (bn != 64 && bn != 128 && bn != 224 && bn != 256) return FW_EINVAL;
+  if (bn == 224 && (a.sa || a.groups != 1 ||
+                    (e.mode != EPI_RESID_TMA && e.mode != EPI_RESID_F32 && e.mode != EPI_F32)))
+    return FW_EINVAL;
   if (a.N % 32 || a.K % (a.sa ? 16 : 8)) return FW_ESHAPE;
   if (a.sa && (!a.sw || (reinterpret_cast<uintptr_t>(a.sw) & 15u))) return FW_EALIGN;
   auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
@@ -402,6 +417,15 @@ int make_out_tmaps(GemmArgs& a, CUtensorMap (&o)[3]) {
   return 0;
 }
 
+int gemm_resid_bn(int M, int N) {
+  if (N < 256) return N >= 128 ? 128 : 64;
+  // waves x tile width: the time of the busiest SM, up to the per-tile constant
+  const int sms = num_sms(), mt = (M + 127) / 128;
+  const long c256 = (long)((mt * ((N + 255) / 256) + sms - 1) / sms) * 256;
+  const long c224 = (long)((mt * ((N + 223) / 224) + sms - 1) / sms) * 224;
+  return c224 < c256 ? 224 : 256;
+}
+
 int gemm_bf16_launch(const CUtensorMap& tmA, const CUtensorMap& tmB, int bn, const GemmArgs& a, cudaStream_t s,
                      int ctas, const CUtensorMap* tmC, const CUtensorMap* tmO) {
   int rc = gemm_check(a, bn);
@@ -418,6 +442,13 @@ int gemm_bf16_launch(const CUtensorMap& tmA, const CUtensorMap& tmB, int bn, con
   switch (bn) {
     case 256:
       return a.sa ? launch_kind<256, true>(tmA, tmB, mc, o, b, s, grid) : launch_kind<256, false>(tmA, tmB, mc, o, b, s, grid);
+    case 224:   // bf16 operands, 32-column epilogue kinds (gemm_check)
+      switch (epi_kind(a.epi, 224)) {
+        case EK_RTMA: return launch_bn<224, false, EK_RTMA>(tmA, tmB, mc, o, b, s, grid);
+        case EK_RF32: return launch_bn<224, false, EK_RF32>(tmA, tmB, mc, o, b, s, grid);
+        case EK_CHUNK: return launch_bn<224, false, EK_CHUNK>(tmA, tmB, mc, o, b, s, grid);
+        default: return FW_EINVAL;
+      }
     case 128:
       return a.sa ? launch_kind<128, true>(tmA, tmB, mc, o, b, s, grid) : launch_kind<128, false>(tmA, tmB, mc, o, b, s, grid);
     default:

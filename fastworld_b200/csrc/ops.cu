@@ -90,7 +90,8 @@ int fw_gemm_bf16(const void* A, const void* B, const void* bias, void* out, int 
   if (epilogue != EPI_BF16 && epilogue != EPI_GELU_BF16 && epilogue != EPI_F32 && epilogue != EPI_GELU_ERF_BF16)
     return FW_EINVAL;
   const int bn = tile_n > 0 ? tile_n : (N >= 256 ? 256 : (N >= 128 ? 128 : 64));
-  if (bn != 64 && bn != 128 && bn != 256 && bn != 512) return FW_EINVAL;
+  if (bn != 64 && bn != 128 && bn != 224 && bn != 256 && bn != 512) return FW_EINVAL;
+  if (bn == 224 && epilogue != EPI_F32) return FW_EINVAL;   // 224-wide tiles: 32-column epilogues only
   CUtensorMap ta, tb;
   int rc = make_tmap_2d(&ta, A, 2, M, K, K, 128, 64, true);
   if (!rc) rc = make_tmap_2d(&tb, B, 2, N, K, K, bn == 512 ? 128 : bn, 64, true);
@@ -184,8 +185,8 @@ int fw_quant_e4m3(const void* x, int M, int K, void* q, float* scale, void* stre
 int fw_gemm_bf16_resid(const void* A, const void* B, const void* bias, float* resid, const float* gate,
                        int rows_per_frame, int M, int N, int K, void* stream) {
   using namespace fw;
-  if (!A || !B || !resid || rows_per_frame <= 0) return FW_EINVAL;
-  const int bn = N >= 256 ? 256 : (N >= 128 ? 128 : 64);
+  if (!A || !B || !resid || rows_per_frame <= 0 || M <= 0 || N <= 0) return FW_EINVAL;
+  const int bn = gemm_resid_bn(M, N);
   CUtensorMap ta, tb;
   int rc = make_tmap_2d(&ta, A, 2, M, K, K, 128, 64, true);
   if (!rc) rc = make_tmap_2d(&tb, B, 2, N, K, K, bn, 64, true);

@@ -1,6 +1,6 @@
 """tcgen05 GEMM parity against an fp32 PyTorch reference of the same op (bf16 inputs).
 
-Covers the tile widths (64/128/256 and the 256 x 256 CTA-pair tile, tile_n 512), M/N/K tails (TMA zero fill + masked epilogue), every
+Covers the tile widths (64/128/224/256 and the 256 x 256 CTA-pair tile, tile_n 512), M/N/K tails (TMA zero fill + masked epilogue), every
 epilogue (bias, GELU-tanh, GELU-erf, fp32 store, gated fp32 residual) and the MG2 shapes.
 Tolerance: rel-L2 <= 6e-3 and max-abs <= 3e-2 * max|ref| (bf16 output rounding is 2^-9).
 """
@@ -56,16 +56,34 @@ def test_gemm_epilogues(epi):
     assert _rel(out, ref) < (1e-5 if epi == "f32" else 6e-3)
 
 
-def test_gemm_residual_gate():
+@pytest.mark.parametrize("M,N,K,rpf", [
+    (2640, 1536, 1536, 880),   # MG2 o-projection: 224-wide tiles (21 x 7 = 147 on 148 SMs)
+    (2640, 1536, 8960, 880),   # MG2 ffn.2
+    (300, 480, 200, 100),      # 224-wide, last column tile 32 of 224 valid, M and K tails
+    (6032, 1536, 256, 1508),   # LingBot rows: 256-wide tiles (two full waves)
+])
+def test_gemm_residual_gate(M, N, K, rpf):
     from fastworld_b200 import ops
-    M, N, K, rpf = 2640, 1536, 1536, 880
     a, b, bias = _data(M, N, K, seed=2)
     g = torch.Generator(device="cuda").manual_seed(3)
     resid = torch.randn(M, N, device="cuda", generator=g)
-    gate = torch.randn(3, N, device="cuda", generator=g)
-    ref = resid + gate.repeat_interleave(rpf, 0) * (a.float() @ b.float().t() + bias.float())
+    gate = torch.randn((M + rpf - 1) // rpf, N, device="cuda", generator=g)
+    ref = resid + gate.repeat_interleave(rpf, 0)[:M] * (a.float() @ b.float().t() + bias.float())
     ops.gemm_resid_(resid, a, b, bias, gate, rpf)
     assert _rel(resid, ref) < 1e-5
+
+
+def test_gemm_tile_224_f32_and_limits():
+    """The 224-wide tile with the fp32-output epilogue agrees with the 256-wide one (same K order
+    per element); bf16-output epilogues are refused at that width."""
+    from fastworld_b200 import ops
+    a, b, bias = _data(2640, 1536, 1536, seed=7)
+    x = ops.gemm(a, b, bias, "f32", 224)
+    y = ops.gemm(a, b, bias, "f32", 256)
+    torch.cuda.synchronize()
+    assert _rel(x, y) < 1e-6
+    with pytest.raises(RuntimeError):
+        ops.gemm(a, b, bias, "none", 224)
 
 
 def test_gemm_deterministic():
