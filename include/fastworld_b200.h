@@ -297,8 +297,8 @@ int fw_selftest_wait(int which, unsigned long long limit_ns, void* scratch, size
 /* ---- individual kernels (used by the engine; exported for tests and reuse) ---- */
 /* C[M,N] = A[M,K] B[N,K]^T (+ bias[N]) with A, B, C bf16 row-major, fp32 accumulate.
  * epilogue: 0 = store bf16, 1 = GELU(tanh) then bf16, 3 = store fp32 (out is float*).
- * tile_n: 64 / 128 / 256 = one CTA per 128 x tile_n tile; 512 = a CTA pair per 256 x 256
- * tile (tcgen05 cta_group::2); 0 = default. */
+ * tile_n: 64 / 128 / 256 = one CTA per 128 x tile_n tile; 224 = the same with 224-wide tiles
+ * (fp32 output only); 512 = a CTA pair per 256 x 256 tile (tcgen05 cta_group::2); 0 = default. */
 int fw_gemm_bf16(const void* A, const void* B, const void* bias, void* out, int M, int N, int K, int epilogue,
                  int tile_n, void* stream);
 /* e4m3 operands (A8 [M,K], B8 [N,K] bytes, K % 16 == 0): C = (A8 B8^T) * sa[row] * sw[col] (+ bias),
