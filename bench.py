@@ -645,6 +645,31 @@ def attn(reps: int) -> None:
           f"({flx / msx / 1e9:.0f} TFLOP/s)")
 
 
+def gemm_vs_cublas(reps: int) -> None:
+    """The engine's bf16 GEMM (plain bf16 epilogue) against cuBLAS (torch.matmul) on the same
+    operands: the MG2, LingBot and 14B linear shapes and 8192^3, both timed through recorded
+    graphs of back-to-back launches.  A comparison only: no product path calls cuBLAS."""
+    from fastworld_b200 import ops
+    g = torch.Generator(device="cuda").manual_seed(0)
+    shapes = [("mg2 qkv", 2640, 4608, 1536), ("mg2 o-proj", 2640, 1536, 1536), ("mg2 ffn.0", 2640, 8960, 1536),
+              ("mg2 ffn.2", 2640, 1536, 8960), ("lingbot qkv", 6032, 4608, 1536),
+              ("lingbot ffn.0", 6032, 8960, 1536), ("14b qkv", 4680, 15360, 5120), ("14b ffn.0", 4680, 13824, 5120),
+              ("14b ffn.2", 4680, 5120, 13824), ("8192^3", 8192, 8192, 8192)]
+    for name, M, N, K in shapes:
+        a = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
+        b = (torch.randn(N, K, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+        bt = b.t()
+        for _ in range(max(reps, 3)):
+            ops.gemm(a, b)
+            torch.matmul(a, bt)
+        torch.cuda.synchronize()
+        ours = _graph_ms([lambda: ops.gemm(a, b)] * 4)
+        lib = _graph_ms([lambda: torch.matmul(a, bt)] * 4)
+        fl = 2.0 * M * N * K
+        print(f"{name:14s} {M}x{N}x{K}: engine {ours * 1e3:8.1f} us {fl / ours / 1e9:6.0f} TFLOP/s | cuBLAS "
+              f"{lib * 1e3:8.1f} us {fl / lib / 1e9:6.0f} TFLOP/s | engine / cuBLAS speed {lib / ours:.3f}")
+
+
 def fp8_peak(reps: int) -> None:
     from fastworld_b200 import ops
     n = 8192
@@ -836,7 +861,7 @@ KERNELS = {"chunk": lambda a: chunk(a.chunks, a.config), "gemm": lambda a: gemm(
            "lingbot": lambda a: lingbot(a.reps), "lingbot_chunk": lambda a: lingbot_chunk(a.reps),
            "gemm_resid": lambda a: gemm_resid(a.reps), "attn": lambda a: attn(a.reps), "ln": lambda a: ln(a.reps),
            "ln14": lambda a: ln14(a.reps), "rms": lambda a: rms(a.reps), "copy": lambda a: copy(a.reps),
-           "fp8_peak": lambda a: fp8_peak(a.reps)}
+           "fp8_peak": lambda a: fp8_peak(a.reps), "gemm_vs_cublas": lambda a: gemm_vs_cublas(a.reps)}
 
 
 def main():
