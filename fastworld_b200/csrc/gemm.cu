@@ -12,8 +12,8 @@
 //               then fused bias / GELU / scales in registers; bf16 outputs go through a
 //               per-warp shared-memory box so that each store instruction writes whole
 //               128-byte rows, gated fp32 residual updates are TMA reduce-adds of such boxes
-// The TMEM accumulator is double-buffered (2 x BN columns) so the epilogue of tile i overlaps
-// the main loop of tile i + 1.  Tile order is M-fastest so consecutive CTAs share a weight
+// The TMEM accumulator is double-buffered (two BN-column buffers; 256 columns apart for BN = 224)
+// so the epilogue of tile i overlaps the main loop of tile i + 1.  BN is 64, 128, 224 or 256.  Tile order is M-fastest so consecutive CTAs share a weight
 // tile in L2.  M, N and K tails are zero-filled by TMA and masked in the epilogue.
 #include "../../include/fastworld_b200.h"
 #include "fw_internal.h"
