@@ -626,8 +626,8 @@ def gemm_resid(reps: int) -> None:
 
 def attn(reps: int) -> None:
     """Steady self-attention (12 heads, 2640 queries over 2640 history + 2640 current keys) and
-    cross-attention (2640 queries over 257 context keys), MG2 shape; timed through recorded
-    graphs of back-to-back launches."""
+    cross-attention (2640 queries over 257 context keys), MG2 shape, and the LingBot window
+    (6032 queries over 27144 keys); timed through recorded graphs of back-to-back launches."""
     from fastworld_b200 import ops
     g = torch.Generator(device="cuda").manual_seed(0)
     r = lambda n: torch.randn(n, 12, 128, device="cuda", generator=g).to(torch.bfloat16)  # noqa: E731
@@ -643,6 +643,15 @@ def attn(reps: int) -> None:
     fl, flx = 4.0 * 2640 * 5280 * 128 * 12, 4.0 * 2640 * 257 * 128 * 12
     print(f"attention self {ms * 1e3:.1f} us ({fl / ms / 1e9:.0f} TFLOP/s), cross {msx * 1e3:.1f} us "
           f"({flx / msx / 1e9:.0f} TFLOP/s)")
+    # the LingBot window: 6032 queries over 27144 keys (one segment), 12 heads
+    ql, kl, vl = r(6032), r(27144), r(27144)
+    meta_l = torch.tensor([27144, 0], dtype=torch.int32, device="cuda")
+    for _ in range(reps):
+        ops.attention(ql, kl, vl, kl, vl, meta_l)
+    torch.cuda.synchronize()
+    msl = _graph_ms([lambda: ops.attention(ql, kl, vl, kl, vl, meta_l)] * 4)
+    fll = 4.0 * 6032 * 27144 * 128 * 12
+    print(f"attention LingBot window {msl * 1e3:.1f} us ({fll / msl / 1e9:.0f} TFLOP/s)")
 
 
 def gemm_vs_cublas(reps: int) -> None:
